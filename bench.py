@@ -1,0 +1,400 @@
+#!/usr/bin/env python3
+"""Benchmark of the out-of-core FP32 SGEMM path (one JSON line on rank 0).
+
+Workload (the metric's single-GPU configuration): column-major
+SGEMM M=8192 N=6144 K=4096, op(A)=T, op(B)=N, alpha=0.5, beta=1.5, A/B/C uniform[-1,1)
+from seeds 10/11/12 (synthetic; no dataset).  N GPUs run one such problem each (weak
+scaling: the C rows of the N-GPU job are split by rank, every rank owns an 8192-row
+block and its A rows; B is per rank in this version -- replicas, no collective).
+
+  value   kernel-only TFLOP/s: the sm_100a SGEMM kernel on HBM-resident operands,
+          K launches timed with CUDA events on the launching stream, max over ranks.
+          The 416 MiB working set is larger than the 126 MB L2, so no flush is needed.
+  e2e     the same metric through the reference-facing C ABI (xvram_cuda_compat_get_api):
+          per step memcpy(H2D) of A, B, C from pinned host buffers, blas_sgemm, and
+          memcpy(D2H) of C -- exactly what a reference caller does.
+  roofline  achieved kernel TFLOP/s against the FP32 (FFMA) pipe peak measured in the
+          same run by xvram_b200_ffma_probe; `traffic` comes from the committed ncu
+          summary profiles/sgemm_ffma_c2_traffic.json when present.
+  host_link  pinned H2D/D2H GB/s measured here; the e2e roofline is
+          max(FLOP / P_fp32, operand bytes / BW_host) per BASELINE.md.
+  cpu_baseline  the reference's CPU FP64 GEMM (reference_result, compiled from the
+          reference sources into oracle/_ref) -- or the oracle port when that build is
+          absent -- timed on a bounded sample on all host cores.
+
+`--impl reference` times only that CPU implementation (the reference has no runnable
+GPU path here: it needs CUDA 13, nvCOMP and cuBLAS 13 redistributables).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M, N, K = 8192, 6144, 4096
+OP_A, OP_B = 1, 0
+ALPHA, BETA = 0.5, 1.5
+FLOP = 2.0 * M * N * K
+WORKLOAD = "C2: column-major SGEMM M=8192 N=6144 K=4096 op(A)=T op(B)=N alpha=0.5 beta=1.5"
+METRIC = "out-of-core SGEMM TFLOP/s + host-link GB/s vs roofline at 1/2/4/8 B200"
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_reference_rate(threads: int, target_s: float):
+    """Times the reference's own CPU FP64 GEMM (compat_bench reference_result, full k loop)
+    on a bounded sample of C2's outputs; falls back to the oracle port over arrays."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle_lib import load_oracle, load_reference
+    ref = load_reference()
+    if ref is not None:
+        def run(count, first=0):
+            t0 = time.perf_counter()
+            ref.xr_cpu_gemm_sample(M, N, K, first, count, ALPHA, BETA, 0, threads)
+            return time.perf_counter() - t0
+        kind = "reference"
+        desc = "reference compat_bench reference_result (FP64, full K) over C2 outputs"
+    else:
+        import numpy as np
+        orc = load_oracle()
+        a = orc.uniform(K * M, 10)
+        b = orc.uniform(K * N, 11)
+        c = orc.uniform(M * N, 12)
+
+        def run(count, first=0):
+            idx = np.arange(first, first + count, dtype=np.int64) % (M * N)
+            t0 = time.perf_counter()
+            orc.gemm_sampled(OP_A, OP_B, K, ALPHA, a, K, b, K, BETA, c, M, idx % M, idx // M,
+                             threads=threads)
+            return time.perf_counter() - t0
+        kind = "port"
+        desc = "oracle FP64 port (xo_gemm_f64_sampled) over C2 outputs"
+    probe = 4096
+    dt = max(run(probe), 1e-4)
+    count = int(min(M * N, max(probe, probe * target_s / dt)))
+    return kind, desc, run, count
+
+
+def cpu_baseline_obj(threads: int, target_s: float = 10.0) -> dict:
+    kind, desc, run, count = cpu_reference_rate(threads, target_s)
+    dt = run(count)
+    flop = 2.0 * K * count
+    return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+            "sample": f"{desc}: {count} of {M * N} outputs ({flop / 1e9:.1f} GFLOP) in {dt:.1f} s"}
+
+
+def run_reference_arm(args) -> None:
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    kind, desc, run, count = cpu_reference_rate(threads, target_s=2.0)
+    for _ in range(args.warmup):
+        run(count)
+    times = [run(count) for _ in range(args.steps)]
+    total = sum(times)
+    value = 2.0 * K * count * args.steps / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_outputs_per_step": count,
+                   "note": "reference CPU FP64 GEMM on host cores (no GPU path builds here)"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                         "sample": f"{desc}: {count} outputs per step"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = max(smax, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        loaded = [x for x in sm if x > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ GPU arm
+def main_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    from xvram_b200 import compat as cp
+    from xvram_b200 import device as xd
+    from xvram_b200._native import lib
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Inputs: rank r owns C rows [8192 r, 8192 (r+1)) of the weak-scaled job; its A rows
+    # and the B panel are generated from the same seeded streams (offset by rank).
+    a_h = torch.empty((M, K), dtype=torch.float32).pin_memory()    # stored K x M (op T)
+    b_h = torch.empty((N, K), dtype=torch.float32).pin_memory()    # stored K x N (op N)
+    c_h = torch.empty((N, M), dtype=torch.float32).pin_memory()    # M x N
+    xd.fill_uniform(a_h, 10, first_index=rank * M * K)
+    xd.fill_uniform(b_h, 11)
+    xd.fill_uniform(c_h, 12, first_index=rank * M * N)
+    c_out = torch.empty_like(c_h).pin_memory()
+
+    stream = torch.cuda.Stream(device=dev)
+    A = a_h.to(dev)
+    B = b_h.to(dev)
+    Cd = c_h.to(dev)
+    torch.cuda.synchronize()
+
+    # FP32 pipe peak on this device, this run (FFMA probe, best of 5).
+    sink = torch.zeros(1, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks, iters = sms * 4, 1500
+    peak = 0.0
+    with torch.cuda.stream(stream):
+        for i in range(6):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            assert xd.ffma_probe(blocks, iters, sink, stream) == 0
+            e1.record(stream)
+            e1.synchronize()
+            if i:
+                peak = max(peak, 2.0 * blocks * 256 * iters * 512 / (e0.elapsed_time(e1) * 1e-3))
+    peak_tflops = peak / 1e12
+
+    # Host link: pinned H2D / D2H GB/s (64 MiB x 8, best).
+    probe_h = torch.empty(16 << 20, dtype=torch.float32).pin_memory()
+    probe_d = torch.empty(16 << 20, dtype=torch.float32, device=dev)
+    h2d = d2h = 0.0
+    with torch.cuda.stream(stream):
+        for _ in range(4):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            probe_d.copy_(probe_h, non_blocking=True)
+            e1.record(stream)
+            probe_h.copy_(probe_d, non_blocking=True)
+            e2.record(stream)
+            e2.synchronize()
+            h2d = max(h2d, probe_h.nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+            d2h = max(d2h, probe_h.nbytes / (e1.elapsed_time(e2) * 1e-3) / 1e9)
+    del probe_h, probe_d
+
+    # ---------------- kernel-only: inputs resident in HBM
+    def launch():
+        st = xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B, K, BETA, Cd, M, stream=stream)
+        assert st == 0, st
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            launch()
+    stream.synchronize()
+    assert xd.kernel_status(stream) == 0
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                launch()
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    assert xd.kernel_status(stream) == 0
+    kernel_ms = start.elapsed_time(stop) / args.steps
+    kernel_ms_max = max_over_ranks(kernel_ms)
+    value = world * FLOP / (kernel_ms_max * 1e-3) / 1e12
+    achieved = FLOP / (kernel_ms * 1e-3) / 1e12
+
+    # ---------------- end to end through the compat C ABI
+    api = cp.CompatApi()
+    cfg = cp.compat_config_init()
+    cfg.session.device_ordinal = local
+    api.check("initialize", api.initialize(cfg))
+    h = api.blas_create()
+    da, db, dc = api.malloc(a_h.nbytes), api.malloc(b_h.nbytes), api.malloc(c_h.nbytes)
+
+    def e2e_step():
+        api.h2d(da, a_h.data_ptr(), a_h.nbytes)
+        api.h2d(db, b_h.data_ptr(), b_h.nbytes)
+        api.h2d(dc, c_h.data_ptr(), c_h.nbytes)
+        api.check("sgemm", api.sgemm(h, OP_A, OP_B, M, N, K, ALPHA, da, K, db, K, BETA, dc, M))
+        api.d2h(c_out.data_ptr(), dc, c_out.nbytes)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    barrier()
+    e2e_s_max = max_over_ranks(e2e_s)
+    tel = api.telemetry()
+    info = cp.runtime_info()
+    launches_e2e = int(info.gemm_in_place)  # one kernel per in-place GEMM
+    for d in (da, db, dc):
+        api.free(d)
+    api.blas_destroy(h)
+    api.shutdown()
+
+    h2d_bytes = a_h.nbytes + b_h.nbytes + c_h.nbytes
+    d2h_bytes = c_out.nbytes
+    bw_host = h2d  # the H2D link is the e2e bottleneck (D2H is the smaller leg)
+    t_roof = max(FLOP / (peak_tflops * 1e12), h2d_bytes / (h2d * 1e9) + d2h_bytes / (d2h * 1e9))
+    t_roof_overlap = max(FLOP / (peak_tflops * 1e12), (h2d_bytes + d2h_bytes) / (bw_host * 1e9))
+
+    traffic = None
+    tfile = ROOT / "profiles" / "sgemm_ffma_c2_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+        except (ValueError, OSError):
+            traffic = None
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.skip_cpu_baseline:
+            cpu = cpu_baseline_obj(os.cpu_count() or 1)
+        line = {
+            "metric": METRIC,
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": kernel_ms_max, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "per_gpu": f"M={M} N={N} K={K}",
+                       "parallelism": f"C rows split over {world} GPU(s), replicas",
+                       "l2": "inputs larger than L2 (416 MiB working set per step)",
+                       "seeds": "A 10, B 11, C 12 (counter-based uniform[-1,1))"},
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak_tflops,
+                         "unit": "TFLOP/s", "frac": achieved / peak_tflops, "traffic": traffic,
+                         "peak_source": "measured FFMA probe (xvram_b200_ffma_probe), this run"},
+            "host_link": {"h2d_gbs": h2d, "d2h_gbs": d2h,
+                          "e2e_link_gbs": (h2d_bytes + d2h_bytes) / e2e_s_max / 1e9,
+                          "e2e_roofline_ms_serial": 1e3 * t_roof,
+                          "e2e_roofline_ms_overlapped": 1e3 * t_roof_overlap,
+                          "e2e_frac_of_roofline": t_roof_overlap / e2e_s_max},
+            "e2e": {"value": world * FLOP / e2e_s_max / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+                    "ms_per_step": 1e3 * e2e_s_max,
+                    "path": "xvram_cuda_compat_get_api: memcpy H2D x3, blas_sgemm, memcpy D2H",
+                    "gemm_in_place": int(info.gemm_in_place),
+                    "gemm_streamed": int(info.gemm_streamed),
+                    "runtime_h2d_bytes": int(tel.runtime.bytes_h2d)},
+            "gpu_launches": args.steps,
+            "gpu_launches_e2e": launches_e2e,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    main_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+/*
+ * xvram_b200.h -- native entry points of the B200 implementation.
+ *
+ * The drop-in boundary is xvram_cuda_compat.h.  The functions here expose the pieces
+ * underneath it to callers that already manage device memory (the tile contraction on
+ * raw device pointers) and to measurement and test harnesses (planner inspection,
+ * validation, synthetic inputs, the FFMA peak probe).  All functions are plain C:
+ * integer sizes, raw pointers, CUDA streams passed as uint64_t (0 = legacy default
+ * stream).  Each notes the reference interface it stands in for, if any.
+ */
+#ifndef XVRAM_B200_H
+#define XVRAM_B200_H
+
+#include "xvram.h"
+
+#if defined(__GNUC__) && defined(XVRAM_BUILDING_CUDA_COMPAT)
+#define XVRAM_B200_API __attribute__((visibility("default")))
+#else
+#define XVRAM_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XVRAM_B200_VERSION_NUMBER 100 /* 0.1.0 */
+
+/* Path selection for xvram_b200_sgemm_device. */
+enum {
+  XVRAM_B200_PATH_AUTO = 0,    /* TMA kernel when aligned, else the generic kernel */
+  XVRAM_B200_PATH_TMA = 1,     /* TMA kernel or INVALID_ARGUMENT */
+  XVRAM_B200_PATH_GENERIC = 2  /* generic kernel (any alignment) */
+};
+
+/*
+ * C = alpha * op(A) * op(B) + beta * C on device-resident column-major FP32 matrices,
+ * enqueued on `stream` and not synchronised.  op 0 = N, 1 = T.  m, n, k >= 0 (k == 0
+ * scales C by beta); beta == 0 does not read C.  Strict FP32: every multiply-add is an
+ * FFMA.  Stands in for the per-tile library call of the reference's executor
+ * (src/gemm/executor.cpp:147-329 -> cublasLtMatmul, src/platform/cublas/cublas_api.cpp:751-918).
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
+    int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, uint64_t stream,
+    uint32_t path);
+
+/* Synchronises `stream`, then returns and clears the device's sticky kernel error word
+ * (nonzero: a pipeline wait inside a kernel ran out of time and the kernel returned
+ * without finishing).  No reference counterpart (the reference has no kernels). */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_kernel_status(uint64_t stream,
+                                                                uint32_t* word);
+
+/* dst[i] = uniform[-1, 1) draw (seed, first_index + i) on `threads` host threads
+ * (0 = all).  Counter-based: any element can be recomputed independently. */
+XVRAM_B200_API void XVRAM_CALL xvram_b200_fill_uniform(float* dst, uint64_t count,
+                                                       uint64_t seed, uint64_t first_index,
+                                                       int32_t threads);
+
+/* Panel plan summary for an out-of-core problem under a device budget.  Stands in for
+ * the reference's gemm::make_plan inspection (src/gemm/planner.cpp:1005-1153). */
+typedef struct xvram_b200_plan_info_v1 {
+  uint32_t struct_size;
+  uint32_t status; /* 0 ok, 1 invalid, 2 budget too small */
+  int64_t block_m, block_n, panel_k;
+  int32_t n_outer; /* 1: n blocks outer loop */
+  int32_t panel_slots;
+  int32_t c_slots;
+  int32_t reserved0;
+  uint64_t slot_bytes, c_slot_bytes;
+  uint64_t steps, panel_loads, panel_hits, panel_evictions;
+  uint64_t h2d_bytes, d2h_bytes;
+  double est_seconds;
+} xvram_b200_plan_info_v1;
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_plan_panels(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, int32_t beta_nonzero,
+    uint64_t budget_bytes, uint64_t quantum_bytes, double flops_per_s, double h2d_bytes_per_s,
+    double d2h_bytes_per_s, int64_t force_mb, int64_t force_nb, int64_t force_kb,
+    xvram_b200_plan_info_v1* out);
+
+/* Writes the plan's step list: for step i, out[5*i .. 5*i+4] = bm, bn, bk, slot_a, slot_b.
+ * `capacity` is the number of steps `out` can hold; returns INVALID_ARGUMENT if smaller. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_plan_steps(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, int32_t beta_nonzero,
+    uint64_t budget_bytes, uint64_t quantum_bytes, int64_t force_mb, int64_t force_nb,
+    int64_t force_kb, int32_t* out, uint64_t capacity);
+
+/* Column-major FP32 GEMM problem validation.  Returns the problem-error enumerator of the
+ * reference's gemm::validate_problem (src/gemm/planner.cpp:785-859) and its operand
+ * letter.  Arrays are indexed A, B, C. */
+XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
+    uint64_t m, uint64_t n, uint64_t k, uint32_t op_a, uint32_t op_b,
+    const uint64_t allocation_ids[3], const uint64_t allocation_bytes[3],
+    const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
+    const uint64_t lds[3], char* operand);
+
+/* Launches `blocks` x 256 threads of dependent FFMA chains (`iterations` x 512 FFMA per
+ * thread) on `stream`; the measured FP32 pipe peak is 2 * blocks * 256 * iterations * 512
+ * FLOP over the launch time.  `sink` (device, >= 1 float) defeats dead-code elimination. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int32_t iterations,
+                                                             float* sink, uint64_t stream);
+
+/* Extra state of the compat adapter's runtime (not in the reference telemetry). */
+typedef struct xvram_b200_runtime_info_v1 {
+  uint32_t struct_size;
+  uint32_t reserved0;
+  uint64_t frame_bytes;
+  uint64_t frame_capacity;
+  uint64_t gemm_in_place;
+  uint64_t gemm_streamed;
+  uint64_t last_block_m, last_block_n, last_panel_k;
+  uint64_t last_steps;
+  uint64_t last_panel_slots;
+  double last_gemm_ms;
+} xvram_b200_runtime_info_v1;
+
+XVRAM_B200_API xvram_status XVRAM_CALL
+xvram_b200_compat_runtime_info(xvram_b200_runtime_info_v1* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XVRAM_B200_H */

@@ -1,0 +1,91 @@
+"""ctypes binding of the native library (xvram_b200/lib/libxvram_cuda_compat.so).
+
+The library is the product: there is no Python or CPU fallback.  Importing this
+module without the built library raises immediately; build it with
+``python -m xvram_b200.build`` (``__graft_entry__.build()`` does the same).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxvram_cuda_compat.so"
+
+u32, u64, i32, i64 = C.c_uint32, C.c_uint64, C.c_int32, C.c_int64
+f32, f64 = C.c_float, C.c_double
+vp = C.c_void_p
+
+
+class PlanInfo(C.Structure):
+    """xvram_b200_plan_info_v1 (include/xvram_b200.h)."""
+
+    _fields_ = [
+        ("struct_size", u32), ("status", u32),
+        ("block_m", i64), ("block_n", i64), ("panel_k", i64),
+        ("n_outer", i32), ("panel_slots", i32), ("c_slots", i32), ("reserved0", i32),
+        ("slot_bytes", u64), ("c_slot_bytes", u64),
+        ("steps", u64), ("panel_loads", u64), ("panel_hits", u64), ("panel_evictions", u64),
+        ("h2d_bytes", u64), ("d2h_bytes", u64),
+        ("est_seconds", f64),
+    ]
+
+
+class RuntimeInfo(C.Structure):
+    """xvram_b200_runtime_info_v1 (include/xvram_b200.h)."""
+
+    _fields_ = [
+        ("struct_size", u32), ("reserved0", u32),
+        ("frame_bytes", u64), ("frame_capacity", u64),
+        ("gemm_in_place", u64), ("gemm_streamed", u64),
+        ("last_block_m", u64), ("last_block_n", u64), ("last_panel_k", u64),
+        ("last_steps", u64), ("last_panel_slots", u64),
+        ("last_gemm_ms", f64),
+    ]
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library with `python -m xvram_b200.build` "
+            "(there is no fallback implementation)")
+    lib = C.CDLL(str(LIB_PATH))
+    lib.xvram_b200_sgemm_device.argtypes = [u32, u32, i64, i64, i64, f32, vp, i64, vp, i64, f32,
+                                            vp, i64, u64, u32]
+    lib.xvram_b200_sgemm_device.restype = u32
+    lib.xvram_b200_kernel_status.argtypes = [u64, C.POINTER(u32)]
+    lib.xvram_b200_kernel_status.restype = u32
+    lib.xvram_b200_fill_uniform.argtypes = [vp, u64, u64, u64, i32]
+    lib.xvram_b200_fill_uniform.restype = None
+    lib.xvram_b200_plan_panels.argtypes = [u32, u32, i64, i64, i64, i32, u64, u64, f64, f64, f64,
+                                           i64, i64, i64, C.POINTER(PlanInfo)]
+    lib.xvram_b200_plan_panels.restype = u32
+    lib.xvram_b200_plan_steps.argtypes = [u32, u32, i64, i64, i64, i32, u64, u64, i64, i64, i64,
+                                          C.POINTER(i32), u64]
+    lib.xvram_b200_plan_steps.restype = u32
+    arr3 = C.POINTER(u64)
+    lib.xvram_b200_validate_gemm.argtypes = [u64, u64, u64, u32, u32, arr3, arr3, arr3, arr3,
+                                             arr3, arr3, C.c_char_p]
+    lib.xvram_b200_validate_gemm.restype = i32
+    lib.xvram_b200_ffma_probe.argtypes = [i32, i32, vp, u64]
+    lib.xvram_b200_ffma_probe.restype = u32
+    lib.xvram_b200_compat_runtime_info.argtypes = [C.POINTER(RuntimeInfo)]
+    lib.xvram_b200_compat_runtime_info.restype = u32
+    lib.xvram_cuda_compat_get_api.argtypes = [u32, u32, vp]
+    lib.xvram_cuda_compat_get_api.restype = u32
+    return lib
+
+
+lib = _load()
+
+# Every symbol include/*.h declares (checked by tests/test_native_load.py).
+EXPORTED = (
+    "xvram_cuda_compat_get_api",
+    "xvram_b200_sgemm_device",
+    "xvram_b200_kernel_status",
+    "xvram_b200_fill_uniform",
+    "xvram_b200_plan_panels",
+    "xvram_b200_plan_steps",
+    "xvram_b200_validate_gemm",
+    "xvram_b200_ffma_probe",
+    "xvram_b200_compat_runtime_info",
+)

@@ -1,0 +1,86 @@
+// device.hpp -- the runtime's only window onto the GPU.
+//
+// The residency runtime, transfer engine and executor talk to the device through this
+// interface, never to CUDA directly.  CudaDevice (cuda_device.cpp) is the product
+// implementation; tests install a host-memory fake through xvram_b200_test_set_device_factory
+// to drive the scheduling, eviction and failure paths without a GPU, the way the
+// reference's fake driver tables do (reference tests/unit/residency_executor_fake_tests.cpp).
+//
+// Addresses are plain 64-bit integers (device virtual addresses for the real device).
+#pragma once
+
+#include "status.hpp"
+
+#include <cstdint>
+#include <memory>
+#include <string>
+
+namespace xvram {
+
+struct DeviceInfo {
+  int ordinal = 0;
+  int device_count = 0;
+  std::string name;
+  uint64_t total_bytes = 0;
+  int sm_count = 0;
+  uint64_t vmm_granularity = 0; // physical allocation granularity for cuMemCreate
+  int driver_version = 0;
+};
+
+using StreamId = uint64_t;
+using EventId = uint64_t;
+
+enum class CopyDir { h2d, d2h, d2d };
+
+class Device {
+public:
+  virtual ~Device() = default;
+
+  virtual Error open(int ordinal, DeviceInfo* info) = 0;
+  virtual Error close() = 0;
+  virtual Error mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes) = 0;
+
+  // Virtual memory management: stable address ranges and physical frames.
+  virtual Error va_reserve(uint64_t bytes, uint64_t* va) = 0;
+  virtual Error va_free(uint64_t va, uint64_t bytes) = 0;
+  virtual Error handle_create(uint64_t bytes, uint64_t* handle) = 0;
+  virtual Error handle_release(uint64_t handle) = 0;
+  // Maps `handle` (exactly `bytes`) at `va` and grants this device read/write access.
+  virtual Error map(uint64_t va, uint64_t bytes, uint64_t handle) = 0;
+  virtual Error unmap(uint64_t va, uint64_t bytes) = 0;
+
+  // Page-locked host memory.
+  virtual Error host_alloc(uint64_t bytes, void** out) = 0;
+  virtual Error host_free(void* p) = 0;
+
+  virtual Error stream_create(StreamId* out) = 0;
+  virtual Error stream_destroy(StreamId s) = 0;
+  virtual Error stream_sync(StreamId s) = 0;
+  virtual Error event_create(EventId* out) = 0;
+  virtual Error event_destroy(EventId e) = 0;
+  virtual Error event_record(EventId e, StreamId s) = 0;
+  virtual Error stream_wait_event(StreamId s, EventId e) = 0;
+  virtual Error event_sync(EventId e) = 0;
+  virtual Error event_elapsed_ms(EventId start, EventId stop, float* ms) = 0;
+
+  // Pitched 2D copy of `height` rows of `width` bytes.
+  virtual Error copy_2d(uint64_t dst, uint64_t dpitch, uint64_t src, uint64_t spitch,
+                        uint64_t width, uint64_t height, CopyDir dir, StreamId s) = 0;
+  virtual Error memset_d32(uint64_t dst, uint32_t value, uint64_t count, StreamId s) = 0;
+
+  // C = alpha * op(A) op(B) + beta * C on device addresses (column-major FP32).
+  virtual Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha,
+                      uint64_t a, int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c,
+                      int64_t ldc, StreamId s) = 0;
+  // Reads and clears the sticky error word of the library's kernels (synchronising s).
+  virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
+};
+
+using DeviceFactory = std::unique_ptr<Device> (*)();
+
+std::unique_ptr<Device> make_cuda_device();
+
+// The factory the adapter uses; tests may replace it before initialize().
+DeviceFactory& device_factory();
+
+} // namespace xvram

@@ -1,0 +1,28 @@
+// kernels.hpp -- host-side launch interface of the library's CUDA kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace xvram {
+
+enum class SgemmPath { automatic = 0, tma = 1, generic = 2 };
+
+// C = alpha * op(A) * op(B) + beta * C on device-resident column-major FP32 data, on
+// `stream`.  op 0 = N, 1 = T.  beta == 0 never reads C.  `automatic` selects the TMA
+// kernel when the operands satisfy its alignment (16-byte bases, ld % 4 == 0).
+cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                       long long lda, const float* b, long long ldb, float beta, float* c,
+                       long long ldc, cudaStream_t stream, SgemmPath path = SgemmPath::automatic);
+
+bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
+                        long long ldb);
+
+// Reads (synchronising `stream`) and clears the device's sticky kernel error word.
+cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream);
+
+unsigned long long kernel_wait_limit_ns();
+
+// Host-side probes used by bench.py for its roofline denominators.
+cudaError_t ffma_peak_probe(int blocks, int iterations, float* sink, cudaStream_t stream);
+
+} // namespace xvram

@@ -1,0 +1,197 @@
+// native_api.cpp -- implementations of include/xvram_b200.h.
+#include "xvram_b200.h"
+
+#include "host_util.hpp"
+#include "kernels.hpp"
+#include "planner.hpp"
+#include "validate.hpp"
+
+#include <cuda_runtime.h>
+
+namespace xvram {
+xvram_status compat_runtime_info(xvram_b200_runtime_info_v1* out);
+}
+
+using namespace xvram;
+
+namespace {
+
+cudaStream_t as_stream(uint64_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+xvram_status from_cuda(cudaError_t e) {
+  switch (e) {
+  case cudaSuccess:
+    return XVRAM_STATUS_SUCCESS;
+  case cudaErrorInvalidValue:
+  case cudaErrorInvalidConfiguration:
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  case cudaErrorMemoryAllocation:
+    return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
+  case cudaErrorNoDevice:
+  case cudaErrorInsufficientDriver:
+    return XVRAM_STATUS_UNAVAILABLE;
+  default:
+    return XVRAM_STATUS_CUDA_ERROR;
+  }
+}
+
+PlanStatus plan_for(uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k,
+                    int32_t beta_nonzero, uint64_t budget, uint64_t quantum, double fps,
+                    double h2d, double d2h, int64_t fm, int64_t fn, int64_t fk, Plan* plan) {
+  PlanProblem p;
+  p.op_a = static_cast<int>(op_a);
+  p.op_b = static_cast<int>(op_b);
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.beta_nonzero = beta_nonzero != 0;
+  PlanLimits lim;
+  lim.budget_bytes = budget;
+  lim.quantum_bytes = quantum;
+  if (fps > 0)
+    lim.flops_per_s = fps;
+  if (h2d > 0)
+    lim.h2d_bytes_per_s = h2d;
+  if (d2h > 0)
+    lim.d2h_bytes_per_s = d2h;
+  lim.force_mb = fm;
+  lim.force_nb = fn;
+  lim.force_kb = fk;
+  return make_panel_plan(p, lim, plan);
+}
+
+} // namespace
+
+extern "C" {
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
+    int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, uint64_t stream,
+    uint32_t path) {
+  if (op_a > 1 || op_b > 1 || m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
+      k > INT32_MAX || path > XVRAM_B200_PATH_GENERIC)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  if (m == 0 || n == 0)
+    return XVRAM_STATUS_SUCCESS;
+  if (!c || ldc < m || (k > 0 && (!a || !b || lda < (op_a == 0 ? m : k) ||
+                                  ldb < (op_b == 0 ? k : n))))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  const SgemmPath p = path == XVRAM_B200_PATH_TMA       ? SgemmPath::tma
+                      : path == XVRAM_B200_PATH_GENERIC ? SgemmPath::generic
+                                                        : SgemmPath::automatic;
+  return from_cuda(sgemm_ffma(static_cast<int>(op_a), static_cast<int>(op_b), static_cast<int>(m),
+                              static_cast<int>(n), static_cast<int>(k), alpha, a, lda, b, ldb,
+                              beta, c, ldc, as_stream(stream), p));
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_kernel_status(uint64_t stream, uint32_t* word) {
+  if (!word)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  unsigned int w = 0;
+  const cudaError_t e = read_and_clear_kernel_error(&w, as_stream(stream));
+  *word = w;
+  return from_cuda(e);
+}
+
+XVRAM_B200_API void XVRAM_CALL xvram_b200_fill_uniform(float* dst, uint64_t count, uint64_t seed,
+                                                       uint64_t first_index, int32_t threads) {
+  if (dst && count)
+    fill_uniform(dst, count, seed, first_index, threads);
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_plan_panels(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, int32_t beta_nonzero,
+    uint64_t budget_bytes, uint64_t quantum_bytes, double flops_per_s, double h2d_bytes_per_s,
+    double d2h_bytes_per_s, int64_t force_mb, int64_t force_nb, int64_t force_kb,
+    xvram_b200_plan_info_v1* out) {
+  if (!out || out->struct_size < sizeof(*out))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  Plan plan;
+  const PlanStatus st = plan_for(op_a, op_b, m, n, k, beta_nonzero, budget_bytes, quantum_bytes,
+                                 flops_per_s, h2d_bytes_per_s, d2h_bytes_per_s, force_mb,
+                                 force_nb, force_kb, &plan);
+  const uint32_t size = out->struct_size;
+  *out = xvram_b200_plan_info_v1{};
+  out->struct_size = size;
+  out->status = static_cast<uint32_t>(st);
+  if (st != PlanStatus::ok)
+    return st == PlanStatus::invalid ? XVRAM_STATUS_INVALID_ARGUMENT : XVRAM_STATUS_BUDGET_PRESSURE;
+  out->block_m = plan.mb;
+  out->block_n = plan.nb;
+  out->panel_k = plan.kb;
+  out->n_outer = plan.n_outer ? 1 : 0;
+  out->panel_slots = plan.panel_slots;
+  out->c_slots = plan.c_slots;
+  out->slot_bytes = plan.slot_bytes;
+  out->c_slot_bytes = plan.c_slot_bytes;
+  out->steps = plan.steps.size();
+  out->panel_loads = plan.panel_loads;
+  out->panel_hits = plan.panel_hits;
+  out->panel_evictions = plan.panel_evictions;
+  out->h2d_bytes = plan.h2d_bytes;
+  out->d2h_bytes = plan.d2h_bytes;
+  out->est_seconds = plan.est_seconds;
+  return XVRAM_STATUS_SUCCESS;
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_plan_steps(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, int32_t beta_nonzero,
+    uint64_t budget_bytes, uint64_t quantum_bytes, int64_t force_mb, int64_t force_nb,
+    int64_t force_kb, int32_t* out, uint64_t capacity) {
+  Plan plan;
+  const PlanStatus st = plan_for(op_a, op_b, m, n, k, beta_nonzero, budget_bytes, quantum_bytes,
+                                 0, 0, 0, force_mb, force_nb, force_kb, &plan);
+  if (st != PlanStatus::ok)
+    return st == PlanStatus::invalid ? XVRAM_STATUS_INVALID_ARGUMENT : XVRAM_STATUS_BUDGET_PRESSURE;
+  if (!out || capacity < plan.steps.size())
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  for (size_t i = 0; i < plan.steps.size(); ++i) {
+    const PlanStep& s = plan.steps[i];
+    out[5 * i + 0] = s.bm;
+    out[5 * i + 1] = s.bn;
+    out[5 * i + 2] = s.bk;
+    out[5 * i + 3] = s.slot_a;
+    out[5 * i + 4] = s.slot_b;
+  }
+  return XVRAM_STATUS_SUCCESS;
+}
+
+XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
+    uint64_t m, uint64_t n, uint64_t k, uint32_t op_a, uint32_t op_b,
+    const uint64_t allocation_ids[3], const uint64_t allocation_bytes[3],
+    const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
+    const uint64_t lds[3], char* operand) {
+  GemmShape s;
+  s.m = m;
+  s.n = n;
+  s.k = k;
+  s.op_a = static_cast<int>(op_a);
+  s.op_b = static_cast<int>(op_b);
+  MatrixRef* mats[3] = {&s.a, &s.b, &s.c};
+  for (int i = 0; i < 3; ++i) {
+    mats[i]->allocation_id = allocation_ids[i];
+    mats[i]->allocation_bytes = allocation_bytes[i];
+    mats[i]->offset_bytes = offsets[i];
+    mats[i]->rows = rows[i];
+    mats[i]->columns = columns[i];
+    mats[i]->ld = lds[i];
+  }
+  const Validation v = validate_gemm(s);
+  if (operand)
+    *operand = v.operand;
+  return static_cast<int32_t>(v.error);
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int32_t iterations,
+                                                             float* sink, uint64_t stream) {
+  if (blocks <= 0 || iterations <= 0 || !sink)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  return from_cuda(ffma_peak_probe(blocks, iterations, sink, as_stream(stream)));
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL
+xvram_b200_compat_runtime_info(xvram_b200_runtime_info_v1* out) {
+  return compat_runtime_info(out);
+}
+
+} // extern "C"

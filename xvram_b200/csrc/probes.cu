@@ -1,0 +1,40 @@
+// probes.cu -- FP32 pipe peak probe.
+//
+// The FP32 (non-tensor) peak is the denominator of the SGEMM roofline.  It is not in
+// the driver-measured peak file, so the bench measures it on the same device in the
+// same run: 8 independent FFMA chains per thread, enough to keep all four SM
+// sub-partitions issuing an FFMA every cycle, with no memory traffic.
+#include "kernels.hpp"
+
+namespace xvram {
+namespace {
+
+__global__ void __launch_bounds__(256) ffma_peak_kernel(int iterations, float* sink) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    v[j] = 1.0f + 1e-7f * static_cast<float>(threadIdx.x + j);
+  const float x = 0.999999f, y = 1e-7f;
+  for (int it = 0; it < iterations; ++it) {
+#pragma unroll
+    for (int r = 0; r < 64; ++r)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = fmaf(v[j], x, y);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    s += v[j];
+  if (s == 123.456f) // never true for these inputs; keeps the chains live
+    sink[0] = s;
+}
+
+} // namespace
+
+cudaError_t ffma_peak_probe(int blocks, int iterations, float* sink, cudaStream_t stream) {
+  ffma_peak_kernel<<<blocks, 256, 0, stream>>>(iterations, sink);
+  return cudaGetLastError();
+}
+
+} // namespace xvram

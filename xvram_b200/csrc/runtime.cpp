@@ -1,0 +1,857 @@
+// runtime.cpp -- see runtime.hpp.
+#include "runtime.hpp"
+#include "host_util.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <set>
+#include <utility>
+
+namespace xvram {
+namespace {
+
+constexpr uint64_t kArenaOwner = UINT64_MAX;
+
+struct Chunk {
+  int32_t frame = -1;         // frame index while resident
+  bool written = false;       // holds caller data (else contents are undefined)
+  bool backing_valid = false; // host backing holds the current data
+  bool dev_valid = false;     // the resident frame holds the current data
+};
+
+struct Alloc {
+  uint64_t id = 0;
+  uint64_t bytes = 0;
+  uint64_t va = 0;
+  uint64_t reserved = 0;
+  void* host = nullptr;
+  std::vector<Chunk> chunks;
+  bool live = true;
+};
+
+struct Frame {
+  uint64_t handle = 0;
+  uint64_t owner = 0; // allocation id, kArenaOwner, or 0 when free
+  uint32_t chunk = 0;
+  uint64_t touch = 0;
+  EventId last_use = 0;
+  bool used = false;      // has held data before (the next owner is a handle reuse)
+  bool pending = false;   // last_use has been recorded
+};
+
+} // namespace
+
+struct Runtime::Impl {
+  RuntimeConfig cfg;
+  std::unique_ptr<Device> dev;
+  DeviceInfo info;
+  xvram_session_telemetry_v1 t{};
+  RuntimeExtra x;
+  uint64_t cb = 0;       // chunk bytes
+  uint64_t capacity = 0; // frames the budget allows
+  std::vector<Frame> frames;
+  std::map<uint64_t, Alloc> allocs;
+  uint64_t next_id = 1;
+  uint64_t clock = 0;
+  StreamId s_h2d = 0, s_d2h = 0, s_compute = 0;
+  EventId e_a = 0, e_b = 0;
+  std::vector<EventId> event_pool;
+  bool opened = false;
+
+  uint64_t chunk_len(const Alloc& a, uint64_t c) const {
+    return std::min<uint64_t>(cb, a.bytes - c * cb);
+  }
+
+  Error get_event(EventId* e) {
+    if (!event_pool.empty()) {
+      *e = event_pool.back();
+      event_pool.pop_back();
+      return {};
+    }
+    return dev->event_create(e);
+  }
+  void put_event(EventId e) {
+    if (e)
+      event_pool.push_back(e);
+  }
+
+  void update_resident() {
+    uint64_t owned = 0;
+    for (const auto& f : frames)
+      if (f.owner)
+        ++owned;
+    t.resident_bytes = owned * cb;
+    t.resident_bytes_peak = std::max(t.resident_bytes_peak, t.resident_bytes);
+  }
+
+  Error ensure_backing(Alloc& a) {
+    if (a.host)
+      return {};
+    void* p = nullptr;
+    if (Error e = dev->host_alloc(a.bytes, &p))
+      return e;
+    a.host = p;
+    x.host_backing_bytes += a.bytes;
+    x.host_backing_peak_bytes = std::max(x.host_backing_peak_bytes, x.host_backing_bytes);
+    t.pinned_staging_bytes = x.host_backing_bytes;
+    return {};
+  }
+
+  Error wait_idle(Frame& f) {
+    if (f.pending) {
+      if (Error e = dev->event_sync(f.last_use))
+        return e;
+      f.pending = false;
+      ++t.event_boundaries;
+    }
+    return {};
+  }
+
+  // Takes frame `fi` away from its chunk: waits for the chunk's last device use, writes
+  // it back to the host when the device copy is newer, and unmaps it.
+  Error evict_frame(size_t fi) {
+    Frame& f = frames[fi];
+    if (!f.owner || f.owner == kArenaOwner)
+      return {};
+    Alloc& a = allocs.at(f.owner);
+    Chunk& ch = a.chunks[f.chunk];
+    if (Error e = wait_idle(f))
+      return e;
+    const uint64_t off = static_cast<uint64_t>(f.chunk) * cb;
+    const uint64_t len = chunk_len(a, f.chunk);
+    if (ch.written && ch.dev_valid && !ch.backing_valid) {
+      if (Error e = ensure_backing(a))
+        return e;
+      if (Error e = dev->copy_2d(reinterpret_cast<uint64_t>(a.host) + off, len, a.va + off, len,
+                                 len, 1, CopyDir::d2h, s_d2h))
+        return e;
+      if (Error e = dev->stream_sync(s_d2h))
+        return e;
+      ch.backing_valid = true;
+      ++t.dirty_evictions;
+      ++t.writebacks_completed;
+      t.bytes_d2h += len;
+    } else {
+      ++t.clean_evictions;
+    }
+    if (Error e = dev->unmap(a.va + off, cb))
+      return e;
+    ++t.unmaps;
+    ch.frame = -1;
+    ch.dev_valid = false;
+    f.owner = 0;
+    update_resident();
+    return {};
+  }
+
+  // A free frame for a new owner; creates one while under capacity, else evicts the
+  // least recently used frame whose chunk is not in `keep`.
+  Error acquire_frame(const std::set<std::pair<uint64_t, uint32_t>>& keep, size_t* out) {
+    for (size_t i = 0; i < frames.size(); ++i) {
+      if (!frames[i].owner) {
+        *out = i;
+        if (frames[i].used)
+          ++t.handle_reuses;
+        return {};
+      }
+    }
+    if (frames.size() < capacity) {
+      Frame f;
+      if (Error e = dev->handle_create(cb, &f.handle))
+        return e;
+      if (Error e = dev->event_create(&f.last_use)) {
+        dev->handle_release(f.handle);
+        return e;
+      }
+      ++t.physical_handles_created;
+      frames.push_back(f);
+      *out = frames.size() - 1;
+      return {};
+    }
+    size_t victim = frames.size();
+    uint64_t oldest = UINT64_MAX;
+    for (size_t i = 0; i < frames.size(); ++i) {
+      const Frame& f = frames[i];
+      if (f.owner == kArenaOwner || keep.count({f.owner, f.chunk}))
+        continue;
+      if (f.touch < oldest) {
+        oldest = f.touch;
+        victim = i;
+      }
+    }
+    if (victim == frames.size())
+      return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "residency", "acquire_frame",
+                        "every frame is pinned by the current operation");
+    if (Error e = evict_frame(victim))
+      return e;
+    ++t.handle_reuses;
+    *out = victim;
+    return {};
+  }
+
+  // Maps chunk c of `a` if needed; uploads its host data when `upload` and the host copy
+  // is the current one.  Uploads go on s_h2d.
+  Error make_resident(Alloc& a, uint32_t c, bool upload,
+                      const std::set<std::pair<uint64_t, uint32_t>>& keep, bool* uploaded) {
+    Chunk& ch = a.chunks[c];
+    if (ch.frame >= 0) {
+      ++t.cache_hits;
+      frames[static_cast<size_t>(ch.frame)].touch = ++clock;
+      return {};
+    }
+    ++t.cache_misses;
+    size_t fi = 0;
+    if (Error e = acquire_frame(keep, &fi))
+      return e;
+    Frame& f = frames[fi];
+    const uint64_t off = static_cast<uint64_t>(c) * cb;
+    if (Error e = dev->map(a.va + off, cb, f.handle))
+      return e;
+    ++t.mappings;
+    ++t.set_access_calls;
+    f.owner = a.id;
+    f.chunk = c;
+    f.used = true;
+    f.touch = ++clock;
+    ch.frame = static_cast<int32_t>(fi);
+    ch.dev_valid = !ch.written; // undefined contents are valid anywhere
+    if (upload && ch.written && ch.backing_valid && a.host) {
+      const uint64_t len = chunk_len(a, c);
+      if (Error e = dev->copy_2d(a.va + off, len, reinterpret_cast<uint64_t>(a.host) + off, len,
+                                 len, 1, CopyDir::h2d, s_h2d))
+        return e;
+      t.bytes_h2d += len;
+      ch.dev_valid = true;
+      *uploaded = true;
+    }
+    update_resident();
+    return {};
+  }
+
+  uint64_t free_frames() const {
+    uint64_t n = capacity - frames.size();
+    for (const auto& f : frames)
+      if (!f.owner)
+        ++n;
+    return n;
+  }
+
+  Error evict_all() {
+    for (size_t i = 0; i < frames.size(); ++i)
+      if (frames[i].owner && frames[i].owner != kArenaOwner)
+        if (Error e = evict_frame(i))
+          return e;
+    return {};
+  }
+
+  Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
+                      const std::set<std::pair<uint64_t, uint32_t>>& keep);
+  Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
+};
+
+Runtime::Runtime() : impl_(std::make_unique<Impl>()) {}
+Runtime::~Runtime() {
+  if (impl_ && impl_->opened)
+    (void)close();
+}
+
+const DeviceInfo& Runtime::info() const { return impl_->info; }
+const xvram_session_telemetry_v1& Runtime::counters() const { return impl_->t; }
+const RuntimeExtra& Runtime::extra() const { return impl_->x; }
+uint64_t Runtime::chunk_bytes() const { return impl_->cb; }
+uint64_t Runtime::frame_capacity() const { return impl_->capacity; }
+
+Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
+  Impl& m = *impl_;
+  m.cfg = cfg;
+  m.dev = std::move(device);
+  m.t = xvram_session_telemetry_v1{};
+  m.t.struct_size = sizeof(m.t);
+  if (Error e = m.dev->open(cfg.device_ordinal, &m.info))
+    return e;
+  if (cfg.chunk_bytes == 0 || (cfg.chunk_bytes & (cfg.chunk_bytes - 1)) != 0 ||
+      (m.info.vmm_granularity && cfg.chunk_bytes % m.info.vmm_granularity != 0))
+    return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "runtime", "open",
+                      "chunk size must be a power of two multiple of the VMM granularity");
+  m.cb = cfg.chunk_bytes;
+  uint64_t free_b = 0, total_b = 0;
+  if (Error e = m.dev->mem_get_info(&free_b, &total_b))
+    return e;
+  const uint64_t usable = free_b > cfg.headroom_bytes ? free_b - cfg.headroom_bytes : 0;
+  const uint64_t budget = cfg.cache_target_bytes ? std::min(cfg.cache_target_bytes, usable) : usable;
+  m.capacity = budget / m.cb;
+  if (m.capacity < 2)
+    return make_error(XVRAM_STATUS_DEVICE_OUT_OF_MEMORY, "runtime", "open",
+                      "device budget is smaller than two frames");
+  m.t.cache_target_bytes = m.capacity * m.cb;
+  m.t.cache_target_minimum_bytes = 2 * m.cb;
+  m.t.cache_target_maximum_bytes = usable;
+  m.t.cuda_driver_version = static_cast<uint32_t>(m.info.driver_version);
+  m.t.cuda_free_bytes_minimum = free_b;
+  m.t.cuda_free_bytes_end = free_b;
+  m.t.budget_sample_count = 1;
+  m.t.flags = XVRAM_TELEMETRY_STABLE_VIRTUAL_ADDRESSES | XVRAM_TELEMETRY_NO_PHYSICAL_ALIASES;
+  if (Error e = m.dev->stream_create(&m.s_h2d))
+    return e;
+  if (Error e = m.dev->stream_create(&m.s_d2h))
+    return e;
+  if (Error e = m.dev->stream_create(&m.s_compute))
+    return e;
+  if (Error e = m.dev->event_create(&m.e_a))
+    return e;
+  if (Error e = m.dev->event_create(&m.e_b))
+    return e;
+  m.opened = true;
+  return {};
+}
+
+Error Runtime::close() {
+  Impl& m = *impl_;
+  if (!m.opened)
+    return {};
+  Error first;
+  auto keep = [&first](Error e) {
+    if (e && !first)
+      first = e;
+  };
+  keep(m.dev->stream_sync(m.s_h2d));
+  keep(m.dev->stream_sync(m.s_compute));
+  keep(m.dev->stream_sync(m.s_d2h));
+  for (auto& [id, a] : m.allocs) {
+    for (size_t c = 0; c < a.chunks.size(); ++c) {
+      if (a.chunks[c].frame >= 0) {
+        keep(m.dev->unmap(a.va + c * m.cb, m.cb));
+        ++m.t.unmaps;
+        m.frames[static_cast<size_t>(a.chunks[c].frame)].owner = 0;
+        a.chunks[c].frame = -1;
+      }
+    }
+    if (a.host) {
+      keep(m.dev->host_free(a.host));
+      a.host = nullptr;
+    }
+    keep(m.dev->va_free(a.va, a.reserved));
+  }
+  m.allocs.clear();
+  for (auto& f : m.frames) {
+    keep(m.dev->handle_release(f.handle));
+    ++m.t.physical_handles_released;
+    keep(m.dev->event_destroy(f.last_use));
+  }
+  m.frames.clear();
+  for (EventId e : m.event_pool)
+    keep(m.dev->event_destroy(e));
+  m.event_pool.clear();
+  keep(m.dev->close());
+  m.opened = false;
+  m.t.resident_bytes = 0;
+  return first;
+}
+
+Error Runtime::allocate(uint64_t bytes, uint64_t* id, uint64_t* va) {
+  Impl& m = *impl_;
+  if (bytes == 0 || bytes > UINT64_MAX - m.cb)
+    return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "runtime", "allocate", "invalid size");
+  Alloc a;
+  a.id = m.next_id++;
+  a.bytes = bytes;
+  a.reserved = round_up(bytes, m.cb);
+  if (Error e = m.dev->va_reserve(a.reserved, &a.va))
+    return e;
+  a.chunks.resize(static_cast<size_t>(a.reserved / m.cb));
+  *id = a.id;
+  *va = a.va;
+  m.allocs.emplace(a.id, std::move(a));
+  return {};
+}
+
+Error Runtime::release(uint64_t id) {
+  Impl& m = *impl_;
+  auto it = m.allocs.find(id);
+  if (it == m.allocs.end() || !it->second.live)
+    return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "runtime", "release", "unknown allocation");
+  Alloc& a = it->second;
+  for (size_t c = 0; c < a.chunks.size(); ++c) {
+    Chunk& ch = a.chunks[c];
+    if (ch.frame < 0)
+      continue;
+    Frame& f = m.frames[static_cast<size_t>(ch.frame)];
+    if (Error e = m.wait_idle(f))
+      return e;
+    if (Error e = m.dev->unmap(a.va + c * m.cb, m.cb))
+      return e;
+    ++m.t.unmaps;
+    f.owner = 0;
+    ch.frame = -1;
+  }
+  if (a.host) {
+    if (Error e = m.dev->host_free(a.host))
+      return e;
+    m.x.host_backing_bytes -= a.bytes;
+    a.host = nullptr;
+  }
+  // The address range stays reserved (tombstoned) until close so a freed pointer can
+  // never alias a later allocation.
+  a.live = false;
+  a.chunks.clear();
+  a.chunks.shrink_to_fit();
+  ++m.x.retired_va_reservations;
+  m.x.retired_va_bytes += a.reserved;
+  m.update_resident();
+  return {};
+}
+
+Error Runtime::write(uint64_t id, uint64_t offset, const void* src, uint64_t bytes) {
+  Impl& m = *impl_;
+  Alloc& a = m.allocs.at(id);
+  if (bytes == 0)
+    return {};
+  const uint32_t c0 = static_cast<uint32_t>(offset / m.cb);
+  const uint32_t c1 = static_cast<uint32_t>((offset + bytes - 1) / m.cb);
+  bool all_resident = true;
+  uint64_t missing = 0;
+  for (size_t c = 0; c < a.chunks.size(); ++c)
+    if (a.chunks[c].frame < 0) {
+      ++missing;
+      if (c >= c0 && c <= c1)
+        all_resident = false;
+    }
+  const bool to_device = all_resident || missing <= m.free_frames();
+  if (to_device) {
+    // Write-allocate: the data goes straight to HBM and the chunks become dirty.
+    std::set<std::pair<uint64_t, uint32_t>> keep;
+    for (uint32_t c = c0; c <= c1; ++c)
+      keep.insert({a.id, c});
+    bool uploaded = false;
+    for (uint32_t c = c0; c <= c1; ++c) {
+      const uint64_t cbeg = static_cast<uint64_t>(c) * m.cb;
+      const uint64_t cend = cbeg + m.chunk_len(a, c);
+      const bool covers = offset <= cbeg && offset + bytes >= cend;
+      if (Error e = m.make_resident(a, c, !covers, keep, &uploaded))
+        return e;
+    }
+    // The copy must follow any earlier device work on these frames and any upload.
+    if (Error e = m.dev->event_record(m.e_a, m.s_compute))
+      return e;
+    if (Error e = m.dev->stream_wait_event(m.s_h2d, m.e_a))
+      return e;
+    if (Error e = m.dev->copy_2d(a.va + offset, bytes, reinterpret_cast<uint64_t>(src), bytes,
+                                 bytes, 1, CopyDir::h2d, m.s_h2d))
+      return e;
+    if (Error e = m.dev->stream_sync(m.s_h2d))
+      return e;
+    m.t.bytes_h2d += bytes;
+    for (uint32_t c = c0; c <= c1; ++c) {
+      Chunk& ch = a.chunks[c];
+      ch.written = true;
+      ch.dev_valid = true;
+      ch.backing_valid = false;
+    }
+    return {};
+  }
+  // Host path: bring any newer device data home first, then update the backing.
+  for (uint32_t c = c0; c <= c1; ++c)
+    if (a.chunks[c].frame >= 0)
+      if (Error e = m.evict_frame(static_cast<size_t>(a.chunks[c].frame)))
+        return e;
+  if (Error e = m.ensure_backing(a))
+    return e;
+  // Chunks written for the first time but only partly: their other bytes are undefined,
+  // which the backing already represents.
+  parallel_memcpy(static_cast<char*>(a.host) + offset, src, bytes);
+  for (uint32_t c = c0; c <= c1; ++c) {
+    Chunk& ch = a.chunks[c];
+    ch.written = true;
+    ch.backing_valid = true;
+    ch.dev_valid = false;
+  }
+  return {};
+}
+
+Error Runtime::read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes) {
+  Impl& m = *impl_;
+  Alloc& a = m.allocs.at(id);
+  if (bytes == 0)
+    return {};
+  const uint64_t end = offset + bytes;
+  bool any_dma = false;
+  if (Error e = m.dev->event_record(m.e_a, m.s_compute))
+    return e;
+  if (Error e = m.dev->stream_wait_event(m.s_d2h, m.e_a))
+    return e;
+  uint64_t pos = offset;
+  while (pos < end) {
+    const uint32_t c = static_cast<uint32_t>(pos / m.cb);
+    const uint64_t cend = std::min(end, static_cast<uint64_t>(c + 1) * m.cb);
+    // Merge consecutive chunks with the same source into one copy.
+    const Chunk& ch = a.chunks[c];
+    const bool from_dev = ch.frame >= 0 && ch.dev_valid && ch.written;
+    uint64_t run_end = cend;
+    while (run_end < end) {
+      const Chunk& nx = a.chunks[static_cast<size_t>(run_end / m.cb)];
+      const bool nx_dev = nx.frame >= 0 && nx.dev_valid && nx.written;
+      if (nx_dev != from_dev || nx.written != ch.written)
+        break;
+      run_end = std::min(end, (run_end / m.cb + 1) * m.cb);
+    }
+    char* out = static_cast<char*>(dst) + (pos - offset);
+    const uint64_t len = run_end - pos;
+    if (from_dev) {
+      if (Error e = m.dev->copy_2d(reinterpret_cast<uint64_t>(out), len, a.va + pos, len, len, 1,
+                                   CopyDir::d2h, m.s_d2h))
+        return e;
+      m.t.bytes_d2h += len;
+      any_dma = true;
+    } else if (ch.written && a.host) {
+      parallel_memcpy(out, static_cast<const char*>(a.host) + pos, len);
+    } else {
+      std::memset(out, 0, len); // never written: contents are undefined, report zeros
+    }
+    pos = run_end;
+  }
+  if (any_dma)
+    if (Error e = m.dev->stream_sync(m.s_d2h))
+      return e;
+  return {};
+}
+
+Error Runtime::synchronize() {
+  Impl& m = *impl_;
+  if (Error e = m.dev->stream_sync(m.s_h2d))
+    return e;
+  if (Error e = m.dev->stream_sync(m.s_compute))
+    return e;
+  return m.dev->stream_sync(m.s_d2h);
+}
+
+Error Runtime::mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes) {
+  Impl& m = *impl_;
+  if (Error e = m.dev->mem_get_info(free_bytes, total_bytes))
+    return e;
+  m.t.cuda_free_bytes_end = *free_bytes;
+  m.t.cuda_free_bytes_minimum = std::min(m.t.cuda_free_bytes_minimum, *free_bytes);
+  ++m.t.budget_sample_count;
+  return {};
+}
+
+Error Runtime::gemm(const GemmCall& call) {
+  Impl& m = *impl_;
+  const auto t0 = std::chrono::steady_clock::now();
+  Alloc& A = m.allocs.at(call.shape.a.allocation_id);
+  Alloc& B = m.allocs.at(call.shape.b.allocation_id);
+  Alloc& C = m.allocs.at(call.shape.c.allocation_id);
+  std::set<std::pair<uint64_t, uint32_t>> keep;
+  const MatrixRef* mats[3] = {&call.shape.a, &call.shape.b, &call.shape.c};
+  Alloc* owners[3] = {&A, &B, &C};
+  for (int i = 0; i < 3; ++i) {
+    uint64_t b = 0, e = 0;
+    matrix_byte_span(*mats[i], &b, &e);
+    for (uint64_t c = b / m.cb; c <= (e - 1) / m.cb; ++c)
+      keep.insert({owners[i]->id, static_cast<uint32_t>(c)});
+  }
+  Error err = keep.size() <= m.capacity ? m.gemm_in_place(call, A, B, C, keep)
+                                        : m.gemm_streamed(call, A, B, C);
+  m.x.last_gemm_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  m.t.last_transaction_ms = m.x.last_gemm_ms;
+  if (!err)
+    ++m.t.transactions_completed;
+  return err;
+}
+
+Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
+                                   const std::set<std::pair<uint64_t, uint32_t>>& keep) {
+  bool uploaded = false;
+  for (const auto& [id, c] : keep)
+    if (Error e = make_resident(allocs.at(id), c, true, keep, &uploaded))
+      return e;
+  if (uploaded) {
+    if (Error e = dev->event_record(e_a, s_h2d))
+      return e;
+    if (Error e = dev->stream_wait_event(s_compute, e_a))
+      return e;
+  }
+  const GemmShape& s = call.shape;
+  ++x.tiles_submitted;
+  ++x.gemm_in_place;
+  if (Error e = dev->sgemm(s.op_a, s.op_b, static_cast<int64_t>(s.m), static_cast<int64_t>(s.n),
+                           static_cast<int64_t>(s.k), call.alpha, A.va + s.a.offset_bytes,
+                           static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
+                           static_cast<int64_t>(s.b.ld), call.beta, C.va + s.c.offset_bytes,
+                           static_cast<int64_t>(s.c.ld), s_compute))
+    return e;
+  for (const auto& [id, c] : keep) {
+    Frame& f = frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)];
+    if (Error e = dev->event_record(f.last_use, s_compute))
+      return e;
+    f.pending = true;
+  }
+  uint32_t word = 0;
+  if (Error e = dev->kernel_status(s_compute, &word))
+    return e;
+  if (word)
+    return make_error(XVRAM_STATUS_TIMEOUT, "executor", "sgemm",
+                      "a kernel pipeline wait exceeded its limit");
+  for (const auto& [id, c] : keep) {
+    if (id != C.id)
+      continue;
+    Chunk& ch = C.chunks[c];
+    ch.written = true;
+    ch.dev_valid = true;
+    ch.backing_valid = false;
+    frames[static_cast<size_t>(ch.frame)].pending = false;
+  }
+  for (const auto& [id, c] : keep)
+    frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)].pending = false;
+  ++x.tiles_retired;
+  return {};
+}
+
+Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C) {
+  const GemmShape& s = call.shape;
+  // 1. Every frame goes to the slot arena: write back and unmap all resident chunks.
+  if (Error e = evict_all())
+    return e;
+  for (Alloc* a : {&A, &B, &C})
+    if (Error e = ensure_backing(*a))
+      return e;
+  // 2. Plan against the whole pool.
+  PlanProblem pp;
+  pp.op_a = s.op_a;
+  pp.op_b = s.op_b;
+  pp.m = static_cast<int64_t>(s.m);
+  pp.n = static_cast<int64_t>(s.n);
+  pp.k = static_cast<int64_t>(s.k);
+  pp.beta_nonzero = call.beta != 0.0f;
+  PlanLimits lim;
+  lim.budget_bytes = capacity * cb;
+  lim.quantum_bytes = cb;
+  lim.flops_per_s = cfg.flops_per_s;
+  lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
+  lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
+  Plan plan;
+  const PlanStatus ps = make_panel_plan(pp, lim, &plan);
+  if (ps != PlanStatus::ok)
+    return make_error(ps == PlanStatus::budget_too_small ? XVRAM_STATUS_BUDGET_PRESSURE
+                                                         : XVRAM_STATUS_INTERNAL,
+                      "planner", "make_panel_plan", "no panel geometry fits the device budget");
+  x.last_mb = plan.mb;
+  x.last_nb = plan.nb;
+  x.last_kb = plan.kb;
+  x.last_steps = static_cast<int64_t>(plan.steps.size());
+  x.last_panel_slots = plan.panel_slots;
+  ++x.gemm_streamed;
+
+  // 3. Slot arena: panel slots then C slots, each a run of whole frames.
+  const uint64_t fps = plan.slot_bytes / cb;
+  const uint64_t fpc = plan.c_slot_bytes / cb;
+  const uint64_t nframes = fps * static_cast<uint64_t>(plan.panel_slots) +
+                           fpc * static_cast<uint64_t>(plan.c_slots);
+  while (frames.size() < nframes) {
+    Frame f;
+    if (Error e = dev->handle_create(cb, &f.handle))
+      return e;
+    if (Error e = dev->event_create(&f.last_use)) {
+      dev->handle_release(f.handle);
+      return e;
+    }
+    ++t.physical_handles_created;
+    frames.push_back(f);
+  }
+  uint64_t arena = 0;
+  if (Error e = dev->va_reserve(nframes * cb, &arena))
+    return e;
+  std::vector<size_t> arena_frames;
+  Error err;
+  for (size_t i = 0; i < frames.size() && arena_frames.size() < nframes; ++i) {
+    if (frames[i].owner)
+      continue;
+    if ((err = dev->map(arena + arena_frames.size() * cb, cb, frames[i].handle)))
+      break;
+    ++t.mappings;
+    ++t.set_access_calls;
+    if (frames[i].used)
+      ++t.handle_reuses;
+    frames[i].owner = kArenaOwner;
+    frames[i].used = true;
+    arena_frames.push_back(i);
+  }
+  update_resident();
+  const uint64_t c_base = arena + fps * cb * static_cast<uint64_t>(plan.panel_slots);
+
+  std::vector<EventId> ready(static_cast<size_t>(plan.panel_slots)),
+      used(static_cast<size_t>(plan.panel_slots)), c_ready(static_cast<size_t>(plan.c_slots)),
+      c_done(static_cast<size_t>(plan.c_slots)), c_wb(static_cast<size_t>(plan.c_slots));
+  std::vector<char> used_rec(static_cast<size_t>(plan.panel_slots), 0),
+      wb_rec(static_cast<size_t>(plan.c_slots), 0);
+  for (auto* v : {&ready, &used, &c_ready, &c_done, &c_wb})
+    for (auto& e : *v)
+      if (!err)
+        err = get_event(&e);
+
+  const uint64_t ha = reinterpret_cast<uint64_t>(A.host) + s.a.offset_bytes;
+  const uint64_t hb = reinterpret_cast<uint64_t>(B.host) + s.b.offset_bytes;
+  const uint64_t hc = reinterpret_cast<uint64_t>(C.host) + s.c.offset_bytes;
+  const int64_t M = static_cast<int64_t>(s.m), N = static_cast<int64_t>(s.n),
+                K = static_cast<int64_t>(s.k);
+  const uint64_t lda = s.a.ld, ldb = s.b.ld, ldc = s.c.ld;
+  const int64_t mb = plan.mb, nb = plan.nb, kb = plan.kb;
+  const auto slot_va = [&](int32_t slot) {
+    return arena + static_cast<uint64_t>(slot) * fps * cb;
+  };
+
+  // 4. Replay the plan.
+  for (size_t si = 0; si < plan.steps.size() && !err; ++si) {
+    const PlanStep& st = plan.steps[si];
+    const int64_t m0 = static_cast<int64_t>(st.bm) * mb, n0 = static_cast<int64_t>(st.bn) * nb,
+                  k0 = static_cast<int64_t>(st.bk) * kb;
+    const int64_t mr = std::min(mb, M - m0), nr = std::min(nb, N - n0), kr = std::min(kb, K - k0);
+    for (uint32_t li = st.load_begin; li < st.load_begin + st.load_count && !err; ++li) {
+      const PanelLoad& ld = plan.loads[li];
+      const size_t sl = static_cast<size_t>(ld.slot);
+      if (used_rec[sl] && (err = dev->stream_wait_event(s_h2d, used[sl])))
+        break;
+      const int64_t lk0 = static_cast<int64_t>(ld.kpanel) * kb;
+      const int64_t lkr = std::min(kb, K - lk0);
+      uint64_t src = 0, spitch = 0, width = 0, height = 0, dpitch = 0;
+      if (ld.operand == 0) {
+        const int64_t lm0 = static_cast<int64_t>(ld.block) * mb, lmr = std::min(mb, M - lm0);
+        if (s.op_a == 0) { // A is m x k: kr columns of mr floats
+          src = ha + (static_cast<uint64_t>(lm0) + static_cast<uint64_t>(lk0) * lda) * 4;
+          width = static_cast<uint64_t>(lmr) * 4;
+          height = static_cast<uint64_t>(lkr);
+          dpitch = static_cast<uint64_t>(mb) * 4;
+        } else { // A is k x m: mr columns of kr floats
+          src = ha + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(lm0) * lda) * 4;
+          width = static_cast<uint64_t>(lkr) * 4;
+          height = static_cast<uint64_t>(lmr);
+          dpitch = static_cast<uint64_t>(kb) * 4;
+        }
+        spitch = lda * 4;
+      } else {
+        const int64_t ln0 = static_cast<int64_t>(ld.block) * nb, lnr = std::min(nb, N - ln0);
+        if (s.op_b == 0) { // B is k x n: nr columns of kr floats
+          src = hb + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(ln0) * ldb) * 4;
+          width = static_cast<uint64_t>(lkr) * 4;
+          height = static_cast<uint64_t>(lnr);
+          dpitch = static_cast<uint64_t>(kb) * 4;
+        } else { // B is n x k: kr columns of nr floats
+          src = hb + (static_cast<uint64_t>(ln0) + static_cast<uint64_t>(lk0) * ldb) * 4;
+          width = static_cast<uint64_t>(lnr) * 4;
+          height = static_cast<uint64_t>(lkr);
+          dpitch = static_cast<uint64_t>(nb) * 4;
+        }
+        spitch = ldb * 4;
+      }
+      if ((err = dev->copy_2d(slot_va(ld.slot), dpitch, src, spitch, width, height, CopyDir::h2d,
+                              s_h2d)))
+        break;
+      if ((err = dev->event_record(ready[sl], s_h2d)))
+        break;
+      t.bytes_h2d += width * height;
+      ++t.cache_misses;
+      if (ld.evicts) {
+        ++t.clean_evictions;
+        ++t.handle_reuses;
+      }
+    }
+    if (err)
+      break;
+    t.cache_hits += 2 - st.load_count;
+    const size_t cs = static_cast<size_t>(st.c_slot);
+    const uint64_t cva = c_base + static_cast<uint64_t>(cs) * fpc * cb;
+    float beta_eff = 1.0f;
+    if (st.first_k) {
+      beta_eff = call.beta;
+      if (call.beta != 0.0f) {
+        if (wb_rec[cs] && (err = dev->stream_wait_event(s_h2d, c_wb[cs])))
+          break;
+        if ((err = dev->copy_2d(cva, static_cast<uint64_t>(mb) * 4,
+                                hc + (static_cast<uint64_t>(m0) + static_cast<uint64_t>(n0) * ldc) * 4,
+                                ldc * 4, static_cast<uint64_t>(mr) * 4, static_cast<uint64_t>(nr),
+                                CopyDir::h2d, s_h2d)))
+          break;
+        t.bytes_h2d += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4;
+        if ((err = dev->event_record(c_ready[cs], s_h2d)) ||
+            (err = dev->stream_wait_event(s_compute, c_ready[cs])))
+          break;
+      } else if (wb_rec[cs] && (err = dev->stream_wait_event(s_compute, c_wb[cs]))) {
+        break;
+      }
+    }
+    if ((err = dev->stream_wait_event(s_compute, ready[static_cast<size_t>(st.slot_a)])) ||
+        (err = dev->stream_wait_event(s_compute, ready[static_cast<size_t>(st.slot_b)])))
+      break;
+    const int64_t lda_s = s.op_a == 0 ? mb : kb;
+    const int64_t ldb_s = s.op_b == 0 ? kb : nb;
+    if ((err = dev->sgemm(s.op_a, s.op_b, mr, nr, kr, call.alpha, slot_va(st.slot_a), lda_s,
+                          slot_va(st.slot_b), ldb_s, beta_eff, cva, mb, s_compute)))
+      break;
+    ++x.tiles_submitted;
+    for (int32_t sl : {st.slot_a, st.slot_b}) {
+      if ((err = dev->event_record(used[static_cast<size_t>(sl)], s_compute)))
+        break;
+      used_rec[static_cast<size_t>(sl)] = 1;
+    }
+    if (err)
+      break;
+    if (st.last_k) {
+      if ((err = dev->event_record(c_done[cs], s_compute)) ||
+          (err = dev->stream_wait_event(s_d2h, c_done[cs])) ||
+          (err = dev->copy_2d(hc + (static_cast<uint64_t>(m0) + static_cast<uint64_t>(n0) * ldc) * 4,
+                              ldc * 4, cva, static_cast<uint64_t>(mb) * 4,
+                              static_cast<uint64_t>(mr) * 4, static_cast<uint64_t>(nr),
+                              CopyDir::d2h, s_d2h)) ||
+          (err = dev->event_record(c_wb[cs], s_d2h)))
+        break;
+      wb_rec[cs] = 1;
+      t.bytes_d2h += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4;
+      ++t.writebacks_completed;
+    }
+  }
+
+  // 5. Drain, check the kernels' error word, dissolve the arena.
+  Error drain;
+  if (!(drain = dev->stream_sync(s_h2d)) && !(drain = dev->stream_sync(s_compute)))
+    drain = dev->stream_sync(s_d2h);
+  if (!err && drain)
+    err = drain;
+  if (!err) {
+    uint32_t word = 0;
+    err = dev->kernel_status(s_compute, &word);
+    if (!err && word)
+      err = make_error(XVRAM_STATUS_TIMEOUT, "executor", "sgemm",
+                       "a kernel pipeline wait exceeded its limit");
+  }
+  if (!err)
+    x.tiles_retired += plan.steps.size();
+  for (size_t i = 0; i < arena_frames.size(); ++i) {
+    Error e = dev->unmap(arena + i * cb, cb);
+    if (e && !err)
+      err = e;
+    ++t.unmaps;
+    frames[arena_frames[i]].owner = 0;
+  }
+  if (Error e = dev->va_free(arena, nframes * cb); e && !err)
+    err = e;
+  for (auto* v : {&ready, &used, &c_ready, &c_done, &c_wb})
+    for (auto& e : *v)
+      put_event(e);
+  update_resident();
+  if (err)
+    return err;
+  // C's rows/columns inside the matrix are now current in the host backing.
+  uint64_t cb0 = 0, ce0 = 0;
+  matrix_byte_span(s.c, &cb0, &ce0);
+  for (uint64_t c = cb0 / cb; c <= (ce0 - 1) / cb; ++c) {
+    Chunk& ch = C.chunks[static_cast<size_t>(c)];
+    ch.written = true;
+    ch.backing_valid = true;
+    ch.dev_valid = false;
+  }
+  return {};
+}
+
+} // namespace xvram

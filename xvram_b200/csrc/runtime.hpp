@@ -1,0 +1,103 @@
+// runtime.hpp -- residency runtime and GEMM executor.
+//
+// Replaces the reference's residency::Runtime (reference src/residency/runtime.hpp:317-372,
+// runtime.cpp) and gemm::execute_tiled_gemm (reference src/gemm/executor.cpp:331-454).
+//
+// Memory model
+//   * Every allocation owns a stable device virtual-address reservation (returned to
+//     the caller as its "device pointer") cut into chunks of session.chunk_size_bytes,
+//     and an optional page-locked host backing store created on first need.
+//   * Device memory is a pool of physical frames (one cuMemCreate handle per chunk-sized
+//     frame) capped by the device budget.  A resident chunk has a frame mapped at its
+//     stable address; frames are created once and then reused (handle reuse), never
+//     released before close.
+//   * A chunk is dirty when the device holds newer data than the host backing; dirty
+//     chunks are written back before their frame is reused (dirty eviction).
+//
+// GEMM execution
+//   * In place: when the chunks under A, B and C fit in the frame pool at once they are
+//     made resident and the sm_100a kernel runs directly on the stable addresses;
+//     C stays resident and dirty (later reads come straight from HBM).
+//   * Streamed (out of core): otherwise the runtime writes back and unmaps every
+//     resident chunk, maps the pool's frames into a slot arena, and replays the panel
+//     plan (planner.hpp): pitched H2D panel copies on a copy stream, one kernel per
+//     (C block, K panel) step on the compute stream (beta applied on the block's first
+//     K panel, 1 afterwards), C blocks written back on a third stream.  Slot reuse is
+//     ordered by per-slot completion events, so copies run ahead of compute without
+//     host waits.
+#pragma once
+
+#include "device.hpp"
+#include "planner.hpp"
+#include "validate.hpp"
+
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+namespace xvram {
+
+struct RuntimeConfig {
+  int device_ordinal = 0;
+  uint64_t chunk_bytes = 64ull << 20;
+  uint64_t cache_target_bytes = 0; // 0 = free device memory at open minus headroom
+  uint64_t headroom_bytes = 512ull << 20;
+  // Planning rates (estimates only; they steer geometry choice, never correctness).
+  double flops_per_s = 70e12;
+  double h2d_bytes_per_s = 50e9;
+  double d2h_bytes_per_s = 50e9;
+};
+
+struct GemmCall {
+  GemmShape shape;
+  float alpha = 1.0f, beta = 0.0f;
+};
+
+// Counters that are not part of xvram_session_telemetry_v1.
+struct RuntimeExtra {
+  uint64_t tiles_submitted = 0;
+  uint64_t tiles_retired = 0;
+  uint64_t gemm_in_place = 0;
+  uint64_t gemm_streamed = 0;
+  uint64_t host_backing_bytes = 0;
+  uint64_t host_backing_peak_bytes = 0;
+  uint64_t retired_va_reservations = 0;
+  uint64_t retired_va_bytes = 0;
+  // Last streamed plan.
+  int64_t last_mb = 0, last_nb = 0, last_kb = 0;
+  int64_t last_steps = 0;
+  int32_t last_panel_slots = 0;
+  double last_gemm_ms = 0;
+};
+
+class Runtime {
+public:
+  Runtime();
+  ~Runtime();
+  Runtime(const Runtime&) = delete;
+  Runtime& operator=(const Runtime&) = delete;
+
+  Error open(const RuntimeConfig& cfg, std::unique_ptr<Device> device);
+  Error close();
+
+  Error allocate(uint64_t bytes, uint64_t* id, uint64_t* va);
+  Error release(uint64_t id);
+  Error write(uint64_t id, uint64_t offset, const void* src, uint64_t bytes);
+  Error read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes);
+  Error gemm(const GemmCall& call);
+  Error synchronize();
+  Error mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes);
+
+  const DeviceInfo& info() const;
+  const xvram_session_telemetry_v1& counters() const;
+  const RuntimeExtra& extra() const;
+  uint64_t chunk_bytes() const;
+  uint64_t frame_capacity() const;
+
+  struct Impl;
+
+private:
+  std::unique_ptr<Impl> impl_;
+};
+
+} // namespace xvram

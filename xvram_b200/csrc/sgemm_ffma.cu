@@ -1,0 +1,439 @@
+// sgemm_ffma.cu -- strict-FP32 tile contraction for sm_100a.
+//
+//   C[m0.., n0..] = alpha * op(A) * op(B) + beta * C      (column-major, op in {N, T})
+//
+// This is the arithmetic the reference delegates to cublasLtMatmul with
+// CUBLAS_COMPUTE_32F_PEDANTIC for every tile of its tiled executor
+// (reference src/gemm/executor.cpp:147-329, src/platform/cublas/cublas_api.cpp:751-918).
+// Every product and sum is an FP32 FFMA; there is no TF32 or reduced-precision step.
+//
+// Main kernel (sgemm_ffma_tma): 128x128 C tile per CTA, K in stages of 32.
+//   * warp 8 (producer): one lane issues 2D TMA loads of the op(A) and op(B) stage
+//     tiles into a 4-deep shared-memory ring, completion on a per-stage "full" mbarrier;
+//   * warps 0-7 (consumers, 256 threads): each thread owns an 8x8 block of C in
+//     registers and runs 64 FFMA per k; a warp releases the stage on an "empty"
+//     mbarrier when done.
+// Shared-memory stage layouts follow the stored layout of each operand so that TMA
+// writes them without transposition:
+//   op(A)=N : A stored M-major -> tile [32 k][128 m], no swizzle.  A thread's rows are
+//             4 consecutive m at tm*4 and 4 more at 64+tm*4 (two LDS.128 per k).
+//   op(A)=T : A stored K-major -> tile [128 m][32 k], 128-byte swizzle.  A thread's rows
+//             are tm + 16*i; one LDS.128 fetches 4 consecutive k of one row.
+//   op(B)=N : B stored K-major -> tile [128 n][32 k], 128-byte swizzle (as op(A)=T).
+//   op(B)=T : B stored N-major -> tile [32 k][128 n], no swizzle (as op(A)=N).
+// Out-of-range rows, columns and k are zero-filled by TMA, so ragged edges need no
+// special path in the main loop; the epilogue predicates its stores.
+//
+// TMA needs 16-byte aligned bases and leading dimensions that are multiples of 4
+// floats.  The out-of-core executor always packs panels that way; the generic
+// kernel below covers every other device-pointer call.
+#include "device_common.cuh"
+#include "kernels.hpp"
+
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+namespace xvram {
+
+// Sticky per-device error word written by kernels whose bounded waits ran out.
+// Bit 0: a consumer gave up on a full barrier; bit 1: the producer gave up on an
+// empty barrier; bit 2: the producer gave up draining its own copies.
+__device__ unsigned int xvram_kernel_error = 0;
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kBK = 32;
+constexpr int kStages = 4;
+constexpr int kConsumerThreads = 256;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kStageFloats = kBM * kBK; // A and B tiles are both 128 x 32
+constexpr uint32_t kStageBytes = 2u * kStageFloats * sizeof(float);
+constexpr int kSmemBytes = 2 * kStages * kStageFloats * sizeof(float) + 1024 /*align*/ + 256;
+
+struct FfmaParams {
+  int m, n, k;
+  int k_tiles;
+  int tiles_m, tiles_n;
+  float alpha, beta;
+  float* c;
+  long long ldc;
+  unsigned long long timeout_ns;
+};
+
+// Fragment loads for one group of 4 consecutive k (g = 0..7 inside a 32-wide stage).
+// frag[kk][i] = op(X)(row_i, 4g + kk).
+template <bool KMAJOR>
+__device__ __forceinline__ void load_frag(const float* tile, int g, int t, float (&frag)[4][8]) {
+  if constexpr (KMAJOR) {
+    // [128 rows][32 k], 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r & 7).
+    const int chunk = (g ^ (t & 7)) * 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(tile + (t + 16 * i) * kBK + chunk);
+      frag[0][i] = v.x;
+      frag[1][i] = v.y;
+      frag[2][i] = v.z;
+      frag[3][i] = v.w;
+    }
+  } else {
+    // [32 k][128 rows], unswizzled.
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float* row = tile + (4 * g + kk) * kBM;
+      const float4 lo = *reinterpret_cast<const float4*>(row + 4 * t);
+      const float4 hi = *reinterpret_cast<const float4*>(row + 64 + 4 * t);
+      frag[kk][0] = lo.x;
+      frag[kk][1] = lo.y;
+      frag[kk][2] = lo.z;
+      frag[kk][3] = lo.w;
+      frag[kk][4] = hi.x;
+      frag[kk][5] = hi.y;
+      frag[kk][6] = hi.z;
+      frag[kk][7] = hi.w;
+    }
+  }
+}
+
+// Tile-local row (or column) of a thread's i-th fragment entry.
+template <bool KMAJOR> __device__ __forceinline__ int frag_index(int t, int i) {
+  if constexpr (KMAJOR)
+    return t + 16 * i;
+  else
+    return (i < 4) ? 4 * t + i : 64 + 4 * t + (i - 4);
+}
+
+template <bool A_KMAJOR, bool B_KMAJOR>
+__global__ void __launch_bounds__(kThreads, 1)
+    sgemm_ffma_tma(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, const FfmaParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  // The 128-byte swizzle pattern repeats every 1024 bytes and is computed from the
+  // absolute shared address, so stage buffers start on a 1024-byte boundary.
+  float* smem = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* smem_a = smem;
+  float* smem_b = smem + kStages * kStageFloats;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * kStageFloats);
+  uint64_t* empty = full + kStages;
+
+  // Grouped rasterisation: 8 consecutive M tiles sweep the N tiles together so the
+  // B stage tiles they share stay in L2.
+  const int bid = blockIdx.x;
+  const int group_span = 8 * p.tiles_n;
+  const int first_m = (bid / group_span) * 8;
+  const int group_m = min(8, p.tiles_m - first_m);
+  const int tile_m = first_m + (bid % group_span) % group_m;
+  const int tile_n = (bid % group_span) / group_m;
+  const int m0 = tile_m * kBM;
+  const int n0 = tile_n * kBN;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerThreads / 32);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerThreads / 32) {
+    // ---------------------------------------------------------------- producer
+    if (lane_id() != 0)
+      return;
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+    int issued = 0;
+    for (int kt = 0; kt < p.k_tiles; ++kt) {
+      const int s = kt % kStages;
+      const int fill = kt / kStages;
+      if (fill > 0 && !mbar_wait_bounded(&empty[s], (fill - 1) & 1, p.timeout_ns)) {
+        atomicOr(&xvram_kernel_error, 2u);
+        break;
+      }
+      mbar_arrive_expect_tx(&full[s], kStageBytes);
+      const int k0 = kt * kBK;
+      if constexpr (A_KMAJOR)
+        tma_load_2d(smem_a + s * kStageFloats, &tmap_a, &full[s], k0, m0);
+      else
+        tma_load_2d(smem_a + s * kStageFloats, &tmap_a, &full[s], m0, k0);
+      if constexpr (B_KMAJOR)
+        tma_load_2d(smem_b + s * kStageFloats, &tmap_b, &full[s], k0, n0);
+      else
+        tma_load_2d(smem_b + s * kStageFloats, &tmap_b, &full[s], n0, k0);
+      ++issued;
+    }
+    // Do not leave the CTA with copies still landing in its shared memory: wait for
+    // the last fill of every stage that was armed (already complete on the normal path).
+    for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt) {
+      if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
+        atomicOr(&xvram_kernel_error, 4u);
+        break;
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const int tm = tid & 15;
+  const int tn = tid >> 4;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[i][j] = 0.0f;
+
+  for (int kt = 0; kt < p.k_tiles; ++kt) {
+    const int s = kt % kStages;
+    if (!mbar_wait_bounded(&full[s], (kt / kStages) & 1, p.timeout_ns)) {
+      atomicOr(&xvram_kernel_error, 1u);
+      return;
+    }
+    const float* as = smem_a + s * kStageFloats;
+    const float* bs = smem_b + s * kStageFloats;
+#pragma unroll
+    for (int g = 0; g < kBK / 4; ++g) {
+      float a[4][8], b[4][8];
+      load_frag<A_KMAJOR>(as, g, tm, a);
+      load_frag<B_KMAJOR>(bs, g, tn, b);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            acc[i][j] = fmaf(a[kk][i], b[kk][j], acc[i][j]);
+    }
+    __syncwarp();
+    if ((tid & 31) == 0)
+      mbar_arrive(&empty[s]);
+  }
+
+  // ------------------------------------------------------------------- epilogue
+  const float alpha = p.alpha, beta = p.beta;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
+    if (col >= p.n)
+      continue;
+    float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+      if (row < p.m) {
+        const float v = alpha * acc[i][j];
+        cc[row] = (beta == 0.0f) ? v : fmaf(beta, cc[row], v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Generic kernel: any alignment and leading dimension.  64x64 C tile, 256 threads,
+// 4x4 per thread, k in steps of 16 through plain shared memory.
+__global__ void __launch_bounds__(256)
+    sgemm_ffma_generic(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                       long long lda, const float* b, long long ldb, float beta, float* c,
+                       long long ldc) {
+  __shared__ float as[16][64 + 4];
+  __shared__ float bs[16][64 + 4];
+  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < k; k0 += 16) {
+    for (int e = tid; e < 16 * 64; e += 256) {
+      const int kk = e >> 6, r = e & 63;
+      const int gi = m0 + r, gk = k0 + kk;
+      float av = 0.0f;
+      if (gi < m && gk < k)
+        av = op_a == 0 ? a[gi + gk * lda] : a[gk + gi * lda];
+      as[kk][r] = av;
+      const int gj = n0 + r;
+      float bv = 0.0f;
+      if (gj < n && gk < k)
+        bv = op_b == 0 ? b[gk + gj * ldb] : b[gj + gk * ldb];
+      bs[kk][r] = bv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float ar[4], br[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        ar[i] = as[kk][tx + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        br[j] = bs[kk][ty + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = n0 + ty + 16 * j;
+    if (col >= n)
+      continue;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = m0 + tx + 16 * i;
+      if (row < m) {
+        float* cp = c + row + static_cast<long long>(col) * ldc;
+        const float v = alpha * acc[i][j];
+        *cp = (beta == 0.0f) ? v : fmaf(beta, *cp, v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2D FP32 tensor map over a column-major matrix stored as `inner` x `outer` with
+// leading dimension `ld` (elements), box = box_inner x box_outer.
+bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint64_t ld,
+               uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  auto encode = tensor_map_encoder();
+  if (!encode)
+    return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld * sizeof(float)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r =
+      encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool AK, bool BK> cudaError_t configure_once() {
+  static cudaError_t status = cudaFuncSetAttribute(
+      sgemm_ffma_tma<AK, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  return status;
+}
+
+template <bool AK, bool BK>
+cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, const FfmaParams& p,
+                       cudaStream_t stream) {
+  if (cudaError_t e = configure_once<AK, BK>(); e != cudaSuccess)
+    return e;
+  const unsigned grid = static_cast<unsigned>(p.tiles_m) * static_cast<unsigned>(p.tiles_n);
+  sgemm_ffma_tma<AK, BK><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+} // namespace
+
+bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
+                        long long ldb) {
+  (void)op_a;
+  (void)op_b;
+  const auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0 && lda > 0 && ldb > 0 &&
+         lda < (1ll << 37) && ldb < (1ll << 37) && tensor_map_encoder() != nullptr;
+}
+
+cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                       long long lda, const float* b, long long ldb, float beta, float* c,
+                       long long ldc, cudaStream_t stream, SgemmPath path) {
+  if (m <= 0 || n <= 0)
+    return cudaSuccess;
+  if (k <= 0) {
+    // C = beta * C: the generic kernel with k = 0 runs the epilogue only.
+    path = SgemmPath::generic;
+  }
+  const bool tma_ok = k > 0 && sgemm_tma_eligible(op_a, op_b, a, lda, b, ldb);
+  if (path == SgemmPath::tma && !tma_ok)
+    return cudaErrorInvalidValue;
+  if (path == SgemmPath::automatic)
+    path = tma_ok ? SgemmPath::tma : SgemmPath::generic;
+
+  if (path == SgemmPath::generic) {
+    dim3 grid((m + 63) / 64, (n + 63) / 64);
+    if (grid.y > 65535)
+      return cudaErrorInvalidConfiguration;
+    sgemm_ffma_generic<<<grid, 256, 0, stream>>>(op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta,
+                                                 c, ldc);
+    return cudaGetLastError();
+  }
+
+  const bool a_kmajor = op_a != 0;
+  const bool b_kmajor = op_b == 0;
+  CUtensorMap ta, tb;
+  bool ok = a_kmajor ? encode_2d(&ta, a, k, m, lda, kBK, kBM, true)
+                     : encode_2d(&ta, a, m, k, lda, kBM, kBK, false);
+  ok = ok && (b_kmajor ? encode_2d(&tb, b, k, n, ldb, kBK, kBN, true)
+                       : encode_2d(&tb, b, n, k, ldb, kBN, kBK, false));
+  if (!ok)
+    return cudaErrorInvalidValue;
+  FfmaParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.k_tiles = (k + kBK - 1) / kBK;
+  p.tiles_m = (m + kBM - 1) / kBM;
+  p.tiles_n = (n + kBN - 1) / kBN;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.c = c;
+  p.ldc = ldc;
+  p.timeout_ns = kernel_wait_limit_ns();
+  if (static_cast<long long>(p.tiles_m) * p.tiles_n > 0x7fffffffll)
+    return cudaErrorInvalidConfiguration;
+  if (a_kmajor && b_kmajor)
+    return launch_tma<true, true>(ta, tb, p, stream);
+  if (a_kmajor)
+    return launch_tma<true, false>(ta, tb, p, stream);
+  if (b_kmajor)
+    return launch_tma<false, true>(ta, tb, p, stream);
+  return launch_tma<false, false>(ta, tb, p, stream);
+}
+
+cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream) {
+  unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, xvram_kernel_error, sizeof(unsigned int), 0,
+                                            cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess)
+    return e;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess || *out == 0)
+    return e;
+  e = cudaMemcpyToSymbolAsync(xvram_kernel_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice,
+                              stream);
+  if (e != cudaSuccess)
+    return e;
+  return cudaStreamSynchronize(stream);
+}
+
+unsigned long long kernel_wait_limit_ns() {
+  // One second of wall clock for any single mbarrier wait; a stage tile lands in
+  // microseconds, so only a broken pipeline ever reaches it.
+  return 1000ull * 1000ull * 1000ull;
+}
+
+} // namespace xvram

@@ -1,0 +1,92 @@
+"""Native entry points of include/xvram_b200.h for Python callers.
+
+Column-major convention: an ``rows x cols`` column-major matrix with leading
+dimension ``ld`` is held in a torch tensor of shape ``(cols, ld)`` (row j of the
+tensor is column j of the matrix).  ``colmajor(t)`` / ``from_colmajor`` convert.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+from ._native import PlanInfo, lib
+
+u32, u64 = C.c_uint32, C.c_uint64
+
+PATH_AUTO, PATH_TMA, PATH_GENERIC = 0, 1, 2
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+def sgemm(op_a: int, op_b: int, m: int, n: int, k: int, alpha: float, a, lda: int, b, ldb: int,
+          beta: float, c, ldc: int, stream=None, path: int = PATH_AUTO) -> int:
+    """C = alpha op(A) op(B) + beta C on CUDA tensors (or raw device pointers); returns
+    the xvram_status.  Enqueued on `stream` (default: torch's current stream)."""
+    ptr = lambda x: x if isinstance(x, int) else x.data_ptr()
+    return lib.xvram_b200_sgemm_device(op_a, op_b, m, n, k, alpha, ptr(a), lda, ptr(b), ldb, beta,
+                                       ptr(c), ldc, _stream_handle(stream), path)
+
+
+def kernel_status(stream=None) -> int:
+    """Synchronises the stream and returns (and clears) the kernel error word."""
+    w = u32(0)
+    st = lib.xvram_b200_kernel_status(_stream_handle(stream), C.byref(w))
+    if st != 0:
+        raise RuntimeError(f"xvram_b200_kernel_status failed with status {st}")
+    return w.value
+
+
+def fill_uniform(t, seed: int, first_index: int = 0, threads: int = 0) -> None:
+    """Fills a contiguous float32 CPU tensor (or numpy array) with the seeded stream."""
+    if hasattr(t, "data_ptr"):
+        assert t.is_contiguous() and t.dtype.itemsize == 4 and not t.is_cuda
+        ptr, count = t.data_ptr(), t.numel()
+    else:
+        assert t.flags["C_CONTIGUOUS"] and t.dtype.itemsize == 4
+        ptr, count = t.ctypes.data, t.size
+    lib.xvram_b200_fill_uniform(ptr, count, seed, first_index, threads)
+
+
+def plan_panels(op_a: int, op_b: int, m: int, n: int, k: int, beta_nonzero: bool, budget: int,
+                quantum: int, flops_per_s: float = 0.0, h2d: float = 0.0, d2h: float = 0.0,
+                force=(0, 0, 0)) -> dict:
+    info = PlanInfo()
+    info.struct_size = C.sizeof(PlanInfo)
+    st = lib.xvram_b200_plan_panels(op_a, op_b, m, n, k, int(beta_nonzero), budget, quantum,
+                                    flops_per_s, h2d, d2h, force[0], force[1], force[2],
+                                    C.byref(info))
+    out = {name: getattr(info, name) for name, _ in PlanInfo._fields_}
+    out["return_status"] = st
+    return out
+
+
+def plan_steps(op_a: int, op_b: int, m: int, n: int, k: int, beta_nonzero: bool, budget: int,
+               quantum: int, force=(0, 0, 0), capacity: Optional[int] = None):
+    """Step list of the plan as a list of (bm, bn, bk, slot_a, slot_b)."""
+    info = plan_panels(op_a, op_b, m, n, k, beta_nonzero, budget, quantum, force=force)
+    if info["return_status"] != 0:
+        return info["return_status"], []
+    cap = info["steps"] if capacity is None else capacity
+    buf = (C.c_int32 * (5 * max(cap, 1)))()
+    st = lib.xvram_b200_plan_steps(op_a, op_b, m, n, k, int(beta_nonzero), budget, quantum,
+                                   force[0], force[1], force[2], buf, cap)
+    if st != 0:
+        return st, []
+    return 0, [tuple(buf[5 * i:5 * i + 5]) for i in range(cap)]
+
+
+def validate(m, n, k, op_a, op_b, ids, nbytes, offsets, rows, cols, lds) -> tuple[int, str]:
+    arr = lambda xs: (u64 * 3)(*xs)
+    op = C.create_string_buffer(1)
+    err = lib.xvram_b200_validate_gemm(m, n, k, op_a, op_b, arr(ids), arr(nbytes), arr(offsets),
+                                       arr(rows), arr(cols), arr(lds), op)
+    return err, (op.value.decode() if op.value else "")
+
+
+def ffma_probe(blocks: int, iterations: int, sink, stream=None) -> int:
+    return lib.xvram_b200_ffma_probe(blocks, iterations, sink.data_ptr(), _stream_handle(stream))
