@@ -329,7 +329,8 @@ def main_gpu(args) -> None:
     e2e_s_max = max_over_ranks(e2e_s)
     tel = api.telemetry()
     info = cp.runtime_info()
-    launches_e2e = int(info.gemm_in_place)  # one kernel per in-place GEMM
+    # one SGEMM kernel plus the two canonicalising transposes per in-place GEMM
+    launches_e2e = int(info.gemm_in_place) * (1 + int(OP_A == 1) + int(OP_B == 0))
     for d in (da, db, dc):
         api.free(d)
     api.blas_destroy(h)
@@ -379,7 +380,8 @@ def main_gpu(args) -> None:
                     "gemm_in_place": int(info.gemm_in_place),
                     "gemm_streamed": int(info.gemm_streamed),
                     "runtime_h2d_bytes": int(tel.runtime.bytes_h2d)},
-            "gpu_launches": args.steps,
+            # per step: the SGEMM kernel plus one transpose per K-major operand (TN: 2)
+            "gpu_launches": args.steps * (1 + int(OP_A == 1) + int(OP_B == 0)),
             "gpu_launches_e2e": launches_e2e,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

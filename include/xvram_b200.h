@@ -36,13 +36,33 @@ enum {
  * C = alpha * op(A) * op(B) + beta * C on device-resident column-major FP32 matrices,
  * enqueued on `stream` and not synchronised.  op 0 = N, 1 = T.  m, n, k >= 0 (k == 0
  * scales C by beta); beta == 0 does not read C.  Strict FP32: every multiply-add is an
- * FFMA.  Stands in for the per-tile library call of the reference's executor
+ * FFMA.  K-major operands are transposed into stream-ordered scratch taken from a private
+ * per-device memory pool (see xvram_b200_sgemm_device_ws to supply the scratch instead).  Stands in for the per-tile library call of the reference's executor
  * (src/gemm/executor.cpp:147-329 -> cublasLtMatmul, src/platform/cublas/cublas_api.cpp:751-918).
  */
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
     uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
     int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, uint64_t stream,
     uint32_t path);
+
+/* Bytes of device workspace the K-major operand canonicalisation needs for this problem:
+ * transposed copies of op(A) when op_a = T and of op(B) when op_b = N (0 for op_a = N,
+ * op_b = T).  No reference counterpart. */
+XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_a, uint32_t op_b,
+                                                                    int64_t m, int64_t n,
+                                                                    int64_t k);
+
+/*
+ * xvram_b200_sgemm_device with caller-provided device workspace (256-byte aligned).  With
+ * at least xvram_b200_sgemm_workspace_bytes, K-major operands are transposed into it and
+ * the faster M-major/N-major kernel runs; with less, the call behaves exactly like
+ * xvram_b200_sgemm_device without allocating.  Results are bit-identical either way.
+ * Calls that share one workspace must be ordered on the device (same stream or events).
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
+    int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, void* workspace,
+    uint64_t workspace_bytes, uint64_t stream, uint32_t path);
 
 /* Synchronises `stream`, then returns and clears the device's sticky kernel error word
  * (nonzero: a pipeline wait inside a kernel ran out of time and the kernel returned

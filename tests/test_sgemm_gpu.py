@@ -186,3 +186,41 @@ def test_ffma_probe_runs():
     sink = torch.zeros(1, device="cuda")
     assert device.ffma_probe(148, 8, sink) == 0
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("op_a,op_b", [(1, 0), (0, 0), (1, 1)])
+def test_canonicalised_path_is_bit_identical(oracle, op_a, op_b):
+    """K-major operands transposed into scratch + the M/N-major kernel give exactly the
+    bits of the direct K-major kernel (same FFMA order per output)."""
+    m, n, k = 700, 520, 300
+    a, lda, b, ldb, c, ldc = operands(oracle, op_a, op_b, m, n, k, (0, 0, 0), 50)
+    lda_p = lda + (-lda) % 4
+    ldb_p = ldb + (-ldb) % 4
+    ap = np.zeros((a.shape[0], lda_p), np.float32); ap[:, :lda] = a
+    bp = np.zeros((b.shape[0], ldb_p), np.float32); bp[:, :ldb] = b
+    A, B = torch.from_numpy(ap).cuda(), torch.from_numpy(bp).cuda()
+    need = device.workspace_bytes(op_a, op_b, m, n, k)
+    assert need > 0
+    ws = torch.empty(need // 4 + 64, device="cuda")
+    outs = []
+    for mode in ("pool", "explicit", "direct"):
+        Cd = torch.from_numpy(c).cuda()
+        if mode == "pool":
+            st = device.sgemm(op_a, op_b, m, n, k, 0.5, A, lda_p, B, ldb_p, 1.5, Cd, ldc)
+        elif mode == "explicit":
+            st = device.sgemm_ws(op_a, op_b, m, n, k, 0.5, A, lda_p, B, ldb_p, 1.5, Cd, ldc, ws,
+                                 need)
+        else:  # too little workspace: the K-major kernel runs directly
+            st = device.sgemm_ws(op_a, op_b, m, n, k, 0.5, A, lda_p, B, ldb_p, 1.5, Cd, ldc, ws, 0)
+        assert st == 0
+        assert device.kernel_status() == 0
+        outs.append(Cd.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+    ref = oracle.gemm(op_a, op_b, m, n, k, 0.5, ap, lda_p, bp, ldb_p, 1.5, c, ldc)
+    check(outs[0], ref, c, m, k, a, b)
+
+
+def test_workspace_query():
+    assert device.workspace_bytes(0, 1, 100, 100, 100) == 0
+    assert device.workspace_bytes(1, 1, 100, 100, 100) == 100 * 100 * 4 + (256 - 100 * 100 * 4 % 256) % 256
+    assert device.workspace_bytes(1, 0, 101, 99, 7) >= (104 * 7 + 100 * 7) * 4

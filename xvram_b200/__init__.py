@@ -7,10 +7,11 @@ only binds it for Python callers, tests and the benchmark:
 * ``xvram_b200.compat``  -- the cudaMalloc/cudaMemcpy/cublasSgemm-style table;
 * ``xvram_b200.device``  -- the tile contraction on torch device tensors, the
   synthetic input generator, planner inspection and the FP32 peak probe.
+
+Importing either submodule loads the library and raises ImportError when it has not
+been built (``python -m xvram_b200.build``); there is no fallback implementation.
 """
 from __future__ import annotations
-
-from . import _native  # noqa: F401  (raises ImportError when the library is not built)
 
 __all__ = ["compat", "device"]
 __version__ = "0.1.0"

@@ -68,10 +68,13 @@ public:
                         uint64_t width, uint64_t height, CopyDir dir, StreamId s) = 0;
   virtual Error memset_d32(uint64_t dst, uint32_t value, uint64_t count, StreamId s) = 0;
 
-  // C = alpha * op(A) op(B) + beta * C on device addresses (column-major FP32).
+  // C = alpha * op(A) op(B) + beta * C on device addresses (column-major FP32).  With
+  // `workspace_bytes` >= sgemm_workspace_bytes K-major operands are canonicalised there.
   virtual Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha,
                       uint64_t a, int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c,
-                      int64_t ldc, StreamId s) = 0;
+                      int64_t ldc, uint64_t workspace, uint64_t workspace_bytes, StreamId s) = 0;
+  // Workspace the canonicalising path needs for this problem (0 if none).
+  virtual uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k) = 0;
   // Reads and clears the sticky error word of the library's kernels (synchronising s).
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
 };

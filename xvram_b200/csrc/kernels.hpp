@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
 namespace xvram {
 
 enum class SgemmPath { automatic = 0, tma = 1, generic = 2 };
@@ -13,6 +15,19 @@ enum class SgemmPath { automatic = 0, tma = 1, generic = 2 };
 cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
                        long long lda, const float* b, long long ldb, float beta, float* c,
                        long long ldc, cudaStream_t stream, SgemmPath path = SgemmPath::automatic);
+
+// Workspace that sgemm_ffma_ws uses to canonicalise K-major operands (0 when op(A) = N
+// and op(B) = T, which the kernel already reads in its fastest form).
+uint64_t sgemm_workspace_bytes(int op_a, int op_b, int m, int n, int k);
+
+// sgemm_ffma with a workspace: when the workspace is at least sgemm_workspace_bytes and
+// 256-byte aligned, K-major operands are transposed into it first and the M-major /
+// N-major kernel runs; otherwise identical to sgemm_ffma.  Same result either way
+// (the transposes move values, they do not round).
+cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                          long long lda, const float* b, long long ldb, float beta, float* c,
+                          long long ldc, void* workspace, uint64_t workspace_bytes,
+                          cudaStream_t stream, SgemmPath path = SgemmPath::automatic);
 
 bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
                         long long ldb);

@@ -8,6 +8,8 @@
 
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 namespace xvram {
 xvram_status compat_runtime_info(xvram_b200_runtime_info_v1* out);
 }
@@ -33,6 +35,48 @@ xvram_status from_cuda(cudaError_t e) {
   default:
     return XVRAM_STATUS_CUDA_ERROR;
   }
+}
+
+// Private stream-ordered pool per device for the scratch of xvram_b200_sgemm_device.
+// Its release threshold is unlimited so steady-state calls reuse pooled memory.
+cudaMemPool_t scratch_pool(int device) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 64)
+    return nullptr;
+  if (!pools[device]) {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    uint64_t threshold = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    pools[device] = pool;
+  }
+  return pools[device];
+}
+
+bool valid_args(uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, const float* a,
+                int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, uint32_t path) {
+  if (op_a > 1 || op_b > 1 || m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
+      k > INT32_MAX || path > XVRAM_B200_PATH_GENERIC)
+    return false;
+  if (m == 0 || n == 0)
+    return true;
+  return c && ldc >= m &&
+         (k == 0 || (a && b && lda >= (op_a == 0 ? m : k) && ldb >= (op_b == 0 ? k : n)));
+}
+
+SgemmPath to_path(uint32_t path) {
+  return path == XVRAM_B200_PATH_TMA       ? SgemmPath::tma
+         : path == XVRAM_B200_PATH_GENERIC ? SgemmPath::generic
+                                           : SgemmPath::automatic;
 }
 
 PlanStatus plan_for(uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k,
@@ -68,20 +112,52 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
     uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
     int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, uint64_t stream,
     uint32_t path) {
-  if (op_a > 1 || op_b > 1 || m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
-      k > INT32_MAX || path > XVRAM_B200_PATH_GENERIC)
+  if (!valid_args(op_a, op_b, m, n, k, a, lda, b, ldb, c, ldc, path))
     return XVRAM_STATUS_INVALID_ARGUMENT;
   if (m == 0 || n == 0)
     return XVRAM_STATUS_SUCCESS;
-  if (!c || ldc < m || (k > 0 && (!a || !b || lda < (op_a == 0 ? m : k) ||
-                                  ldb < (op_b == 0 ? k : n))))
+  const int oa = static_cast<int>(op_a), ob = static_cast<int>(op_b);
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  const uint64_t need = sgemm_workspace_bytes(oa, ob, mi, ni, ki);
+  cudaStream_t s = as_stream(stream);
+  if (need && path != XVRAM_B200_PATH_GENERIC && sgemm_tma_eligible(oa, ob, a, lda, b, ldb)) {
+    int dev = 0;
+    cudaMemPool_t pool = cudaGetDevice(&dev) == cudaSuccess ? scratch_pool(dev) : nullptr;
+    void* ws = nullptr;
+    if (pool && cudaMallocFromPoolAsync(&ws, need, pool, s) == cudaSuccess) {
+      const cudaError_t e = sgemm_ffma_ws(oa, ob, mi, ni, ki, alpha, a, lda, b, ldb, beta, c, ldc,
+                                          ws, need, s, to_path(path));
+      const cudaError_t f = cudaFreeAsync(ws, s);
+      return from_cuda(e != cudaSuccess ? e : f);
+    }
+    cudaGetLastError(); // no scratch: run the K-major kernel directly
+  }
+  return from_cuda(sgemm_ffma(oa, ob, mi, ni, ki, alpha, a, lda, b, ldb, beta, c, ldc, s,
+                              to_path(path)));
+}
+
+XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_a, uint32_t op_b,
+                                                                    int64_t m, int64_t n,
+                                                                    int64_t k) {
+  if (op_a > 1 || op_b > 1 || m <= 0 || n <= 0 || k <= 0 || m > INT32_MAX || n > INT32_MAX ||
+      k > INT32_MAX)
+    return 0;
+  return sgemm_workspace_bytes(static_cast<int>(op_a), static_cast<int>(op_b),
+                               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
+    int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, void* workspace,
+    uint64_t workspace_bytes, uint64_t stream, uint32_t path) {
+  if (!valid_args(op_a, op_b, m, n, k, a, lda, b, ldb, c, ldc, path))
     return XVRAM_STATUS_INVALID_ARGUMENT;
-  const SgemmPath p = path == XVRAM_B200_PATH_TMA       ? SgemmPath::tma
-                      : path == XVRAM_B200_PATH_GENERIC ? SgemmPath::generic
-                                                        : SgemmPath::automatic;
-  return from_cuda(sgemm_ffma(static_cast<int>(op_a), static_cast<int>(op_b), static_cast<int>(m),
-                              static_cast<int>(n), static_cast<int>(k), alpha, a, lda, b, ldb,
-                              beta, c, ldc, as_stream(stream), p));
+  if (m == 0 || n == 0)
+    return XVRAM_STATUS_SUCCESS;
+  return from_cuda(sgemm_ffma_ws(static_cast<int>(op_a), static_cast<int>(op_b),
+                                 static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                                 alpha, a, lda, b, ldb, beta, c, ldc, workspace, workspace_bytes,
+                                 as_stream(stream), to_path(path)));
 }
 
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_kernel_status(uint64_t stream, uint32_t* word) {

@@ -68,7 +68,17 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
   pl.c_slot_bytes = round_up(static_cast<uint64_t>(g.mb) * g.nb * 4u, q);
   const int64_t blocks = pl.blocks_m * pl.blocks_n;
   pl.c_slots = blocks > 1 ? 2 : 1;
-  const uint64_t c_total = pl.c_slot_bytes * static_cast<uint64_t>(pl.c_slots);
+  {
+    const auto up = [](uint64_t v, uint64_t m) { return (v + m - 1) / m * m; };
+    uint64_t ws = 0;
+    if (lim.transpose_a)
+      ws += up(up(static_cast<uint64_t>(g.mb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
+    if (lim.transpose_b)
+      ws += up(up(static_cast<uint64_t>(g.nb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
+    pl.workspace_bytes = round_up(ws, q);
+  }
+  const uint64_t c_total =
+      pl.c_slot_bytes * static_cast<uint64_t>(pl.c_slots) + pl.workspace_bytes;
   if (c_total >= lim.budget_bytes)
     return false;
   const int64_t distinct = (pl.blocks_m + pl.blocks_n) * pl.panels_k;

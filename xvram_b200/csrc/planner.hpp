@@ -37,6 +37,9 @@ struct PlanLimits {
   double h2d_bytes_per_s = 50e9;
   double d2h_bytes_per_s = 50e9;
   int64_t force_mb = 0, force_nb = 0, force_kb = 0; // 0 = search (tests pin geometry)
+  // Per-step device workspace for canonicalising K-major panels: the kernel transposes
+  // op(A) panels when transpose_a and op(B) panels when transpose_b.
+  bool transpose_a = false, transpose_b = false;
   int force_order = -1;                             // -1 search, 0 m-outer, 1 n-outer
 };
 
@@ -64,6 +67,7 @@ struct Plan {
   int64_t blocks_m = 0, blocks_n = 0, panels_k = 0;
   uint64_t slot_bytes = 0;   // panel slot size (multiple of quantum)
   uint64_t c_slot_bytes = 0; // C block slot size (multiple of quantum)
+  uint64_t workspace_bytes = 0; // per-step canonicalisation workspace (multiple of quantum)
   int32_t panel_slots = 0;
   int32_t c_slots = 0;
   std::vector<PlanStep> steps;

@@ -13,6 +13,9 @@ namespace xvram {
 namespace {
 
 constexpr uint64_t kArenaOwner = UINT64_MAX;
+// Internal allocation that holds the kernels' canonicalisation workspace for in-place
+// GEMMs.  Its chunks are never "written", so evicting them is free (no write-back).
+constexpr uint64_t kScratchId = UINT64_MAX - 1;
 
 struct Chunk {
   int32_t frame = -1;         // frame index while resident
@@ -247,7 +250,7 @@ struct Runtime::Impl {
   }
 
   Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
-                      const std::set<std::pair<uint64_t, uint32_t>>& keep);
+                      const std::set<std::pair<uint64_t, uint32_t>>& keep, uint64_t ws);
   Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
 };
 
@@ -303,6 +306,16 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
     return e;
   if (Error e = m.dev->event_create(&m.e_b))
     return e;
+  {
+    Alloc scratch;
+    scratch.id = kScratchId;
+    scratch.bytes = m.capacity * m.cb;
+    scratch.reserved = scratch.bytes;
+    if (Error e = m.dev->va_reserve(scratch.reserved, &scratch.va))
+      return e;
+    scratch.chunks.resize(static_cast<size_t>(m.capacity));
+    m.allocs.emplace(kScratchId, std::move(scratch));
+  }
   m.opened = true;
   return {};
 }
@@ -551,8 +564,16 @@ Error Runtime::gemm(const GemmCall& call) {
     for (uint64_t c = b / m.cb; c <= (e - 1) / m.cb; ++c)
       keep.insert({owners[i]->id, static_cast<uint32_t>(c)});
   }
-  Error err = keep.size() <= m.capacity ? m.gemm_in_place(call, A, B, C, keep)
-                                        : m.gemm_streamed(call, A, B, C);
+  // The kernel's canonicalisation workspace comes out of the same frame budget.
+  const GemmShape& sh = call.shape;
+  const uint64_t ws = m.dev->sgemm_workspace(sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
+                                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k));
+  const uint64_t ws_chunks = (ws + m.cb - 1) / m.cb;
+  const size_t data_chunks = keep.size();
+  for (uint64_t c = 0; c < ws_chunks && c < m.capacity; ++c)
+    keep.insert({kScratchId, static_cast<uint32_t>(c)});
+  Error err = data_chunks + ws_chunks <= m.capacity ? m.gemm_in_place(call, A, B, C, keep, ws)
+                                                    : m.gemm_streamed(call, A, B, C);
   m.x.last_gemm_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   m.t.last_transaction_ms = m.x.last_gemm_ms;
@@ -562,7 +583,8 @@ Error Runtime::gemm(const GemmCall& call) {
 }
 
 Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
-                                   const std::set<std::pair<uint64_t, uint32_t>>& keep) {
+                                   const std::set<std::pair<uint64_t, uint32_t>>& keep,
+                                   uint64_t ws) {
   bool uploaded = false;
   for (const auto& [id, c] : keep)
     if (Error e = make_resident(allocs.at(id), c, true, keep, &uploaded))
@@ -580,7 +602,8 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
                            static_cast<int64_t>(s.k), call.alpha, A.va + s.a.offset_bytes,
                            static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
                            static_cast<int64_t>(s.b.ld), call.beta, C.va + s.c.offset_bytes,
-                           static_cast<int64_t>(s.c.ld), s_compute))
+                           static_cast<int64_t>(s.c.ld), ws ? allocs.at(kScratchId).va : 0, ws,
+                           s_compute))
     return e;
   for (const auto& [id, c] : keep) {
     Frame& f = frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)];
@@ -631,6 +654,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
   lim.flops_per_s = cfg.flops_per_s;
   lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
   lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
+  lim.transpose_a = s.op_a != 0;
+  lim.transpose_b = s.op_b == 0;
   Plan plan;
   const PlanStatus ps = make_panel_plan(pp, lim, &plan);
   if (ps != PlanStatus::ok)
@@ -648,7 +673,7 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
   const uint64_t fps = plan.slot_bytes / cb;
   const uint64_t fpc = plan.c_slot_bytes / cb;
   const uint64_t nframes = fps * static_cast<uint64_t>(plan.panel_slots) +
-                           fpc * static_cast<uint64_t>(plan.c_slots);
+                           fpc * static_cast<uint64_t>(plan.c_slots) + plan.workspace_bytes / cb;
   while (frames.size() < nframes) {
     Frame f;
     if (Error e = dev->handle_create(cb, &f.handle))
@@ -680,6 +705,7 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
   }
   update_resident();
   const uint64_t c_base = arena + fps * cb * static_cast<uint64_t>(plan.panel_slots);
+  const uint64_t ws_base = c_base + fpc * cb * static_cast<uint64_t>(plan.c_slots);
 
   std::vector<EventId> ready(static_cast<size_t>(plan.panel_slots)),
       used(static_cast<size_t>(plan.panel_slots)), c_ready(static_cast<size_t>(plan.c_slots)),
@@ -787,7 +813,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     const int64_t lda_s = s.op_a == 0 ? mb : kb;
     const int64_t ldb_s = s.op_b == 0 ? kb : nb;
     if ((err = dev->sgemm(s.op_a, s.op_b, mr, nr, kr, call.alpha, slot_va(st.slot_a), lda_s,
-                          slot_va(st.slot_b), ldb_s, beta_eff, cva, mb, s_compute)))
+                          slot_va(st.slot_b), ldb_s, beta_eff, cva, mb,
+                          plan.workspace_bytes ? ws_base : 0, plan.workspace_bytes, s_compute)))
       break;
     ++x.tiles_submitted;
     for (int32_t sl : {st.slot_a, st.slot_b}) {

@@ -7,12 +7,20 @@
 // (reference src/gemm/executor.cpp:147-329, src/platform/cublas/cublas_api.cpp:751-918).
 // Every product and sum is an FP32 FFMA; there is no TF32 or reduced-precision step.
 //
-// Main kernel (sgemm_ffma_tma): 128x128 C tile per CTA, K in stages of 32.
-//   * warp 8 (producer): one lane issues 2D TMA loads of the op(A) and op(B) stage
-//     tiles into a 4-deep shared-memory ring, completion on a per-stage "full" mbarrier;
-//   * warps 0-7 (consumers, 256 threads): each thread owns an 8x8 block of C in
-//     registers and runs 64 FFMA per k; a warp releases the stage on an "empty"
-//     mbarrier when done.
+// Main kernel (sgemm_ffma_tma): 128 x BN C tile per CTA (BN = 256 by default, 128 for
+// narrow N), K in stages of 32.
+//   * 8 warps (256 threads) each own an 8 x (BN/16) block of C per thread in registers;
+//     a warp releases a stage on its "empty" mbarrier when it has consumed it;
+//   * thread 0 also drives the 4-deep ring of 2D TMA loads: it fills every stage up
+//     front and refills a stage with the tile 4 ahead once all eight warps have
+//     released it; completion is signalled on the stage's "full" mbarrier.
+//   There is no separate producer warp: a 9-warp block would put three warps on one
+//   SM sub-partition and cap every thread at 168 registers, too few for 8x16.
+// Why 8x16 per thread: an LDS.128 costs four shared-memory wavefronts whatever the
+// broadcast, so shared-memory bandwidth per FFMA falls only with the register tile.  An
+// 8x8 tile needs one wavefront per SM-clock at full FFMA rate (all of it); 8x16 needs
+// 0.75.  The 16 B values are streamed one column (K-major B) or one k row (N-major B)
+// at a time so the 128 accumulators fit in the register budget.
 // Shared-memory stage layouts follow the stored layout of each operand so that TMA
 // writes them without transposition:
 //   op(A)=N : A stored M-major -> tile [32 k][128 m], no swizzle.  A thread's rows are
@@ -45,15 +53,28 @@ __device__ unsigned int xvram_kernel_error = 0;
 
 namespace {
 
+#ifndef XVRAM_FFMA_STAGES
+#define XVRAM_FFMA_STAGES 4
+#endif
+#ifndef XVRAM_FFMA_GROUP_UNROLL
+#define XVRAM_FFMA_GROUP_UNROLL 8
+#endif
 constexpr int kBM = 128;
-constexpr int kBN = 128;
 constexpr int kBK = 32;
-constexpr int kStages = 4;
-constexpr int kConsumerThreads = 256;
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kStageFloats = kBM * kBK; // A and B tiles are both 128 x 32
-constexpr uint32_t kStageBytes = 2u * kStageFloats * sizeof(float);
-constexpr int kSmemBytes = 2 * kStages * kStageFloats * sizeof(float) + 1024 /*align*/ + 256;
+constexpr int kStages = XVRAM_FFMA_STAGES;
+constexpr int kGroupUnroll = XVRAM_FFMA_GROUP_UNROLL;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kAStageFloats = kBM * kBK;
+
+// Thread tile 8 x TN (TN = 8 or 16): CTA tile 128 x (16 * TN).
+template <int TN> struct TileCfg {
+  static constexpr int BN = 16 * TN;
+  static constexpr int BStageFloats = BN * kBK;
+  static constexpr uint32_t StageBytes = (kAStageFloats + BStageFloats) * sizeof(float);
+  static constexpr int SmemBytes =
+      kStages * (kAStageFloats + BStageFloats) * sizeof(float) + 1024 /*align*/ + 256;
+};
 
 struct FfmaParams {
   int m, n, k;
@@ -99,26 +120,72 @@ __device__ __forceinline__ void load_frag(const float* tile, int g, int t, float
   }
 }
 
-// Tile-local row (or column) of a thread's i-th fragment entry.
+// Tile-local row (or column) of a thread's i-th fragment entry: 16-strided rows for
+// K-major tiles, groups of four consecutive rows every 64 for M/N-major tiles.
 template <bool KMAJOR> __device__ __forceinline__ int frag_index(int t, int i) {
   if constexpr (KMAJOR)
     return t + 16 * i;
   else
-    return (i < 4) ? 4 * t + i : 64 + 4 * t + (i - 4);
+    return 64 * (i >> 2) + 4 * t + (i & 3);
 }
 
-template <bool A_KMAJOR, bool B_KMAJOR>
+// One k-group (4 consecutive k) of the B fragment, streamed: calls body(j, b[0..3]) for
+// a K-major tile (b = 4 k of column j) -- see group_ffma below for the N-major form.
+template <int TN>
+__device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const float* bs, int g,
+                                              int tn, float (&acc)[8][TN]) {
+  const int chunk = (g ^ (tn & 7)) * 4;
+#pragma unroll
+  for (int j = 0; j < TN; ++j) {
+    const float4 v = *reinterpret_cast<const float4*>(bs + (tn + 16 * j) * kBK + chunk);
+    const float b[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        acc[i][j] = fmaf(a[kk][i], b[kk], acc[i][j]);
+  }
+}
+
+// N-major B tile [32 k][BN]: one k row of the thread's TN columns at a time.
+template <int TN>
+__device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const float* bs, int g,
+                                              int tn, float (&acc)[8][TN]) {
+  constexpr int BN = 16 * TN;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const float* row = bs + (4 * g + kk) * BN + 4 * tn;
+    float b[TN];
+#pragma unroll
+    for (int q = 0; q < TN / 4; ++q) {
+      const float4 v = *reinterpret_cast<const float4*>(row + 64 * q);
+      b[4 * q + 0] = v.x;
+      b[4 * q + 1] = v.y;
+      b[4 * q + 2] = v.z;
+      b[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j)
+        acc[i][j] = fmaf(a[kk][i], b[j], acc[i][j]);
+  }
+}
+
+template <bool A_KMAJOR, bool B_KMAJOR, int TN>
 __global__ void __launch_bounds__(kThreads, 1)
     sgemm_ffma_tma(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const FfmaParams p) {
+  using Cfg = TileCfg<TN>;
+  constexpr int BN = Cfg::BN;
   extern __shared__ unsigned char smem_raw[];
   // The 128-byte swizzle pattern repeats every 1024 bytes and is computed from the
   // absolute shared address, so stage buffers start on a 1024-byte boundary.
   float* smem = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* smem_a = smem;
-  float* smem_b = smem + kStages * kStageFloats;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * kStageFloats);
+  float* smem_b = smem + kStages * kAStageFloats;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * Cfg::BStageFloats);
   uint64_t* empty = full + kStages;
 
   // Grouped rasterisation: 8 consecutive M tiles sweep the N tiles together so the
@@ -130,97 +197,101 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_m = first_m + (bid % group_span) % group_m;
   const int tile_n = (bid % group_span) / group_m;
   const int m0 = tile_m * kBM;
-  const int n0 = tile_n * kBN;
+  const int n0 = tile_n * BN;
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerThreads / 32);
+      mbar_init(&empty[s], kWarps);
     }
     fence_mbarrier_init();
   }
   __syncthreads();
 
-  if (warp == kConsumerThreads / 32) {
-    // ---------------------------------------------------------------- producer
-    if (lane_id() != 0)
-      return;
+  // Thread 0 arms stage s for K tile kt: expected bytes, then the two TMA loads.
+  auto issue = [&](int kt) {
+    const int s = kt % kStages;
+    mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+    const int k0 = kt * kBK;
+    float* sa = smem_a + s * kAStageFloats;
+    float* sb = smem_b + s * Cfg::BStageFloats;
+    if constexpr (A_KMAJOR)
+      tma_load_2d(sa, &tmap_a, &full[s], k0, m0);
+    else
+      tma_load_2d(sa, &tmap_a, &full[s], m0, k0);
+    if constexpr (B_KMAJOR)
+      tma_load_2d(sb, &tmap_b, &full[s], k0, n0);
+    else
+      tma_load_2d(sb, &tmap_b, &full[s], n0, k0);
+  };
+  int issued = 0; // meaningful in thread 0 only
+  if (tid == 0) {
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
-    int issued = 0;
-    for (int kt = 0; kt < p.k_tiles; ++kt) {
-      const int s = kt % kStages;
-      const int fill = kt / kStages;
-      if (fill > 0 && !mbar_wait_bounded(&empty[s], (fill - 1) & 1, p.timeout_ns)) {
-        atomicOr(&xvram_kernel_error, 2u);
-        break;
-      }
-      mbar_arrive_expect_tx(&full[s], kStageBytes);
-      const int k0 = kt * kBK;
-      if constexpr (A_KMAJOR)
-        tma_load_2d(smem_a + s * kStageFloats, &tmap_a, &full[s], k0, m0);
-      else
-        tma_load_2d(smem_a + s * kStageFloats, &tmap_a, &full[s], m0, k0);
-      if constexpr (B_KMAJOR)
-        tma_load_2d(smem_b + s * kStageFloats, &tmap_b, &full[s], k0, n0);
-      else
-        tma_load_2d(smem_b + s * kStageFloats, &tmap_b, &full[s], n0, k0);
-      ++issued;
-    }
-    // Do not leave the CTA with copies still landing in its shared memory: wait for
-    // the last fill of every stage that was armed (already complete on the normal path).
-    for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt) {
-      if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
-        atomicOr(&xvram_kernel_error, 4u);
-        break;
-      }
-    }
-    return;
+    for (; issued < kStages && issued < p.k_tiles; ++issued)
+      issue(issued);
   }
 
-  // ------------------------------------------------------------------ consumers
   const int tm = tid & 15;
   const int tn = tid >> 4;
-  float acc[8][8];
+  float acc[8][TN];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < TN; ++j)
       acc[i][j] = 0.0f;
 
+  bool aborted = false;
   for (int kt = 0; kt < p.k_tiles; ++kt) {
     const int s = kt % kStages;
-    if (!mbar_wait_bounded(&full[s], (kt / kStages) & 1, p.timeout_ns)) {
+    const uint32_t phase = (kt / kStages) & 1;
+    if (!mbar_wait_bounded(&full[s], phase, p.timeout_ns)) {
       atomicOr(&xvram_kernel_error, 1u);
-      return;
+      aborted = true;
+      break;
     }
-    const float* as = smem_a + s * kStageFloats;
-    const float* bs = smem_b + s * kStageFloats;
-#pragma unroll
+    const float* as = smem_a + s * kAStageFloats;
+    const float* bs = smem_b + s * Cfg::BStageFloats;
+#pragma unroll kGroupUnroll
     for (int g = 0; g < kBK / 4; ++g) {
-      float a[4][8], b[4][8];
+      float a[4][8];
       load_frag<A_KMAJOR>(as, g, tm, a);
-      load_frag<B_KMAJOR>(bs, g, tn, b);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            acc[i][j] = fmaf(a[kk][i], b[kk][j], acc[i][j]);
+      if constexpr (B_KMAJOR)
+        ffma_group_bk<TN>(a, bs, g, tn, acc);
+      else
+        ffma_group_bn<TN>(a, bs, g, tn, acc);
     }
     __syncwarp();
     if ((tid & 31) == 0)
       mbar_arrive(&empty[s]);
+    // Refill this stage with tile kt + 4 once every warp has released tile kt.
+    if (tid == 0 && issued < p.k_tiles) {
+      if (!mbar_wait_bounded(&empty[s], phase, p.timeout_ns)) {
+        atomicOr(&xvram_kernel_error, 2u);
+        aborted = true;
+        break;
+      }
+      issue(issued++);
+    }
+  }
+  if (aborted) {
+    // Never leave the CTA with copies still landing in its shared memory: thread 0 waits
+    // (bounded) for the last fill of every stage it armed; then everyone returns.
+    if (tid == 0)
+      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
+        if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
+          atomicOr(&xvram_kernel_error, 4u);
+          break;
+        }
+    return;
   }
 
   // ------------------------------------------------------------------- epilogue
   const float alpha = p.alpha, beta = p.beta;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < TN; ++j) {
     const int col = n0 + frag_index<B_KMAJOR>(tn, j);
     if (col >= p.n)
       continue;
@@ -234,6 +305,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------------
+// Layout canonicalisation.  K-major operand tiles (op(A)=T, op(B)=N) cost the FFMA
+// kernel 15-25 % against M/N-major tiles (the 4-k fragment loads keep the whole A or B
+// fragment live and the register budget is exhausted), so the workspace path first
+// transposes such operands in HBM -- a bandwidth-bound pass of 2 x the operand bytes,
+// about 1-2 % of the GEMM time -- and then runs the M-major / N-major kernel.
+//
+// dst (cols x rows, column-major, ldd) = src^T (src rows x cols, column-major, lds).
+__global__ void __launch_bounds__(256)
+    transpose_f32(const float* __restrict__ src, long long lds, float* __restrict__ dst,
+                  long long ldd, int rows, int cols, int tiles_r) {
+  __shared__ float tile[32][33];
+  const int tr = blockIdx.x % tiles_r;
+  const int tc = blockIdx.x / tiles_r;
+  const int r0 = tr * 32, c0 = tc * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = ty; j < 32; j += 8) {
+    const int r = r0 + tx, c = c0 + j;
+    if (r < rows && c < cols)
+      tile[j][tx] = src[r + static_cast<long long>(c) * lds];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = ty; j < 32; j += 8) {
+    const int c = c0 + tx, r = r0 + j;
+    if (r < rows && c < cols)
+      dst[c + static_cast<long long>(r) * ldd] = tile[tx][j];
+  }
+}
+
+cudaError_t launch_transpose(const float* src, long long lds, float* dst, long long ldd, int rows,
+                             int cols, cudaStream_t stream) {
+  const long long tiles_r = (rows + 31) / 32, tiles_c = (cols + 31) / 32;
+  if (tiles_r * tiles_c > 0x7fffffffll)
+    return cudaErrorInvalidConfiguration;
+  transpose_f32<<<static_cast<unsigned>(tiles_r * tiles_c), 256, 0, stream>>>(
+      src, lds, dst, ldd, rows, cols, static_cast<int>(tiles_r));
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------
@@ -331,20 +443,33 @@ bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t out
   return r == CUDA_SUCCESS;
 }
 
-template <bool AK, bool BK> cudaError_t configure_once() {
-  static cudaError_t status = cudaFuncSetAttribute(
-      sgemm_ffma_tma<AK, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+template <bool AK, bool BK, int TN> cudaError_t configure_once() {
+  static cudaError_t status =
+      cudaFuncSetAttribute(sgemm_ffma_tma<AK, BK, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TileCfg<TN>::SmemBytes);
   return status;
 }
 
-template <bool AK, bool BK>
+template <bool AK, bool BK, int TN>
 cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, const FfmaParams& p,
                        cudaStream_t stream) {
-  if (cudaError_t e = configure_once<AK, BK>(); e != cudaSuccess)
+  if (cudaError_t e = configure_once<AK, BK, TN>(); e != cudaSuccess)
     return e;
   const unsigned grid = static_cast<unsigned>(p.tiles_m) * static_cast<unsigned>(p.tiles_n);
-  sgemm_ffma_tma<AK, BK><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  sgemm_ffma_tma<AK, BK, TN><<<grid, kThreads, TileCfg<TN>::SmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
+}
+
+template <int TN>
+cudaError_t launch_tn(bool a_kmajor, bool b_kmajor, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const FfmaParams& p, cudaStream_t stream) {
+  if (a_kmajor && b_kmajor)
+    return launch_tma<true, true, TN>(ta, tb, p, stream);
+  if (a_kmajor)
+    return launch_tma<true, false, TN>(ta, tb, p, stream);
+  if (b_kmajor)
+    return launch_tma<false, true, TN>(ta, tb, p, stream);
+  return launch_tma<false, false, TN>(ta, tb, p, stream);
 }
 
 } // namespace
@@ -356,6 +481,55 @@ bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const
   const auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0 && lda > 0 && ldb > 0 &&
          lda < (1ll << 37) && ldb < (1ll << 37) && tensor_map_encoder() != nullptr;
+}
+
+uint64_t sgemm_workspace_bytes(int op_a, int op_b, int m, int n, int k) {
+  if (m <= 0 || n <= 0 || k <= 0)
+    return 0;
+  const auto up = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
+  uint64_t bytes = 0;
+  if (op_a != 0)
+    bytes += up(up(static_cast<uint64_t>(m), 4) * static_cast<uint64_t>(k) * 4, 256);
+  if (op_b == 0)
+    bytes += up(up(static_cast<uint64_t>(n), 4) * static_cast<uint64_t>(k) * 4, 256);
+  return bytes;
+}
+
+cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                          long long lda, const float* b, long long ldb, float beta, float* c,
+                          long long ldc, void* workspace, uint64_t workspace_bytes,
+                          cudaStream_t stream, SgemmPath path) {
+  if (m <= 0 || n <= 0)
+    return cudaSuccess;
+  const uint64_t need = sgemm_workspace_bytes(op_a, op_b, m, n, k);
+  if (need > 0 && workspace && workspace_bytes >= need && path != SgemmPath::generic &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+      sgemm_tma_eligible(op_a, op_b, a, lda, b, ldb)) {
+    // Canonicalise K-major operands into the workspace, then run the M/N-major kernel.
+    const auto up4 = [](long long v) { return (v + 3) / 4 * 4; };
+    char* ws = static_cast<char*>(workspace);
+    const float* a2 = a;
+    const float* b2 = b;
+    long long lda2 = lda, ldb2 = ldb;
+    if (op_a != 0) {
+      float* at = reinterpret_cast<float*>(ws);
+      lda2 = up4(m);
+      if (cudaError_t e = launch_transpose(a, lda, at, lda2, k, m, stream); e != cudaSuccess)
+        return e;
+      a2 = at;
+      ws += (static_cast<uint64_t>(lda2) * k * 4 + 255) / 256 * 256;
+    }
+    if (op_b == 0) {
+      float* bt = reinterpret_cast<float*>(ws);
+      ldb2 = up4(n);
+      if (cudaError_t e = launch_transpose(b, ldb, bt, ldb2, k, n, stream); e != cudaSuccess)
+        return e;
+      b2 = bt;
+    }
+    return sgemm_ffma(0, 1, m, n, k, alpha, a2, lda2, b2, ldb2, beta, c, ldc, stream,
+                      SgemmPath::tma);
+  }
+  return sgemm_ffma(op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, stream, path);
 }
 
 cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
@@ -384,11 +558,15 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
 
   const bool a_kmajor = op_a != 0;
   const bool b_kmajor = op_b == 0;
+  // Wide tiles halve shared-memory traffic per FFMA; narrow N keeps 128-wide tiles so
+  // fewer columns are wasted on padding.
+  const int tn = n > 128 ? 16 : 8;
+  const int bn = 16 * tn;
   CUtensorMap ta, tb;
   bool ok = a_kmajor ? encode_2d(&ta, a, k, m, lda, kBK, kBM, true)
                      : encode_2d(&ta, a, m, k, lda, kBM, kBK, false);
-  ok = ok && (b_kmajor ? encode_2d(&tb, b, k, n, ldb, kBK, kBN, true)
-                       : encode_2d(&tb, b, n, k, ldb, kBN, kBK, false));
+  ok = ok && (b_kmajor ? encode_2d(&tb, b, k, n, ldb, kBK, bn, true)
+                       : encode_2d(&tb, b, n, k, ldb, bn, kBK, false));
   if (!ok)
     return cudaErrorInvalidValue;
   FfmaParams p;
@@ -397,7 +575,7 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
   p.k = k;
   p.k_tiles = (k + kBK - 1) / kBK;
   p.tiles_m = (m + kBM - 1) / kBM;
-  p.tiles_n = (n + kBN - 1) / kBN;
+  p.tiles_n = (n + bn - 1) / bn;
   p.alpha = alpha;
   p.beta = beta;
   p.c = c;
@@ -405,13 +583,8 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
   p.timeout_ns = kernel_wait_limit_ns();
   if (static_cast<long long>(p.tiles_m) * p.tiles_n > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
-  if (a_kmajor && b_kmajor)
-    return launch_tma<true, true>(ta, tb, p, stream);
-  if (a_kmajor)
-    return launch_tma<true, false>(ta, tb, p, stream);
-  if (b_kmajor)
-    return launch_tma<false, true>(ta, tb, p, stream);
-  return launch_tma<false, false>(ta, tb, p, stream);
+  return tn == 16 ? launch_tn<16>(a_kmajor, b_kmajor, ta, tb, p, stream)
+                  : launch_tn<8>(a_kmajor, b_kmajor, ta, tb, p, stream);
 }
 
 cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream) {

@@ -32,6 +32,21 @@ def sgemm(op_a: int, op_b: int, m: int, n: int, k: int, alpha: float, a, lda: in
                                        ptr(c), ldc, _stream_handle(stream), path)
 
 
+def workspace_bytes(op_a: int, op_b: int, m: int, n: int, k: int) -> int:
+    """Scratch the K-major canonicalisation needs (0 for op(A)=N, op(B)=T)."""
+    return lib.xvram_b200_sgemm_workspace_bytes(op_a, op_b, m, n, k)
+
+
+def sgemm_ws(op_a: int, op_b: int, m: int, n: int, k: int, alpha: float, a, lda: int, b,
+             ldb: int, beta: float, c, ldc: int, workspace, workspace_bytes: int, stream=None,
+             path: int = PATH_AUTO) -> int:
+    """sgemm with caller-provided device workspace (no allocation inside)."""
+    ptr = lambda x: x if isinstance(x, int) else x.data_ptr()
+    return lib.xvram_b200_sgemm_device_ws(op_a, op_b, m, n, k, alpha, ptr(a), lda, ptr(b), ldb,
+                                          beta, ptr(c), ldc, ptr(workspace), workspace_bytes,
+                                          _stream_handle(stream), path)
+
+
 def kernel_status(stream=None) -> int:
     """Synchronises the stream and returns (and clears) the kernel error word."""
     w = u32(0)
