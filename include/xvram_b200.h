@@ -64,6 +64,41 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
     int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, void* workspace,
     uint64_t workspace_bytes, uint64_t stream, uint32_t path);
 
+/* Size of the fixed scratch array behind xvram_b200_sgemm_device_noalloc (32 MiB). */
+#define XVRAM_B200_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * xvram_b200_sgemm_device for callers that must not allocate device memory.  No
+ * counterpart in the reference.
+ *
+ * Who needs it: an application that has already handed the GPU's memory to its own
+ * allocator (a fixed arena in a serving process or framework), code running inside such
+ * an allocator's callbacks, and plugins whose host only lets them use memory it passes in.
+ * For them a cudaMalloc -- or a pool allocation, which xvram_b200_sgemm_device makes for
+ * its scratch -- fails or re-enters their allocator.
+ *
+ * What it does instead: the scratch for transposing K-major operands comes from one
+ * array compiled into the library, XVRAM_B200_NOALLOC_SCRATCH_BYTES large, which sits in
+ * device memory on every GPU where the library's device code is loaded until the process
+ * exits.  The call makes no cudaMalloc, cudaFree or other allocating call.  The caller
+ * still provides A, B and C.  Arguments and results are those of xvram_b200_sgemm_device;
+ * the device is the caller's current device.
+ *
+ * Limits: a problem that needs more scratch than the array
+ * (xvram_b200_sgemm_workspace_bytes > XVRAM_B200_NOALLOC_SCRATCH_BYTES, for example a TN
+ * product with (M + N) x K above 8 Mi floats) is refused with
+ * XVRAM_STATUS_BUDGET_PRESSURE before anything is launched.  Every call uses the same array
+ * and it keeps whatever the last call left there; each call overwrites all the scratch it
+ * reads, so nothing needs clearing, but calls that overlap on the GPU (different streams
+ * without ordering, or different host threads) race on it and must be serialised by the
+ * caller.  The first call on a device looks up the array's device address (and may load
+ * the library's device code there); make that first call before any stream capture.
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_noalloc(
+    uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
+    int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, uint64_t stream,
+    uint32_t path);
+
 /* Synchronises `stream`, then returns and clears the device's sticky kernel error word
  * (nonzero: a pipeline wait inside a kernel ran out of time and the kernel returned
  * without finishing).  No reference counterpart (the reference has no kernels). */

@@ -55,6 +55,9 @@ def _load() -> C.CDLL:
     lib.xvram_b200_sgemm_device_ws.argtypes = [u32, u32, i64, i64, i64, f32, vp, i64, vp, i64,
                                                f32, vp, i64, vp, u64, u64, u32]
     lib.xvram_b200_sgemm_device_ws.restype = u32
+    lib.xvram_b200_sgemm_device_noalloc.argtypes = [u32, u32, i64, i64, i64, f32, vp, i64, vp,
+                                                    i64, f32, vp, i64, u64, u32]
+    lib.xvram_b200_sgemm_device_noalloc.restype = u32
     lib.xvram_b200_sgemm_workspace_bytes.argtypes = [u32, u32, i64, i64, i64]
     lib.xvram_b200_sgemm_workspace_bytes.restype = u64
     lib.xvram_b200_kernel_status.argtypes = [u64, C.POINTER(u32)]
@@ -88,6 +91,7 @@ EXPORTED = (
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",
+    "xvram_b200_sgemm_device_noalloc",
     "xvram_b200_kernel_status",
     "xvram_b200_fill_uniform",
     "xvram_b200_plan_panels",
