@@ -155,6 +155,36 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int32_t iterations,
                                                              float* sink, uint64_t stream);
 
+/*
+ * Multi-GPU partitioned SGEMM (no reference counterpart: the reference is single-GPU,
+ * src/cuda_compat/adapter.cpp:595-600).  One process or thread per GPU:
+ *   rank 0: xvram_b200_shard_unique_id(id, 128) and share the 128 bytes with the others;
+ *   every rank, with its GPU current: xvram_b200_shard_group_create(id, 128, rank, world, &g);
+ *   every rank, collectively: xvram_b200_sgemm_sharded(g, ...) on its own rows.
+ * Group creation waits at most 120 s for the other ranks (UNAVAILABLE after that).
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_unique_id(void* out, uint64_t bytes);
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void* unique_id,
+                                                                   uint64_t bytes, int32_t rank,
+                                                                   int32_t world,
+                                                                   uint64_t* out_group);
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_destroy(uint64_t group);
+
+/*
+ * C_local = alpha * op(A_local) * op(B) + beta * C_local for this rank's m_local rows of C,
+ * all operands in (preferably page-locked) host memory, column-major.  A_local holds this
+ * rank's rows of op(A) (m_local x k for op N, k x m_local for op T); B is the whole
+ * matrix on every rank, but each rank copies only a 1/world slice of every K panel to
+ * its GPU and the slices are all-gathered over NVLink.  K is processed in panels of
+ * `panel_k` (0 = 1024) with copies and the all-gather of the next panel overlapping the
+ * current panel's kernel.  Blocking; every wait is bounded (TIMEOUT after 60 s without
+ * progress, after which the group is unusable and returns POISONED).
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
+    uint64_t group, uint32_t op_a, uint32_t op_b, int64_t m_local, int64_t n, int64_t k,
+    float alpha, const float* a, int64_t lda, const float* b, int64_t ldb, float beta, float* c,
+    int64_t ldc, int64_t panel_k);
+
 /* Extra state of the compat adapter's runtime (not in the reference telemetry). */
 typedef struct xvram_b200_runtime_info_v1 {
   uint32_t struct_size;

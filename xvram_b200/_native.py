@@ -60,6 +60,15 @@ def _load() -> C.CDLL:
     lib.xvram_b200_sgemm_device_noalloc.restype = u32
     lib.xvram_b200_sgemm_workspace_bytes.argtypes = [u32, u32, i64, i64, i64]
     lib.xvram_b200_sgemm_workspace_bytes.restype = u64
+    lib.xvram_b200_shard_unique_id.argtypes = [vp, u64]
+    lib.xvram_b200_shard_unique_id.restype = u32
+    lib.xvram_b200_shard_group_create.argtypes = [vp, u64, i32, i32, C.POINTER(u64)]
+    lib.xvram_b200_shard_group_create.restype = u32
+    lib.xvram_b200_shard_group_destroy.argtypes = [u64]
+    lib.xvram_b200_shard_group_destroy.restype = u32
+    lib.xvram_b200_sgemm_sharded.argtypes = [u64, u32, u32, i64, i64, i64, f32, vp, i64, vp, i64,
+                                             f32, vp, i64, i64]
+    lib.xvram_b200_sgemm_sharded.restype = u32
     lib.xvram_b200_kernel_status.argtypes = [u64, C.POINTER(u32)]
     lib.xvram_b200_kernel_status.restype = u32
     lib.xvram_b200_fill_uniform.argtypes = [vp, u64, u64, u64, i32]
@@ -93,6 +102,10 @@ EXPORTED = (
     "xvram_b200_sgemm_workspace_bytes",
     "xvram_b200_sgemm_device_noalloc",
     "xvram_b200_kernel_status",
+    "xvram_b200_shard_unique_id",
+    "xvram_b200_shard_group_create",
+    "xvram_b200_shard_group_destroy",
+    "xvram_b200_sgemm_sharded",
     "xvram_b200_fill_uniform",
     "xvram_b200_plan_panels",
     "xvram_b200_plan_steps",

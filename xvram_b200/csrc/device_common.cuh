@@ -70,7 +70,7 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2D tiled TMA load (no multicast) into this CTA's shared memory; completion is
+// 2D tiled TMA load into this CTA's own shared memory only; completion is
 // signalled as transaction bytes on `bar`.  x is the innermost coordinate.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
