@@ -187,6 +187,129 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ---------------------------------------------------------------- out-of-core workload
+def run_out_of_core(args) -> None:
+    """One streamed GEMM through the compat ABI with operands far above the device budget
+    (BASELINE config 3 scaled to the host's memory: NT, alpha 1, beta 1, n^3 with n =
+    --ooc-n, budget --ooc-budget-gib).  Reports the blas_sgemm time, the host-link bytes it
+    moved, eviction / frame-reuse counters and the fraction of
+    max(FLOP / P_fp32, algorithmic H2D bytes / BW_h2d, C bytes / BW_d2h)."""
+    import numpy as np
+    import torch
+
+    from xvram_b200 import compat as cp
+    from xvram_b200 import device as xd
+
+    n = args.ooc_n
+    budget = int(args.ooc_budget_gib * (1 << 30))
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(device=dev)
+    peak_tflops = measure_ffma_peak(dev, stream)
+    h2d_gbs, d2h_gbs = measure_link(dev, stream)
+
+    api = cp.CompatApi()
+    cfg = cp.compat_config_init()
+    cfg.session.cache_target_bytes = budget
+    api.check("initialize", api.initialize(cfg))
+    arrs = []
+    for seed in (100, 101, 102):
+        x = np.empty((n, n), np.float32)
+        xd.fill_uniform(x, seed)
+        arrs.append(x)
+    ptrs = []
+    for x in arrs:
+        d = api.malloc(x.nbytes)
+        api.h2d(d, x.ctypes.data, x.nbytes)
+        ptrs.append(d)
+    h = api.blas_create()
+    flop = 2.0 * n ** 3
+    times, moved = [], []
+    with ClockSampler(0) as clocks:
+        for _ in range(max(args.steps, 1)):
+            t0 = api.telemetry().runtime
+            b0 = (t0.bytes_h2d, t0.bytes_d2h)
+            start = time.perf_counter()
+            api.check("sgemm", api.sgemm(h, 0, 1, n, n, n, 1.0, ptrs[0], n, ptrs[1], n, 1.0,
+                                         ptrs[2], n))
+            times.append(time.perf_counter() - start)
+            t1 = api.telemetry().runtime
+            moved.append((t1.bytes_h2d - b0[0], t1.bytes_d2h - b0[1]))
+    tel = api.telemetry()
+    info = cp.runtime_info()
+    api.shutdown()
+    sec = min(times)
+    h2d_b, d2h_b = moved[times.index(sec)]
+    alg_h2d = 3 * n * n * 4          # A + B + C_in, each once
+    alg_d2h = n * n * 4              # C_out
+    t_roof = max(flop / (peak_tflops * 1e12), alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
+    line = {
+        "metric": METRIC, "workload": f"C3 scaled: {n}^3 NT alpha 1 beta 1, {n * n * 4 >> 30} GiB "
+                                      f"per operand, device budget {args.ooc_budget_gib} GiB",
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": len(times),
+        "ms_per_step": 1e3 * sec, "dtype": "f32", "data": "synthetic",
+        "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
+                     "p_fp32_tflops": peak_tflops, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs,
+                     "bound": "fp32" if flop / (peak_tflops * 1e12) >= alg_h2d / (h2d_gbs * 1e9)
+                     else "host-link"},
+        "host_link": {"h2d_bytes": h2d_b, "d2h_bytes": d2h_b,
+                      "h2d_over_algorithmic": h2d_b / alg_h2d,
+                      "achieved_h2d_gbs": h2d_b / sec / 1e9},
+        "plan": {"block_m": int(info.last_block_m), "block_n": int(info.last_block_n),
+                 "panel_k": int(info.last_panel_k), "steps": int(info.last_steps),
+                 "panel_slots": int(info.last_panel_slots)},
+        "residency": {"cache_target_bytes": int(tel.runtime.cache_target_bytes),
+                      "resident_bytes_peak": int(tel.runtime.resident_bytes_peak),
+                      "clean_evictions": int(tel.runtime.clean_evictions),
+                      "dirty_evictions": int(tel.runtime.dirty_evictions),
+                      "handle_reuses": int(tel.runtime.handle_reuses),
+                      "mappings": int(tel.runtime.mappings), "unmaps": int(tel.runtime.unmaps),
+                      "tiles_retired": int(tel.tiles_retired)},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def measure_ffma_peak(dev, stream, iters: int = 8000) -> float:
+    """FP32 pipe peak (TFLOP/s) from the FFMA probe: ~15 ms launches, best of 7."""
+    import torch
+    from xvram_b200 import device as xd
+    sink = torch.zeros(1, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * 4
+    best = 0.0
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            assert xd.ffma_probe(blocks, iters, sink, stream) == 0
+            e1.record(stream)
+            e1.synchronize()
+            if i:
+                best = max(best, 2.0 * blocks * 256 * iters * 512 / (e0.elapsed_time(e1) * 1e-3))
+    return best / 1e12
+
+
+def measure_link(dev, stream) -> tuple[float, float]:
+    """Pinned H2D and D2H GB/s (64 MiB copies, best of 4)."""
+    import torch
+    probe_h = torch.empty(16 << 20, dtype=torch.float32).pin_memory()
+    probe_d = torch.empty(16 << 20, dtype=torch.float32, device=dev)
+    h2d = d2h = 0.0
+    with torch.cuda.stream(stream):
+        for _ in range(4):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            probe_d.copy_(probe_h, non_blocking=True)
+            e1.record(stream)
+            probe_h.copy_(probe_d, non_blocking=True)
+            e2.record(stream)
+            e2.synchronize()
+            h2d = max(h2d, probe_h.nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+            d2h = max(d2h, probe_h.nbytes / (e1.elapsed_time(e2) * 1e-3) / 1e9)
+    return h2d, d2h
+
+
 # ------------------------------------------------------------------------------ GPU arm
 def main_gpu(args) -> None:
     import torch
@@ -232,45 +355,11 @@ def main_gpu(args) -> None:
     Cd = c_h.to(dev)
     torch.cuda.synchronize()
 
-    # FP32 pipe peak on this device, this run (FFMA probe, ~15 ms launches, best of 8;
-    # repeated after the kernel's timed region so both see a warm clock).
-    sink = torch.zeros(1, device=dev)
+    # FP32 pipe peak on this device, this run (FFMA probe), repeated after the kernel's
+    # timed region so both see a warm clock; pinned host-link bandwidth.
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    blocks, iters = sms * 4, 8000
-
-    def ffma_peak() -> float:
-        best = 0.0
-        with torch.cuda.stream(stream):
-            for i in range(8):
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                assert xd.ffma_probe(blocks, iters, sink, stream) == 0
-                e1.record(stream)
-                e1.synchronize()
-                if i:
-                    best = max(best, 2.0 * blocks * 256 * iters * 512 /
-                               (e0.elapsed_time(e1) * 1e-3))
-        return best / 1e12
-
-    peak_tflops = ffma_peak()
-
-    # Host link: pinned H2D / D2H GB/s (64 MiB x 8, best).
-    probe_h = torch.empty(16 << 20, dtype=torch.float32).pin_memory()
-    probe_d = torch.empty(16 << 20, dtype=torch.float32, device=dev)
-    h2d = d2h = 0.0
-    with torch.cuda.stream(stream):
-        for _ in range(4):
-            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            e0.record(stream)
-            probe_d.copy_(probe_h, non_blocking=True)
-            e1.record(stream)
-            probe_h.copy_(probe_d, non_blocking=True)
-            e2.record(stream)
-            e2.synchronize()
-            h2d = max(h2d, probe_h.nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
-            d2h = max(d2h, probe_h.nbytes / (e1.elapsed_time(e2) * 1e-3) / 1e9)
-    del probe_h, probe_d
+    peak_tflops = measure_ffma_peak(dev, stream)
+    h2d, d2h = measure_link(dev, stream)
 
     # ---------------- kernel-only: inputs resident in HBM
     def launch():
@@ -295,7 +384,7 @@ def main_gpu(args) -> None:
     torch.cuda.synchronize()
     barrier()
     assert xd.kernel_status(stream) == 0
-    peak_tflops = max(peak_tflops, ffma_peak())
+    peak_tflops = max(peak_tflops, measure_ffma_peak(dev, stream))
     kernel_ms = start.elapsed_time(stop) / args.steps
     kernel_ms_max = max_over_ranks(kernel_ms)
     value = world * FLOP / (kernel_ms_max * 1e-3) / 1e12
@@ -438,11 +527,18 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c2", "c3s"], default="c2",
+                    help="c2: the headline (BASELINE config 2); c3s: one out-of-core GEMM")
+    ap.add_argument("--ooc-n", type=int, default=65536)
+    ap.add_argument("--ooc-budget-gib", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload == "c3s":
+        run_out_of_core(args)
         return
     main_gpu(args)
 

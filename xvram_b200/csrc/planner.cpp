@@ -15,7 +15,8 @@ constexpr int64_t kTileN = 128;
 constexpr int64_t kTileK = 32;
 constexpr int kSmCount = 148;
 constexpr double kStepOverheadS = 15e-6; // launch + event bookkeeping per step
-constexpr int64_t kMaxSteps = 1 << 20;
+constexpr int64_t kMaxSteps = 1 << 15;     // steps a plan may have
+constexpr int kMaxSimulations = 96;          // candidates simulated per plan
 constexpr int32_t kNever = INT32_MAX;
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -262,33 +263,69 @@ PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* ou
     if (v <= 0 || v % kTileK)
       return PlanStatus::invalid;
 
-  bool found = false;
-  Geo best{};
-  Plan trial, best_plan;
-  int considered = 0;
+  // Rank candidates by a closed-form lower bound on their time -- compute at the block's
+  // wave efficiency plus per-step overhead, or the unavoidable link traffic (every operand
+  // byte once) -- and simulate only while the bound can still beat the best plan.
+  struct Cand {
+    Geo g;
+    double lb;
+  };
+  std::vector<Cand> cands;
+  const double flops = 2.0 * static_cast<double>(p.m) * static_cast<double>(p.n) *
+                       static_cast<double>(p.k);
+  const double min_h2d =
+      4.0 * (static_cast<double>(p.m) * p.k + static_cast<double>(p.k) * p.n +
+             (p.beta_nonzero ? static_cast<double>(p.m) * p.n : 0.0));
+  const double min_d2h = 4.0 * static_cast<double>(p.m) * p.n;
+  const bool forced = lim.force_mb || lim.force_nb || lim.force_kb;
   for (int64_t mb : mbs)
     for (int64_t nb : nbs)
       for (int64_t kb : kbs)
         for (int order = 0; order < 2; ++order) {
           if (lim.force_order >= 0 && order != lim.force_order)
             continue;
-          const Geo g{mb, nb, kb, order == 1};
-          if (!simulate(p, lim, g, false, &trial))
+          const int64_t steps = ceil_div(p.m, mb) * ceil_div(p.n, nb) * ceil_div(p.k, kb);
+          if (steps > kMaxSteps)
             continue;
-          ++considered;
-          const bool better =
-              !found || trial.est_seconds < best_plan.est_seconds * (1 - 1e-9) ||
-              (trial.est_seconds <= best_plan.est_seconds * (1 + 1e-9) &&
-               (trial.h2d_bytes < best_plan.h2d_bytes ||
-                (trial.h2d_bytes == best_plan.h2d_bytes &&
-                 trial.blocks_m * trial.blocks_n * trial.panels_k <
-                     best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k)));
-          if (better) {
-            found = true;
-            best = g;
-            best_plan = trial;
-          }
+          // A block smaller than one wave of CTAs wastes SMs on every launch; skip it
+          // unless the problem itself is that small (or the geometry is forced).
+          if (!forced && ceil_div(std::min(mb, p.m), kTileM) * ceil_div(std::min(nb, p.n), kTileN) <
+                             kSmCount &&
+              (mb < p.m || nb < p.n))
+            continue;
+          const double lb = std::max({flops / lim.flops_per_s /
+                                          wave_efficiency(std::min(mb, p.m), std::min(nb, p.n)) +
+                                          steps * kStepOverheadS,
+                                      min_h2d / lim.h2d_bytes_per_s,
+                                      min_d2h / lim.d2h_bytes_per_s});
+          cands.push_back({Geo{mb, nb, kb, order == 1}, lb});
         }
+  std::stable_sort(cands.begin(), cands.end(),
+                   [](const Cand& x, const Cand& y) { return x.lb < y.lb; });
+
+  bool found = false;
+  Geo best{};
+  Plan trial, best_plan;
+  int considered = 0;
+  for (const Cand& cd : cands) {
+    if (found && (cd.lb > best_plan.est_seconds || considered >= kMaxSimulations))
+      break;
+    if (!simulate(p, lim, cd.g, false, &trial))
+      continue;
+    ++considered;
+    const bool better =
+        !found || trial.est_seconds < best_plan.est_seconds * (1 - 1e-9) ||
+        (trial.est_seconds <= best_plan.est_seconds * (1 + 1e-9) &&
+         (trial.h2d_bytes < best_plan.h2d_bytes ||
+          (trial.h2d_bytes == best_plan.h2d_bytes &&
+           trial.blocks_m * trial.blocks_n * trial.panels_k <
+               best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k)));
+    if (better) {
+      found = true;
+      best = cd.g;
+      best_plan = trial;
+    }
+  }
   if (!found)
     return PlanStatus::budget_too_small;
   simulate(p, lim, best, true, out);
