@@ -29,7 +29,11 @@ extern "C" {
 enum {
   XVRAM_B200_PATH_AUTO = 0,    /* TMA kernel when aligned, else the generic kernel */
   XVRAM_B200_PATH_TMA = 1,     /* TMA kernel or INVALID_ARGUMENT */
-  XVRAM_B200_PATH_GENERIC = 2  /* generic kernel (any alignment) */
+  XVRAM_B200_PATH_GENERIC = 2, /* generic kernel (any alignment) */
+  /* Three-term TF32 on the tensor cores (tcgen05/TMEM): FP32-accurate within
+   * max|err| / (K max|a| max|b|) <= 1e-6 but not bit-identical to the FFMA kernels.
+   * Needs xvram_b200_sgemm_workspace_bytes(...) with this path, k > 0. */
+  XVRAM_B200_PATH_TF32X3 = 3
 };
 
 /*
@@ -47,7 +51,9 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
 
 /* Bytes of device workspace the K-major operand canonicalisation needs for this problem:
  * transposed copies of op(A) when op_a = T and of op(B) when op_b = N (0 for op_a = N,
- * op_b = T).  No reference counterpart. */
+ * op_b = T).  Pass op_a | XVRAM_B200_WORKSPACE_TF32X3 for the tensor-core path's split
+ * operands instead.  No reference counterpart. */
+#define XVRAM_B200_WORKSPACE_TF32X3 0x100u
 XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_a, uint32_t op_b,
                                                                     int64_t m, int64_t n,
                                                                     int64_t k);

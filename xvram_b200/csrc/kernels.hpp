@@ -32,8 +32,18 @@ cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, 
 bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
                         long long ldb);
 
+// Three-term TF32 tensor-core GEMM (tcgen05 + TMEM), FP32-accurate within the path's
+// tolerance but not bit-identical to the FFMA kernel.  Needs sgemm_tf32x3_workspace_bytes
+// of 256-byte-aligned scratch for the split hi/lo operands; k must be positive.
+uint64_t sgemm_tf32x3_workspace_bytes(int m, int n, int k);
+cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
+                         long long lda, const float* b, long long ldb, float beta, float* c,
+                         long long ldc, void* workspace, uint64_t workspace_bytes,
+                         cudaStream_t stream);
+
 // Reads (synchronising `stream`) and clears the device's sticky kernel error word.
 cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream);
+cudaError_t read_and_clear_kernel_error_tc(unsigned int* out, cudaStream_t stream);
 
 unsigned long long kernel_wait_limit_ns();
 

@@ -65,7 +65,7 @@ cudaMemPool_t scratch_pool(int device) {
 bool valid_args(uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, const float* a,
                 int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, uint32_t path) {
   if (op_a > 1 || op_b > 1 || m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
-      k > INT32_MAX || path > XVRAM_B200_PATH_GENERIC)
+      k > INT32_MAX || path > XVRAM_B200_PATH_TF32X3)
     return false;
   if (m == 0 || n == 0)
     return true;
@@ -74,6 +74,7 @@ bool valid_args(uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, c
 }
 
 SgemmPath to_path(uint32_t path) {
+  // (XVRAM_B200_PATH_TF32X3 is dispatched before this mapping is used.)
   return path == XVRAM_B200_PATH_TMA       ? SgemmPath::tma
          : path == XVRAM_B200_PATH_GENERIC ? SgemmPath::generic
                                            : SgemmPath::automatic;
@@ -118,8 +119,22 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
     return XVRAM_STATUS_SUCCESS;
   const int oa = static_cast<int>(op_a), ob = static_cast<int>(op_b);
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-  const uint64_t need = sgemm_workspace_bytes(oa, ob, mi, ni, ki);
   cudaStream_t s = as_stream(stream);
+  if (path == XVRAM_B200_PATH_TF32X3 && k > 0) {
+    const uint64_t tneed = sgemm_tf32x3_workspace_bytes(mi, ni, ki);
+    int dev = 0;
+    cudaMemPool_t pool = cudaGetDevice(&dev) == cudaSuccess ? scratch_pool(dev) : nullptr;
+    void* ws = nullptr;
+    if (!pool || cudaMallocFromPoolAsync(&ws, tneed, pool, s) != cudaSuccess) {
+      cudaGetLastError();
+      return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
+    }
+    const cudaError_t e =
+        sgemm_tf32x3(oa, ob, mi, ni, ki, alpha, a, lda, b, ldb, beta, c, ldc, ws, tneed, s);
+    const cudaError_t f = cudaFreeAsync(ws, s);
+    return from_cuda(e != cudaSuccess ? e : f);
+  }
+  const uint64_t need = sgemm_workspace_bytes(oa, ob, mi, ni, ki);
   if (need && path != XVRAM_B200_PATH_GENERIC && sgemm_tma_eligible(oa, ob, a, lda, b, ldb)) {
     int dev = 0;
     cudaMemPool_t pool = cudaGetDevice(&dev) == cudaSuccess ? scratch_pool(dev) : nullptr;
@@ -139,9 +154,14 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device(
 XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_a, uint32_t op_b,
                                                                     int64_t m, int64_t n,
                                                                     int64_t k) {
+  const bool tf32x3 = (op_a & XVRAM_B200_WORKSPACE_TF32X3) != 0;
+  op_a &= ~XVRAM_B200_WORKSPACE_TF32X3;
   if (op_a > 1 || op_b > 1 || m <= 0 || n <= 0 || k <= 0 || m > INT32_MAX || n > INT32_MAX ||
       k > INT32_MAX)
     return 0;
+  if (tf32x3)
+    return sgemm_tf32x3_workspace_bytes(static_cast<int>(m), static_cast<int>(n),
+                                        static_cast<int>(k));
   return sgemm_workspace_bytes(static_cast<int>(op_a), static_cast<int>(op_b),
                                static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
 }
@@ -154,6 +174,11 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
     return XVRAM_STATUS_INVALID_ARGUMENT;
   if (m == 0 || n == 0)
     return XVRAM_STATUS_SUCCESS;
+  if (path == XVRAM_B200_PATH_TF32X3 && k > 0)
+    return from_cuda(sgemm_tf32x3(static_cast<int>(op_a), static_cast<int>(op_b),
+                                  static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                                  alpha, a, lda, b, ldb, beta, c, ldc, workspace, workspace_bytes,
+                                  as_stream(stream)));
   return from_cuda(sgemm_ffma_ws(static_cast<int>(op_a), static_cast<int>(op_b),
                                  static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
                                  alpha, a, lda, b, ldb, beta, c, ldc, workspace, workspace_bytes,
@@ -163,9 +188,11 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_kernel_status(uint64_t stream, uint32_t* word) {
   if (!word)
     return XVRAM_STATUS_INVALID_ARGUMENT;
-  unsigned int w = 0;
-  const cudaError_t e = read_and_clear_kernel_error(&w, as_stream(stream));
-  *word = w;
+  unsigned int w = 0, wt = 0;
+  cudaError_t e = read_and_clear_kernel_error(&w, as_stream(stream));
+  if (e == cudaSuccess)
+    e = read_and_clear_kernel_error_tc(&wt, as_stream(stream));
+  *word = w | (wt << 8); // tensor-core kernel bits in the second byte
   return from_cuda(e);
 }
 
