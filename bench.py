@@ -290,6 +290,15 @@ def measure_ffma_peak(dev, stream, iters: int = 8000) -> float:
     return best / 1e12
 
 
+def measured_tf32_peak():
+    """Dense TF32 tensor peak implied by the driver-measured BF16 GEMM burst figure."""
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return peaks["bf16_tflops"] / 2.0
+    except (OSError, ValueError, KeyError):
+        return 1590.0 / 2.0  # fallback figure of the profiling recipe (bf16 1.59 PFLOP/s)
+
+
 def measure_link(dev, stream) -> tuple[float, float]:
     """Pinned H2D and D2H GB/s (64 MiB copies, best of 4)."""
     import torch
@@ -390,6 +399,33 @@ def main_gpu(args) -> None:
     value = world * FLOP / (kernel_ms_max * 1e-3) / 1e12
     achieved = FLOP / (kernel_ms * 1e-3) / 1e12
 
+    # ---------------- kernel-only, tensor-core path (three-term TF32 on tcgen05/TMEM)
+    tc_need = lib.xvram_b200_sgemm_workspace_bytes(OP_A | 0x100, OP_B, M, N, K)
+    tc_ws = torch.empty(tc_need // 4 + 64, dtype=torch.float32, device=dev)
+    C_tc = Cd.clone()
+
+    def launch_tc():
+        st = xd.sgemm_ws(OP_A, OP_B, M, N, K, ALPHA, A, K, B, K, BETA, C_tc, M, tc_ws, tc_need,
+                         stream=stream, path=3)
+        assert st == 0, st
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            launch_tc()
+    stream.synchronize()
+    barrier()
+    with ClockSampler(local) as tc_clocks:
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            t0e.record(stream)
+            for _ in range(args.steps):
+                launch_tc()
+            t1e.record(stream)
+        t1e.synchronize()
+    assert xd.kernel_status(stream) == 0
+    tc_ms = max_over_ranks(t0e.elapsed_time(t1e) / args.steps)
+    del tc_ws, C_tc
+
     # ---------------- end to end, sharded path: C rows per rank, B panels read 1/N per rank
     # from host memory and all-gathered over NVLink (xvram_b200_sgemm_sharded)
     from xvram_b200 import shard
@@ -446,6 +482,18 @@ def main_gpu(args) -> None:
     e2e_s_max = max_over_ranks(e2e_s)
     tel = api.telemetry()
     info = cp.runtime_info()
+    # the same steps with the handle in TF32 tensor-op math mode (three-term TF32 kernel)
+    api.check("math", api.t.blas_set_math_mode(h, 3))
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_tc_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    api.check("math", api.t.blas_set_math_mode(h, 0))
     # one SGEMM kernel plus the two canonicalising transposes per in-place GEMM
     launches_e2e = int(info.gemm_in_place) * (1 + int(OP_A == 1) + int(OP_B == 0))
     for d in (da, db, dc):
@@ -509,6 +557,22 @@ def main_gpu(args) -> None:
                             "d2h_bytes_per_step": sh_d2h, "panel_k": 1024,
                             "path": "xvram_b200_sgemm_sharded (copies overlap compute)"},
             # per step: the SGEMM kernel plus one transpose per K-major operand (TN: 2)
+            "tf32x3": {
+                "what": "three-term TF32 on tcgen05/TMEM (math mode 3 / XVRAM_B200_PATH_TF32X3); "
+                        "FP32-accurate within max|err|/(K max|a| max|b|) <= 1e-6, not bit-identical",
+                "value": world * FLOP / (tc_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": tc_ms,
+                "vs_fp32_ffma_peak": FLOP / (tc_ms * 1e-3) / 1e12 / peak_tflops,
+                "tensor_pipe": {"bound": "tensor", "tf32_flop_per_step": 3 * FLOP,
+                                "achieved_tf32_tflops": 3 * FLOP / (tc_ms * 1e-3) / 1e12,
+                                "peak_tf32_tflops": measured_tf32_peak(),
+                                "peak_source": "MEASURED_PEAKS.json bf16_tflops / 2 (TF32 runs "
+                                               "at half the BF16 tensor rate)"},
+                "e2e": {"value": FLOP / e2e_tc_s / 1e12, "unit": "TFLOP/s",
+                        "ms_per_step": 1e3 * e2e_tc_s,
+                        "path": "compat ABI, blas_set_math_mode(3)"},
+                "clocks": tc_clocks.summary(),
+            },
             "gpu_launches": args.steps * (1 + int(OP_A == 1) + int(OP_B == 0)),
             "gpu_launches_e2e": launches_e2e,
             "clocks": clocks.summary(),

@@ -142,6 +142,7 @@ def scenario_errors(oracle):
     r["set_device_other"] = api.t.set_device(1)
     r["set_stream"] = api.t.blas_set_stream(h, 1234)
     r["pointer_mode_device"] = api.t.blas_set_pointer_mode(h, 1)
+    r["math_tensor_op"] = api.t.blas_set_math_mode(h, 1)
     r["math_tf32"] = api.t.blas_set_math_mode(h, 3)
     r["math_pedantic"] = api.t.blas_set_math_mode(h, 2)
     r["free_interior"] = api.t.free_device(da + 64)
@@ -220,6 +221,37 @@ def scenario_in_place_two_passes(oracle):
     info = cp.runtime_info()
     res = dict(err=err, ok=err <= TOLERANCE, in_place=info.gemm_in_place,
                streamed=info.gemm_streamed)
+    res["shutdown"] = api.shutdown()
+    return res
+
+
+def scenario_tensor_cores(oracle):
+    """Math mode 3 (TF32 tensor-op math) selects the three-term TF32 tcgen05 path, in place
+    and out of core (512 MiB budget), both within the stated tolerance."""
+    api = cp.CompatApi()
+    init(api, cache_target=512 * MiB, chunk=64 * MiB)
+    h = api.blas_create()
+    api.check("math", api.t.blas_set_math_mode(h, 3))
+    mode = C.c_uint32(0)
+    api.check("get_math", api.t.blas_get_math_mode(h, C.byref(mode)))
+    res = {"mode": mode.value}
+    for tag, (m, n, k) in (("in_place", (1024, 768, 1536)), ("streamed", (6144, 6144, 6144))):
+        a = oracle.uniform(m * k, 60).reshape(m, k)   # op T: stored k x m
+        b = oracle.uniform(k * n, 61).reshape(n, k)   # op N: stored k x n
+        c = oracle.uniform(m * n, 62).reshape(n, m)
+        da, db, dc = upload(api, a), upload(api, b), upload(api, c)
+        api.check("sgemm", api.sgemm(h, 1, 0, m, n, k, 0.5, da, k, db, k, 1.5, dc, m))
+        out = np.empty_like(c)
+        api.d2h(ptr(out), dc, out.nbytes)
+        rng = np.random.default_rng(2)
+        rows, cols = rng.integers(0, m, 8192), rng.integers(0, n, 8192)
+        ref = oracle.gemm_sampled(1, 0, k, 0.5, a, k, b, k, 1.5, c, m, rows, cols, threads=16)
+        res[tag] = float(np.max(np.abs(out[cols, rows] - ref))) / k
+        for d in (da, db, dc):
+            api.free(d)
+    info = cp.runtime_info()
+    res.update(in_place_calls=info.gemm_in_place, streamed_calls=info.gemm_streamed,
+               ok=max(res["in_place"], res["streamed"]) <= TOLERANCE)
     res["shutdown"] = api.shutdown()
     return res
 

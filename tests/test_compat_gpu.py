@@ -42,9 +42,10 @@ def test_error_classes():
                 "memcpy_oob", "memcpy_host_is_managed", "double_free", "use_after_free"):
         assert r[key] == S["INVALID_ARGUMENT"], key
     for key in ("bad_op", "zero_m", "nan_alpha", "set_device_other", "set_stream",
-                "pointer_mode_device", "math_tf32", "memcpy_d2d"):
+                "pointer_mode_device", "math_tensor_op", "memcpy_d2d"):
         assert r[key] == S["UNSUPPORTED"], key
-    assert r["math_pedantic"] == 0 and r["free_null"] == 0 and r["free"] == 0
+    assert r["math_tf32"] == 0 and r["math_pedantic"] == 0
+    assert r["free_null"] == 0 and r["free"] == 0
     assert r["shutdown"] == 0 and r["after_shutdown"] == S["CLOSED"]
     assert r["second_init"] == S["CLOSED"] and r["state"] == 4 and r["attempted_eq"]
 
@@ -65,3 +66,11 @@ def test_in_place_two_passes():
     r = run("in_place_two_passes")
     assert r["ok"], r
     assert r["in_place"] == 2 and r["streamed"] == 0
+
+
+def test_tensor_core_math_mode_in_place_and_streamed():
+    r = run("tensor_cores")
+    assert r["mode"] == 3
+    assert r["ok"], r
+    assert r["in_place_calls"] == 1 and r["streamed_calls"] == 1
+    assert r["shutdown"] == 0

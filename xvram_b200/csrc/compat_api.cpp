@@ -401,8 +401,11 @@ public:
       Handle* hd = handle(h);
       if (!hd)
         return invalid("cublasSetMathMode", "live handle required");
-      if (mode != 0 && mode != 2)
-        return unsupported("cublasSetMathMode", "only default and pedantic FP32 math modes are supported");
+      // 0 default and 2 pedantic: strict FP32 (FFMA), as in the reference.  3 (TF32 tensor-op
+      // math) selects the three-term TF32 tensor-core path, which is more accurate than the
+      // single-TF32 products that mode permits.
+      if (mode != 0 && mode != 2 && mode != 3)
+        return unsupported("cublasSetMathMode", "math modes 0, 2 (strict FP32) and 3 (tensor cores) are supported");
       hd->math_mode = mode;
       return {};
     });
@@ -470,6 +473,9 @@ public:
                           problem_error_name(v.error));
       call.alpha = alpha_v;
       call.beta = beta_v;
+      call.tensor_cores = handle(h)->math_mode == 3;
+      if (call.tensor_cores)
+        call.flops_per_s = 150e12; // plan for the tensor-core rate
       if (Error e = runtime_->gemm(call))
         return e;
       std::lock_guard lock(snap_mu_);

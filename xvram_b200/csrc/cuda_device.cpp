@@ -281,9 +281,20 @@ public:
 
   Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha, uint64_t a,
               int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c, int64_t ldc,
-              uint64_t workspace, uint64_t workspace_bytes, StreamId s) override {
+              uint64_t workspace, uint64_t workspace_bytes, bool tensor_cores,
+              StreamId s) override {
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
       return make_error(XVRAM_STATUS_INTERNAL, "executor", "sgemm", "tile exceeds int32");
+    if (tensor_cores && k > 0) {
+      const cudaError_t e = sgemm_tf32x3(
+          op_a, op_b, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), alpha,
+          reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(b), ldb, beta,
+          reinterpret_cast<float*>(c), ldc, reinterpret_cast<void*>(workspace), workspace_bytes,
+          stream(s));
+      if (e != cudaSuccess)
+        return rt_error("sgemm_tf32x3 launch", e);
+      return {};
+    }
     const cudaError_t e = sgemm_ffma_ws(
         op_a, op_b, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), alpha,
         reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(b), ldb, beta,
@@ -294,17 +305,22 @@ public:
     return {};
   }
 
-  uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k) override {
+  uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                           bool tensor_cores) override {
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
       return 0;
+    if (tensor_cores)
+      return sgemm_tf32x3_workspace_bytes(static_cast<int>(m), static_cast<int>(n),
+                                          static_cast<int>(k));
     return sgemm_workspace_bytes(op_a, op_b, static_cast<int>(m), static_cast<int>(n),
                                  static_cast<int>(k));
   }
 
   Error kernel_status(StreamId s, uint32_t* word) override {
-    unsigned int w = 0;
+    unsigned int w = 0, wt = 0;
     XV_RT("read_kernel_error", read_and_clear_kernel_error(&w, stream(s)));
-    *word = w;
+    XV_RT("read_kernel_error_tc", read_and_clear_kernel_error_tc(&wt, stream(s)));
+    *word = w | (wt << 8);
     return {};
   }
 

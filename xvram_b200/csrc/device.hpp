@@ -70,11 +70,14 @@ public:
 
   // C = alpha * op(A) op(B) + beta * C on device addresses (column-major FP32).  With
   // `workspace_bytes` >= sgemm_workspace_bytes K-major operands are canonicalised there.
+  // `tensor_cores` selects the three-term TF32 tcgen05 kernel instead of the FFMA kernel.
   virtual Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha,
                       uint64_t a, int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c,
-                      int64_t ldc, uint64_t workspace, uint64_t workspace_bytes, StreamId s) = 0;
-  // Workspace the canonicalising path needs for this problem (0 if none).
-  virtual uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k) = 0;
+                      int64_t ldc, uint64_t workspace, uint64_t workspace_bytes, bool tensor_cores,
+                      StreamId s) = 0;
+  // Workspace the chosen kernel needs for this problem (0 if none).
+  virtual uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                                   bool tensor_cores) = 0;
   // Reads and clears the sticky error word of the library's kernels (synchronising s).
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
 };

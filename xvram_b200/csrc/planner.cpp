@@ -76,6 +76,9 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
       ws += up(up(static_cast<uint64_t>(g.mb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
     if (lim.transpose_b)
       ws += up(up(static_cast<uint64_t>(g.nb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
+    if (lim.tf32x3)
+      ws = 2 * up(static_cast<uint64_t>(g.mb) * up(static_cast<uint64_t>(g.kb), 4) * 4u, 256) +
+           2 * up(static_cast<uint64_t>(g.nb) * up(static_cast<uint64_t>(g.kb), 4) * 4u, 256);
     pl.workspace_bytes = round_up(ws, q);
   }
   const uint64_t c_total =

@@ -40,6 +40,8 @@ struct PlanLimits {
   // Per-step device workspace for canonicalising K-major panels: the kernel transposes
   // op(A) panels when transpose_a and op(B) panels when transpose_b.
   bool transpose_a = false, transpose_b = false;
+  // Tensor-core steps instead: hi/lo split copies of both panels (2 x (mb + nb) x kb floats).
+  bool tf32x3 = false;
   int force_order = -1;                             // -1 search, 0 m-outer, 1 n-outer
 };
 

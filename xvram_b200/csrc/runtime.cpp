@@ -567,7 +567,8 @@ Error Runtime::gemm(const GemmCall& call) {
   // The kernel's canonicalisation workspace comes out of the same frame budget.
   const GemmShape& sh = call.shape;
   const uint64_t ws = m.dev->sgemm_workspace(sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
-                                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k));
+                                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k),
+                                             call.tensor_cores);
   const uint64_t ws_chunks = (ws + m.cb - 1) / m.cb;
   const size_t data_chunks = keep.size();
   for (uint64_t c = 0; c < ws_chunks && c < m.capacity; ++c)
@@ -603,7 +604,7 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
                            static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
                            static_cast<int64_t>(s.b.ld), call.beta, C.va + s.c.offset_bytes,
                            static_cast<int64_t>(s.c.ld), ws ? allocs.at(kScratchId).va : 0, ws,
-                           s_compute))
+                           call.tensor_cores, s_compute))
     return e;
   for (const auto& [id, c] : keep) {
     Frame& f = frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)];
@@ -654,8 +655,11 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
   lim.flops_per_s = cfg.flops_per_s;
   lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
   lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
-  lim.transpose_a = s.op_a != 0;
-  lim.transpose_b = s.op_b == 0;
+  lim.transpose_a = !call.tensor_cores && s.op_a != 0;
+  lim.transpose_b = !call.tensor_cores && s.op_b == 0;
+  lim.tf32x3 = call.tensor_cores;
+  if (call.flops_per_s > 0)
+    lim.flops_per_s = call.flops_per_s;
   Plan plan;
   const PlanStatus ps = make_panel_plan(pp, lim, &plan);
   if (ps != PlanStatus::ok)
@@ -814,7 +818,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     const int64_t ldb_s = s.op_b == 0 ? kb : nb;
     if ((err = dev->sgemm(s.op_a, s.op_b, mr, nr, kr, call.alpha, slot_va(st.slot_a), lda_s,
                           slot_va(st.slot_b), ldb_s, beta_eff, cva, mb,
-                          plan.workspace_bytes ? ws_base : 0, plan.workspace_bytes, s_compute)))
+                          plan.workspace_bytes ? ws_base : 0, plan.workspace_bytes,
+                          call.tensor_cores, s_compute)))
       break;
     ++x.tiles_submitted;
     for (int32_t sl : {st.slot_a, st.slot_b}) {

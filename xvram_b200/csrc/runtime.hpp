@@ -51,6 +51,11 @@ struct RuntimeConfig {
 struct GemmCall {
   GemmShape shape;
   float alpha = 1.0f, beta = 0.0f;
+  // Three-term TF32 on the tensor cores (FP32-accurate within 1e-6 of the normalised
+  // error bound) instead of strict FFMA.
+  bool tensor_cores = false;
+  // Rates for planning this call (0 = the runtime's configured rates).
+  double flops_per_s = 0;
 };
 
 // Counters that are not part of xvram_session_telemetry_v1.
