@@ -66,3 +66,54 @@ def test_long_k_accuracy(oracle):
     """K = 8192: the dropped lo*lo term and TF32 rounding of lo stay far below tolerance."""
     err = run(oracle, 1, 0, 256, 256, 8192, 1.0, 0.0, seed=13)
     assert err <= TOLERANCE / 10
+
+
+def _positive_case(oracle, path, k):
+    m, n = 256, 256
+    a = (oracle.uniform(m * k, 21).reshape(m, k) + 1.0) * 0.5   # uniform[0, 1): same sign
+    b = (oracle.uniform(k * n, 22).reshape(n, k) + 1.0) * 0.5
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    Cd = torch.zeros((n, m), device="cuda")
+    assert device.sgemm(1, 0, m, n, k, 1.0, A, k, B, k, 0.0, Cd, m, path=path) == 0
+    ref = oracle.gemm(1, 0, m, n, k, 1.0, a, k, b, k, 0.0, None, m, threads=16)
+    out = Cd.cpu().numpy().astype(np.float64)
+    return float(np.max(np.abs(out - ref) / np.abs(ref)))
+
+
+@pytest.mark.parametrize("k", [512, 2048, 8192])
+def test_same_sign_data_relative_error(oracle, k):
+    """All-positive operands make the accumulator grow linearly, the worst case for the
+    tensor core's FP32 accumulation.  The relative error must stay within the reference's
+    own acceptance slope (2e-5 |ref|, src/compat_bench/executor.cpp:93-96) and within 8x
+    the strict FFMA kernel's."""
+    tc = _positive_case(oracle, TF32X3, k)
+    ffma = _positive_case(oracle, 0, k)
+    print(f"k={k} max relative error: tf32x3 {tc:.3e}  ffma {ffma:.3e}")
+    assert tc <= 2e-5
+    assert tc <= 8 * max(ffma, 2 ** -24)
+
+
+def test_reference_gate_pattern_acceptance(oracle):
+    """The reference's padded gate operands (compat_bench patterns, 37x19x67) through the
+    tensor-core path meet the reference's own acceptance criterion."""
+    import json
+    from pathlib import Path
+    from oracle_lib import reference_criterion
+    g = json.loads((Path(__file__).parent / "golden" / "reference_vectors.json").read_text())
+    fills = {(f["ta"], f["tb"], f["operand"]): f for f in g["cb_padded_fills"]["fills"]}
+    shp = g["cb_padded_fills"]["shape"]
+    m, n, k, off = shp["m"], shp["n"], shp["k"], shp["offset"]
+    for ta in (0, 1):
+        for tb in (0, 1):
+            arrs = [np.frombuffer(bytes.fromhex(fills[(ta, tb, o)]["bits"]), np.float32).copy()
+                    for o in range(3)]
+            lds = [fills[(ta, tb, o)]["ld"] for o in range(3)]
+            A, B, Cd = (torch.from_numpy(x).cuda() for x in arrs)
+            st = device.sgemm(ta, tb, m, n, k, 0.5, A[off:], lds[0], B[off:], lds[1], 1.5,
+                              Cd[off:], lds[2], path=TF32X3)
+            assert st == 0
+            out = Cd.cpu().numpy()
+            ref = oracle.gemm(ta, tb, m, n, k, 0.5, arrs[0][off:], lds[0], arrs[1][off:], lds[1],
+                              1.5, arrs[2][off:], lds[2])
+            body = np.stack([out[off + j * lds[2]: off + j * lds[2] + m] for j in range(n)])
+            assert reference_criterion(body, ref)
