@@ -5,7 +5,8 @@ Workload (the metric's single-GPU configuration): column-majo
 SGEMM M=8192 N=6144 K=4096, op(A)=T, op(B)=N, alpha=0.5, beta=1.5, A/B/C uniform[-1,1)
 from seeds 10/11/12 (synthetic; no dataset).  N GPUs run one such problem each (weak
 scaling: the C rows of the N-GPU job are split by rank, every rank owns an 8192-row
-block and its A rows; B is per rank in this version -- replicas, no collective).
+block and its A rows; B is shared: the kernel-only leg keeps a copy per GPU, the sharded
+end-to-end leg reads 1/N of B per rank from the host and all-gathers it over NVLink).
 
   value   kernel-only TFLOP/s: the sm_100a SGEMM kernel on HBM-resident operands,
           K launches timed with CUDA events on the launching stream, max over ranks.
@@ -16,8 +17,8 @@ block and its A rows; B is per rank in this version -- replicas, no collective).
   roofline  achieved kernel TFLOP/s against the FP32 (FFMA) pipe peak measured in the
           same run by xvram_b200_ffma_probe; `traffic` comes from the committed ncu
           summary profiles/sgemm_ffma_c2_traffic.json when present.
-  host_link  pinned H2D/D2H GB/s measured here; the e2e roofline is
-          max(FLOP / P_fp32, operand bytes / BW_host) per BASELINE.md.
+  host_link  pinned H2D/D2H GB/s measured here with every rank copying at once; the e2e
+          roofline is max(FLOP / P_fp32, operand bytes / BW_host).
   cpu_baseline  the reference's CPU FP64 GEMM (reference_result, compiled from the
           reference sources into oracle/_ref) -- or the oracle port when that build is
           absent -- timed on a bounded sample on all host cores.
@@ -299,23 +300,28 @@ def measured_tf32_peak():
         return 1590.0 / 2.0  # fallback figure of the profiling recipe (bf16 1.59 PFLOP/s)
 
 
-def measure_link(dev, stream) -> tuple[float, float]:
-    """Pinned H2D and D2H GB/s (64 MiB copies, best of 4)."""
+def measure_link(dev, stream, barrier) -> tuple[float, float]:
+    """Pinned H2D and D2H GB/s per GPU (256 MiB copies, best of 4), every rank copying at
+    the same time (a barrier before each copy), so shared root complexes show."""
     import torch
-    probe_h = torch.empty(16 << 20, dtype=torch.float32).pin_memory()
-    probe_d = torch.empty(16 << 20, dtype=torch.float32, device=dev)
+    probe_h = torch.empty(64 << 20, dtype=torch.float32).pin_memory()
+    probe_d = torch.empty(64 << 20, dtype=torch.float32, device=dev)
     h2d = d2h = 0.0
     with torch.cuda.stream(stream):
         for _ in range(4):
-            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+            barrier()
             e0.record(stream)
             probe_d.copy_(probe_h, non_blocking=True)
             e1.record(stream)
-            probe_h.copy_(probe_d, non_blocking=True)
+            e1.synchronize()
+            barrier()
             e2.record(stream)
-            e2.synchronize()
+            probe_h.copy_(probe_d, non_blocking=True)
+            e3.record(stream)
+            e3.synchronize()
             h2d = max(h2d, probe_h.nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
-            d2h = max(d2h, probe_h.nbytes / (e1.elapsed_time(e2) * 1e-3) / 1e9)
+            d2h = max(d2h, probe_h.nbytes / (e2.elapsed_time(e3) * 1e-3) / 1e9)
     return h2d, d2h
 
 
@@ -368,7 +374,9 @@ def main_gpu(args) -> None:
     # timed region so both see a warm clock; pinned host-link bandwidth.
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     peak_tflops = measure_ffma_peak(dev, stream)
-    h2d, d2h = measure_link(dev, stream)
+    h2d, d2h = measure_link(dev, stream, barrier)
+    # the job's host link is as slow as its slowest GPU's
+    h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
 
     # ---------------- kernel-only: inputs resident in HBM
     def launch():
@@ -503,9 +511,13 @@ def main_gpu(args) -> None:
 
     h2d_bytes = a_h.nbytes + b_h.nbytes + c_h.nbytes
     d2h_bytes = c_out.nbytes
-    bw_host = h2d  # the H2D link is the e2e bottleneck (D2H is the smaller leg)
-    t_roof = max(FLOP / (peak_tflops * 1e12), h2d_bytes / (h2d * 1e9) + d2h_bytes / (d2h * 1e9))
-    t_roof_overlap = max(FLOP / (peak_tflops * 1e12), (h2d_bytes + d2h_bytes) / (bw_host * 1e9))
+    # e2e roofline per GPU: max(FP32 compute at the measured peak, operand bytes over the
+    # measured pinned H2D bandwidth with every rank copying at once).  Operand bytes are
+    # A + B + C_in + C_out once each; with B shared over NVLink a rank moves 1/N of B.
+    t_compute = FLOP / (peak_tflops * 1e12)
+    t_roof = max(t_compute, h2d_bytes / (h2d * 1e9) + d2h_bytes / (d2h * 1e9))
+    t_roof_overlap = max(t_compute, (h2d_bytes + d2h_bytes) / (h2d * 1e9))
+    t_roof_sharded = max(t_compute, (sh_h2d + sh_d2h) / (h2d * 1e9))
 
     traffic = None
     tfile = ROOT / "profiles" / "sgemm_ffma_c2_traffic.json"
@@ -533,11 +545,15 @@ def main_gpu(args) -> None:
                          "peak_source": "measured FFMA probe (xvram_b200_ffma_probe), this run",
                          "peak_nominal_at_sampled_clock":
                              sms * 128 * 2 * (clocks.summary()["sm_mhz"] or 0) * 1e6 / 1e12},
-            "host_link": {"h2d_gbs": h2d, "d2h_gbs": d2h,
-                          "e2e_link_gbs": (h2d_bytes + d2h_bytes) / e2e_s_max / 1e9,
-                          "e2e_roofline_ms_serial": 1e3 * t_roof,
-                          "e2e_roofline_ms_overlapped": 1e3 * t_roof_overlap,
-                          "e2e_frac_of_roofline": t_roof_overlap / e2e_s_max},
+            "host_link": {"h2d_gbs": h2d, "d2h_gbs": d2h, "concurrent_ranks": world,
+                          "how": "pinned 256 MiB copies, all ranks at once, min over ranks",
+                          "compat_e2e_link_gbs": (h2d_bytes + d2h_bytes) / e2e_s_max / 1e9,
+                          "compat_e2e_roofline_ms_serial": 1e3 * t_roof,
+                          "compat_e2e_roofline_ms": 1e3 * t_roof_overlap,
+                          "compat_e2e_frac_of_roofline": t_roof_overlap / e2e_s_max,
+                          "sharded_e2e_link_gbs": (sh_h2d + sh_d2h) / sharded_s / 1e9,
+                          "sharded_e2e_roofline_ms": 1e3 * t_roof_sharded,
+                          "sharded_e2e_frac_of_roofline": t_roof_sharded / sharded_s},
             "e2e": (
                 {"value": FLOP / e2e_s_max / 1e12, "unit": "TFLOP/s",
                  "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
@@ -555,6 +571,7 @@ def main_gpu(args) -> None:
             "e2e_sharded": {"value": world * FLOP / sharded_s / 1e12, "unit": "TFLOP/s",
                             "ms_per_step": 1e3 * sharded_s, "h2d_bytes_per_step": sh_h2d,
                             "d2h_bytes_per_step": sh_d2h, "panel_k": 1024,
+                            "frac_of_roofline": t_roof_sharded / sharded_s,
                             "path": "xvram_b200_sgemm_sharded (copies overlap compute)"},
             # per step: the SGEMM kernel plus one transpose per K-major operand (TN: 2)
             "tf32x3": {

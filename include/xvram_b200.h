@@ -180,11 +180,16 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_destroy(uint64_t g
  * C_local = alpha * op(A_local) * op(B) + beta * C_local for this rank's m_local rows of C,
  * all operands in (preferably page-locked) host memory, column-major.  A_local holds this
  * rank's rows of op(A) (m_local x k for op N, k x m_local for op T); B is the whole
- * matrix on every rank, but each rank copies only a 1/world slice of every K panel to
- * its GPU and the slices are all-gathered over NVLink.  K is processed in panels of
- * `panel_k` (0 = 1024) with copies and the all-gather of the next panel overlapping the
- * current panel's kernel.  Blocking; every wait is bounded (TIMEOUT after 60 s without
- * progress, after which the group is unusable and returns POISONED).
+ * matrix on every rank, but each rank copies only a 1/world slice of each block of B to
+ * its GPU and the slices are all-gathered over NVLink.  A_local is kept resident in HBM
+ * (in row groups when it does not fit next to the other buffers), arriving in K panels of
+ * `panel_k` (0 = 1024) so the first kernel starts after the first panel; C is processed in
+ * column blocks whose copies in and out overlap the neighbouring blocks' kernels.  Ranks
+ * may pass different m_local (0 included); the call agrees on one plan first.  Blocking;
+ * every wait is bounded (TIMEOUT after 60 s without progress, after which the group is
+ * unusable and returns POISONED).  Tuning (environment, read per call; the same on every
+ * rank): XVRAM_B200_SHARD_BLOCK_N = C block width (default 1024),
+ * XVRAM_B200_SHARD_BUDGET_BYTES = cap on the device memory the call may use.
  */
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
     uint64_t group, uint32_t op_a, uint32_t op_b, int64_t m_local, int64_t n, int64_t k,

@@ -32,6 +32,12 @@ cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, 
 bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
                         long long ldb);
 
+// dst (cols x rows, column-major, ldd) = src^T (src: rows x cols, column-major, lds), on
+// `stream`.  Moves values only; used to bring K-major operands into the M/N-major form
+// the kernel reads fastest.
+cudaError_t transpose_f32_async(const float* src, long long lds, float* dst, long long ldd,
+                                int rows, int cols, cudaStream_t stream);
+
 // Three-term TF32 tensor-core GEMM (tcgen05 + TMEM), FP32-accurate within the path's
 // tolerance but not bit-identical to the FFMA kernel.  Needs sgemm_tf32x3_workspace_bytes
 // of 256-byte-aligned scratch for the split hi/lo operands; k must be positive.

@@ -587,6 +587,13 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
                   : launch_tn<8>(a_kmajor, b_kmajor, ta, tb, p, stream);
 }
 
+cudaError_t transpose_f32_async(const float* src, long long lds, float* dst, long long ldd,
+                                int rows, int cols, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0)
+    return cudaSuccess;
+  return launch_transpose(src, lds, dst, ldd, rows, cols, stream);
+}
+
 cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream) {
   unsigned int zero = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(out, xvram_kernel_error, sizeof(unsigned int), 0,
