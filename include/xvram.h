@@ -15,6 +15,9 @@
  *   reference include/xvram/xvram.h:111-150 session configuration and its defaults
  *   reference include/xvram/xvram.h:314-318 matrix operation constants
  *   reference include/xvram/xvram.h:411-457 session telemetry
+ *   reference include/xvram/xvram.h:152-410 SDK v1: allocations, access ranges,
+ *                                            prefetch, transactions, operations, GEMM
+ *   reference include/xvram/xvram.h:459-533 the SDK v1 function table, xvram_get_api
  *
  * Convention: every public structure begins with struct_size, which the caller
  * sets to sizeof() of the structure it was compiled against; the library rejects
@@ -140,9 +143,230 @@ typedef struct xvram_session_config_v1 {
    UINT64_C(67108864), UINT64_C(0), UINT64_C(536870912), UINT64_C(4194304), UINT64_C(100),       \
    UINT64_C(0), 4U, XVRAM_CACHE_POLICY_CLOCK, 2U, 0U, {0, 0, 0, 0}}
 
-/* Operation applied to a stored column-major matrix before the product. */
+/* ------------------------------------------------------------------ SDK v1 objects */
+
+/* Opaque handles of the SDK v1 (xvram_get_api). */
+typedef struct xvram_session_t* xvram_session;
+typedef struct xvram_allocation_t* xvram_allocation;
+typedef struct xvram_operation_t* xvram_operation;
+typedef struct xvram_gemm_plan_t* xvram_gemm_plan;
+
+/* Allocation priorities are accepted and reported; eviction does not use them. */
+typedef uint32_t xvram_allocation_priority;
+enum { XVRAM_ALLOCATION_NORMAL = 0, XVRAM_ALLOCATION_HOT = 1, XVRAM_ALLOCATION_STREAMING = 2 };
+
+/* Bytes never written read as zero, on the host and on the device. */
+enum { XVRAM_ALLOCATION_FLAG_ZERO_INITIALIZE = UINT32_C(1) << 0 };
+
+typedef struct xvram_allocation_desc_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  uint64_t size_bytes;
+  uint64_t alignment_bytes; /* 0 or a power of two dividing the chunk size */
+  xvram_allocation_priority priority;
+  uint32_t reserved0;
+  uint64_t reserved[2];
+} xvram_allocation_desc_v1;
+
+#define XVRAM_ALLOCATION_DESC_V1_INIT                                                            \
+  {(uint32_t)sizeof(xvram_allocation_desc_v1), 0U, UINT64_C(0), UINT64_C(0),                     \
+   XVRAM_ALLOCATION_NORMAL, 0U, {0, 0}}
+
+typedef struct xvram_allocation_info_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  uint64_t allocation_id;
+  uint64_t size_bytes;
+  uint64_t alignment_bytes;
+  xvram_allocation_priority priority;
+  uint32_t stable_virtual_address; /* 1: the device address never changes */
+  uint64_t reserved[2];
+} xvram_allocation_info_v1;
+
+typedef uint32_t xvram_access_mode;
+enum { XVRAM_ACCESS_READ = 0, XVRAM_ACCESS_READ_WRITE = 1, XVRAM_ACCESS_WRITE_ONLY = 2 };
+
+/* A byte range of an allocation that a prefetch or transaction touches. */
+typedef struct xvram_access_range_v1 {
+  xvram_allocation allocation;
+  uint64_t offset_bytes;
+  uint64_t length_bytes;
+  xvram_access_mode mode;
+  uint32_t reserved0;
+} xvram_access_range_v1;
+
+typedef struct xvram_prefetch_desc_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  const xvram_access_range_v1* ranges;
+  uint64_t range_count;
+  uint64_t deadline_ms; /* after submission; 0 = none */
+  uint64_t reserved[2];
+} xvram_prefetch_desc_v1;
+
+/* A range once resident: device_address is where offset_bytes lives in device memory. */
+typedef struct xvram_resolved_range_v1 {
+  uint64_t allocation_id;
+  uint64_t offset_bytes;
+  uint64_t length_bytes;
+  uint64_t device_address;
+  xvram_access_mode mode;
+  uint32_t reserved0;
+} xvram_resolved_range_v1;
+
+typedef struct xvram_transaction_context_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  uint64_t operation_id;
+  uint64_t transaction_id;
+  const xvram_resolved_range_v1* ranges;
+  uint64_t range_count;
+  uint64_t workspace_device_address;
+  uint64_t workspace_bytes;
+  uint64_t native_stream; /* the cudaStream_t to enqueue on */
+  uint64_t reserved[2];
+} xvram_transaction_context_v1;
+
+/* Runs on the session's worker thread with the session's device current.  It may only
+ * enqueue work on context->native_stream (no synchronisation, no context change) and must
+ * not keep any address from the context after it returns.  A status other than SUCCESS
+ * fails the operation; callback_error may describe why. */
+typedef xvram_status(XVRAM_CALL* xvram_transaction_callback_v1)(
+    const xvram_transaction_context_v1* context, void* user_data,
+    xvram_error_info_v1* callback_error);
+
+typedef struct xvram_transaction_desc_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  const xvram_access_range_v1* ranges;
+  uint64_t range_count;
+  uint64_t workspace_bytes; /* at most the session's workspace_cap_bytes */
+  uint64_t deadline_ms;     /* after submission; 0 = none */
+  xvram_transaction_callback_v1 callback;
+  void* user_data;
+  uint64_t reserved[2];
+} xvram_transaction_desc_v1;
+
+typedef uint32_t xvram_operation_state;
+enum {
+  XVRAM_OPERATION_QUEUED = 0,
+  XVRAM_OPERATION_RUNNING = 1,
+  XVRAM_OPERATION_COMPLETED = 2,
+  XVRAM_OPERATION_CANCELLED = 3,
+  XVRAM_OPERATION_FAILED = 4
+};
+
+typedef struct xvram_operation_info_v1 {
+  uint32_t struct_size;
+  xvram_operation_state state;
+  xvram_status result;
+  uint32_t reserved0;
+  uint64_t operation_id;
+  uint64_t units_completed;
+  uint64_t units_total;
+  double elapsed_ms;
+  uint64_t bytes_h2d;
+  uint64_t bytes_d2h;
+  uint64_t cache_hits;
+  uint64_t cache_misses;
+  uint64_t reserved[2];
+} xvram_operation_info_v1;
+
+#define XVRAM_OPERATION_INFO_V1_INIT                                                             \
+  {(uint32_t)sizeof(xvram_operation_info_v1), XVRAM_OPERATION_QUEUED, XVRAM_STATUS_SUCCESS, 0U,  \
+   UINT64_C(0), UINT64_C(0), UINT64_C(0), 0.0, UINT64_C(0), UINT64_C(0), UINT64_C(0),            \
+   UINT64_C(0), {0, 0}}
+
+/* Element types.  This implementation computes FP32 only; the others are UNSUPPORTED. */
+typedef uint32_t xvram_data_type;
+enum { XVRAM_DATA_FP16 = 0, XVRAM_DATA_BF16 = 1, XVRAM_DATA_FP32 = 2, XVRAM_DATA_FP64 = 3 };
+
+/* AUTO and FP32_STRICT: every product and sum an FP32 FFMA.  FP32_TF32: tensor cores,
+ * as the three-term TF32 kernel (FP32-accurate within max|err| / (K max|a| max|b|) <= 1e-6,
+ * tighter than single-pass TF32).  FP64: UNSUPPORTED. */
+typedef uint32_t xvram_compute_mode;
+enum {
+  XVRAM_COMPUTE_AUTO = 0,
+  XVRAM_COMPUTE_FP32_STRICT = 1,
+  XVRAM_COMPUTE_FP32_TF32 = 2,
+  XVRAM_COMPUTE_FP64 = 3
+};
+
+typedef uint32_t xvram_matrix_layout;
+enum { XVRAM_MATRIX_ROW_MAJOR = 0, XVRAM_MATRIX_COLUMN_MAJOR = 1 };
+
+/* Operation applied to a stored matrix before the product. */
 typedef uint32_t xvram_matrix_operation;
 enum { XVRAM_MATRIX_OP_N = 0, XVRAM_MATRIX_OP_T = 1 };
+
+/* A rows x columns matrix (before its operation) at offset_bytes of an allocation. */
+typedef struct xvram_matrix_v1 {
+  uint32_t struct_size;
+  xvram_data_type data_type;
+  xvram_allocation allocation;
+  uint64_t offset_bytes;
+  uint64_t rows;
+  uint64_t columns;
+  uint64_t leading_dimension;
+  xvram_matrix_layout layout;
+  uint32_t reserved0;
+  uint64_t reserved[2];
+} xvram_matrix_v1;
+
+#define XVRAM_MATRIX_V1_INIT                                                                     \
+  {(uint32_t)sizeof(xvram_matrix_v1), XVRAM_DATA_FP32, (xvram_allocation)0, UINT64_C(0),          \
+   UINT64_C(0), UINT64_C(0), UINT64_C(0), XVRAM_MATRIX_ROW_MAJOR, 0U, {0, 0}}
+
+/* C = alpha op(A) op(B) + beta C.  Tile hints are accepted and ignored: the panel
+ * planner chooses the geometry from the device budget and the transfer volume. */
+typedef struct xvram_gemm_desc_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  xvram_matrix_v1 a;
+  xvram_matrix_v1 b;
+  xvram_matrix_v1 c;
+  xvram_matrix_operation operation_a;
+  xvram_matrix_operation operation_b;
+  xvram_compute_mode compute_mode;
+  uint32_t reserved0;
+  double alpha;
+  double beta;
+  uint64_t workspace_cap_bytes;
+  uint64_t deadline_ms; /* after submission; 0 = none */
+  uint64_t tile_m_hint;
+  uint64_t tile_n_hint;
+  uint64_t tile_k_hint;
+  uint64_t reserved[3];
+} xvram_gemm_desc_v1;
+
+#define XVRAM_GEMM_DESC_V1_INIT                                                                  \
+  {(uint32_t)sizeof(xvram_gemm_desc_v1), 0U, XVRAM_MATRIX_V1_INIT, XVRAM_MATRIX_V1_INIT,          \
+   XVRAM_MATRIX_V1_INIT, XVRAM_MATRIX_OP_N, XVRAM_MATRIX_OP_N, XVRAM_COMPUTE_AUTO, 0U, 1.0, 0.0,  \
+   UINT64_C(0), UINT64_C(0), UINT64_C(0), UINT64_C(0), UINT64_C(0), {0, 0, 0}}
+
+/* How a plan will run: one in-place launch (tile = the whole problem, tile_count 1) or the
+ * panel schedule's block geometry and step count.  uses_cublas_lt is always 0. */
+typedef struct xvram_gemm_plan_info_v1 {
+  uint32_t struct_size;
+  uint32_t flags;
+  uint64_t m;
+  uint64_t n;
+  uint64_t k;
+  uint64_t tile_m;
+  uint64_t tile_n;
+  uint64_t tile_k;
+  uint64_t maximum_working_set_bytes;
+  uint64_t workspace_bytes;
+  uint64_t tile_count;
+  xvram_compute_mode effective_compute_mode;
+  uint32_t uses_cublas_lt;
+  uint64_t reserved[2];
+} xvram_gemm_plan_info_v1;
+
+#define XVRAM_GEMM_PLAN_INFO_V1_INIT                                                             \
+  {(uint32_t)sizeof(xvram_gemm_plan_info_v1), 0U, UINT64_C(0), UINT64_C(0), UINT64_C(0),          \
+   UINT64_C(0), UINT64_C(0), UINT64_C(0), UINT64_C(0), UINT64_C(0), UINT64_C(0),                 \
+   XVRAM_COMPUTE_AUTO, 0U, {0, 0}}
 
 /* Cumulative counters of the residency layer.  The B200 implementation fills the
  * fields it has an equivalent for and leaves the rest zero: cublas_* (no cuBLAS on
@@ -199,6 +423,81 @@ enum {
   XVRAM_TELEMETRY_STABLE_VIRTUAL_ADDRESSES = 1U << 0U,
   XVRAM_TELEMETRY_NO_PHYSICAL_ALIASES = 1U << 1U
 };
+
+enum {
+  XVRAM_CUBLAS_SOURCE_UNKNOWN = 0,
+  XVRAM_CUBLAS_SOURCE_SYSTEM = 1,
+  XVRAM_CUBLAS_SOURCE_APP_LOCAL = 2,
+  XVRAM_CUBLAS_SOURCE_EXPLICIT = 3
+};
+
+/* ------------------------------------------------------------ SDK v1 function table
+ *
+ * Every session owns a worker thread; operations (prefetch, transaction, GEMM) run on it
+ * in submission order.  Synchronous calls (allocation_*, gemm_plan_create, telemetry) are
+ * queued behind the operations already submitted.  An operation can be cancelled while
+ * it is queued (BUSY once it runs). */
+typedef struct xvram_api_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+
+  const char*(XVRAM_CALL* status_name)(xvram_status status);
+
+  xvram_status(XVRAM_CALL* session_create)(const xvram_session_config_v1* config,
+                                           xvram_session* out_session);
+  xvram_status(XVRAM_CALL* session_get_error)(xvram_session session,
+                                              xvram_error_info_v1* out_error);
+  xvram_status(XVRAM_CALL* session_get_telemetry)(xvram_session session,
+                                                  xvram_session_telemetry_v1* out_telemetry);
+  xvram_status(XVRAM_CALL* session_drain)(xvram_session session, uint64_t timeout_ms);
+  xvram_status(XVRAM_CALL* session_close)(xvram_session session, uint64_t timeout_ms);
+  void(XVRAM_CALL* session_release)(xvram_session session);
+
+  xvram_status(XVRAM_CALL* allocation_create)(xvram_session session,
+                                              const xvram_allocation_desc_v1* desc,
+                                              xvram_allocation* out_allocation);
+  xvram_status(XVRAM_CALL* allocation_get_info)(xvram_allocation allocation,
+                                                xvram_allocation_info_v1* out_info);
+  xvram_status(XVRAM_CALL* allocation_write)(xvram_allocation allocation, uint64_t offset_bytes,
+                                             const void* source, uint64_t size_bytes);
+  xvram_status(XVRAM_CALL* allocation_read)(xvram_allocation allocation, uint64_t offset_bytes,
+                                            void* destination, uint64_t size_bytes);
+  xvram_status(XVRAM_CALL* allocation_release)(xvram_allocation allocation);
+
+  xvram_status(XVRAM_CALL* prefetch_submit)(xvram_session session,
+                                            const xvram_prefetch_desc_v1* desc,
+                                            xvram_operation* out_operation);
+  xvram_status(XVRAM_CALL* transaction_submit)(xvram_session session,
+                                               const xvram_transaction_desc_v1* desc,
+                                               xvram_operation* out_operation);
+  xvram_status(XVRAM_CALL* transaction_execute)(xvram_session session,
+                                                const xvram_transaction_desc_v1* desc,
+                                                uint64_t timeout_ms);
+
+  xvram_status(XVRAM_CALL* gemm_plan_create)(xvram_session session, const xvram_gemm_desc_v1* desc,
+                                             xvram_gemm_plan* out_plan);
+  xvram_status(XVRAM_CALL* gemm_plan_get_info)(xvram_gemm_plan plan,
+                                               xvram_gemm_plan_info_v1* out_info);
+  xvram_status(XVRAM_CALL* gemm_submit)(xvram_gemm_plan plan, xvram_operation* out_operation);
+  xvram_status(XVRAM_CALL* gemm_execute)(xvram_gemm_plan plan, uint64_t timeout_ms);
+  void(XVRAM_CALL* gemm_plan_release)(xvram_gemm_plan plan);
+
+  xvram_status(XVRAM_CALL* operation_poll)(xvram_operation operation,
+                                           xvram_operation_info_v1* out_info);
+  xvram_status(XVRAM_CALL* operation_wait)(xvram_operation operation, uint64_t timeout_ms,
+                                           xvram_operation_info_v1* out_info);
+  xvram_status(XVRAM_CALL* operation_cancel)(xvram_operation operation);
+  xvram_status(XVRAM_CALL* operation_get_error)(xvram_operation operation,
+                                                xvram_error_info_v1* out_error);
+  void(XVRAM_CALL* operation_release)(xvram_operation operation);
+
+  uint64_t reserved[16];
+} xvram_api_v1;
+
+/* Copies the v1 table to out_api (caller_api_size >= sizeof(xvram_api_v1)).  INVALID_ARGUMENT
+ * for a null or short buffer, INCOMPATIBLE_ABI for any version but 1. */
+XVRAM_API xvram_status XVRAM_CALL xvram_get_api(uint32_t requested_abi_version,
+                                                uint32_t caller_api_size, void* out_api);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -196,6 +196,22 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
     float alpha, const float* a, int64_t lda, const float* b, int64_t ldb, float beta, float* c,
     int64_t ldc, int64_t panel_k);
 
+/*
+ * Y = act(Y + bias) over a column-major rows x cols FP32 block on the device (bias: rows
+ * floats, or 0 for none), enqueued on `stream` (a cudaStream_t; 0 = the legacy default
+ * stream).  No reference counterpart: the reference's tiled GEMM takes no bias and its
+ * torch route rejects biased linear layers (reference python/xvram/torch_native.py:
+ * 1913-1921).  Meant for SDK transaction callbacks, which receive the resident addresses
+ * and the stream (xvram_transaction_context_v1), so a caller can run Linear + bias + ReLU
+ * as gemm_execute followed by transaction_execute on the output.
+ */
+enum { XVRAM_B200_ACTIVATION_NONE = 0, XVRAM_B200_ACTIVATION_RELU = 1 };
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_bias_activation(uint64_t y, int64_t ldy,
+                                                                 int64_t rows, int64_t cols,
+                                                                 uint64_t bias,
+                                                                 uint32_t activation,
+                                                                 uint64_t stream);
+
 /* Extra state of the compat adapter's runtime (not in the reference telemetry). */
 typedef struct xvram_b200_runtime_info_v1 {
   uint32_t struct_size;

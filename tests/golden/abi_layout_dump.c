@@ -1,4 +1,4 @@
-/* Prints the binary layout of the v1 compat ABI as JSON: sizeof and offsetof of every
+/* Prints the binary layout of the v1 compat and SDK ABIs as JSON: sizeof and offsetof of every
  * field, enumerator values, and the bytes of the *_INIT default initialisers.
  * Compiled against the reference headers (XVRAM_DUMP_REFERENCE, by make_abi_layout.py)
  * and against include/ (by tests/test_abi_layout.py); the two outputs must match. */
@@ -92,6 +92,102 @@ int main(void) {
   OF(T, blas_get_stream); OF(T, blas_set_pointer_mode); OF(T, blas_get_pointer_mode);
   OF(T, blas_set_math_mode); OF(T, blas_get_math_mode); OF(T, blas_sgemm); OF(T, reserved);
 #undef T
+
+  /* SDK v1 (xvram_get_api) */
+  SZ(xvram_allocation_desc_v1);
+#define T xvram_allocation_desc_v1
+  OF(T, struct_size); OF(T, flags); OF(T, size_bytes); OF(T, alignment_bytes); OF(T, priority);
+  OF(T, reserved0); OF(T, reserved);
+#undef T
+  SZ(xvram_allocation_info_v1);
+#define T xvram_allocation_info_v1
+  OF(T, struct_size); OF(T, flags); OF(T, allocation_id); OF(T, size_bytes); OF(T, alignment_bytes);
+  OF(T, priority); OF(T, stable_virtual_address); OF(T, reserved);
+#undef T
+  SZ(xvram_access_range_v1);
+#define T xvram_access_range_v1
+  OF(T, allocation); OF(T, offset_bytes); OF(T, length_bytes); OF(T, mode); OF(T, reserved0);
+#undef T
+  SZ(xvram_prefetch_desc_v1);
+#define T xvram_prefetch_desc_v1
+  OF(T, struct_size); OF(T, flags); OF(T, ranges); OF(T, range_count); OF(T, deadline_ms);
+  OF(T, reserved);
+#undef T
+  SZ(xvram_resolved_range_v1);
+#define T xvram_resolved_range_v1
+  OF(T, allocation_id); OF(T, offset_bytes); OF(T, length_bytes); OF(T, device_address);
+  OF(T, mode); OF(T, reserved0);
+#undef T
+  SZ(xvram_transaction_context_v1);
+#define T xvram_transaction_context_v1
+  OF(T, struct_size); OF(T, flags); OF(T, operation_id); OF(T, transaction_id); OF(T, ranges);
+  OF(T, range_count); OF(T, workspace_device_address); OF(T, workspace_bytes);
+  OF(T, native_stream); OF(T, reserved);
+#undef T
+  SZ(xvram_transaction_desc_v1);
+#define T xvram_transaction_desc_v1
+  OF(T, struct_size); OF(T, flags); OF(T, ranges); OF(T, range_count); OF(T, workspace_bytes);
+  OF(T, deadline_ms); OF(T, callback); OF(T, user_data); OF(T, reserved);
+#undef T
+  SZ(xvram_operation_info_v1);
+#define T xvram_operation_info_v1
+  OF(T, struct_size); OF(T, state); OF(T, result); OF(T, reserved0); OF(T, operation_id);
+  OF(T, units_completed); OF(T, units_total); OF(T, elapsed_ms); OF(T, bytes_h2d); OF(T, bytes_d2h);
+  OF(T, cache_hits); OF(T, cache_misses); OF(T, reserved);
+#undef T
+  SZ(xvram_matrix_v1);
+#define T xvram_matrix_v1
+  OF(T, struct_size); OF(T, data_type); OF(T, allocation); OF(T, offset_bytes); OF(T, rows);
+  OF(T, columns); OF(T, leading_dimension); OF(T, layout); OF(T, reserved0); OF(T, reserved);
+#undef T
+  SZ(xvram_gemm_desc_v1);
+#define T xvram_gemm_desc_v1
+  OF(T, struct_size); OF(T, flags); OF(T, a); OF(T, b); OF(T, c); OF(T, operation_a);
+  OF(T, operation_b); OF(T, compute_mode); OF(T, reserved0); OF(T, alpha); OF(T, beta);
+  OF(T, workspace_cap_bytes); OF(T, deadline_ms); OF(T, tile_m_hint); OF(T, tile_n_hint);
+  OF(T, tile_k_hint); OF(T, reserved);
+#undef T
+  SZ(xvram_gemm_plan_info_v1);
+#define T xvram_gemm_plan_info_v1
+  OF(T, struct_size); OF(T, flags); OF(T, m); OF(T, n); OF(T, k); OF(T, tile_m); OF(T, tile_n);
+  OF(T, tile_k); OF(T, maximum_working_set_bytes); OF(T, workspace_bytes); OF(T, tile_count);
+  OF(T, effective_compute_mode); OF(T, uses_cublas_lt); OF(T, reserved);
+#undef T
+  SZ(xvram_api_v1);
+#define T xvram_api_v1
+  OF(T, struct_size); OF(T, abi_version); OF(T, status_name); OF(T, session_create);
+  OF(T, session_get_error); OF(T, session_get_telemetry); OF(T, session_drain);
+  OF(T, session_close); OF(T, session_release); OF(T, allocation_create);
+  OF(T, allocation_get_info); OF(T, allocation_write); OF(T, allocation_read);
+  OF(T, allocation_release); OF(T, prefetch_submit); OF(T, transaction_submit);
+  OF(T, transaction_execute); OF(T, gemm_plan_create); OF(T, gemm_plan_get_info);
+  OF(T, gemm_submit); OF(T, gemm_execute); OF(T, gemm_plan_release); OF(T, operation_poll);
+  OF(T, operation_wait); OF(T, operation_cancel); OF(T, operation_get_error);
+  OF(T, operation_release); OF(T, reserved);
+#undef T
+  EN(XVRAM_ALLOCATION_NORMAL); EN(XVRAM_ALLOCATION_HOT); EN(XVRAM_ALLOCATION_STREAMING);
+  EN(XVRAM_ALLOCATION_FLAG_ZERO_INITIALIZE);
+  EN(XVRAM_ACCESS_READ); EN(XVRAM_ACCESS_READ_WRITE); EN(XVRAM_ACCESS_WRITE_ONLY);
+  EN(XVRAM_OPERATION_QUEUED); EN(XVRAM_OPERATION_RUNNING); EN(XVRAM_OPERATION_COMPLETED);
+  EN(XVRAM_OPERATION_CANCELLED); EN(XVRAM_OPERATION_FAILED);
+  EN(XVRAM_DATA_FP16); EN(XVRAM_DATA_BF16); EN(XVRAM_DATA_FP32); EN(XVRAM_DATA_FP64);
+  EN(XVRAM_COMPUTE_AUTO); EN(XVRAM_COMPUTE_FP32_STRICT); EN(XVRAM_COMPUTE_FP32_TF32);
+  EN(XVRAM_COMPUTE_FP64); EN(XVRAM_MATRIX_ROW_MAJOR); EN(XVRAM_MATRIX_COLUMN_MAJOR);
+  EN(XVRAM_CUBLAS_SOURCE_UNKNOWN); EN(XVRAM_CUBLAS_SOURCE_SYSTEM);
+  EN(XVRAM_CUBLAS_SOURCE_APP_LOCAL); EN(XVRAM_CUBLAS_SOURCE_EXPLICIT);
+  {
+    /* none of these structures has padding, so their initialisers' bytes are defined */
+    xvram_allocation_desc_v1 ad = XVRAM_ALLOCATION_DESC_V1_INIT;
+    xvram_operation_info_v1 oi = XVRAM_OPERATION_INFO_V1_INIT;
+    xvram_matrix_v1 mx = XVRAM_MATRIX_V1_INIT;
+    xvram_gemm_desc_v1 gd = XVRAM_GEMM_DESC_V1_INIT;
+    xvram_gemm_plan_info_v1 pi = XVRAM_GEMM_PLAN_INFO_V1_INIT;
+    bytes("xvram_allocation_desc_v1", &ad, sizeof ad);
+    bytes("xvram_operation_info_v1", &oi, sizeof oi);
+    bytes("xvram_matrix_v1", &mx, sizeof mx);
+    bytes("xvram_gemm_desc_v1", &gd, sizeof gd);
+    bytes("xvram_gemm_plan_info_v1", &pi, sizeof pi);
+  }
 
   EN(XVRAM_ABI_VERSION_1); EN(XVRAM_ABI_VERSION_CURRENT); EN(XVRAM_TIMEOUT_INFINITE);
   EN(XVRAM_STATUS_SUCCESS); EN(XVRAM_STATUS_INVALID_ARGUMENT); EN(XVRAM_STATUS_INCOMPATIBLE_ABI);

@@ -30,6 +30,16 @@ def test_library_exports_every_declared_symbol():
     assert {s for s in exported if not s.startswith("xvram_")} == set()
 
 
+def test_sdk_library_exports_only_xvram_get_api():
+    """libxvram.so is the SDK drop-in: like the reference's SDK library it exports
+    xvram_get_api alone, under the version node XVRAM_0.1."""
+    from xvram_b200 import _native
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.SDK_LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == {"xvram_get_api@@XVRAM_0.1"}, exported
+
+
 def test_library_has_no_cuda_runtime_dependency():
     from xvram_b200 import _native
     out = subprocess.run(["ldd", str(_native.LIB_PATH)], capture_output=True, text=True).stdout

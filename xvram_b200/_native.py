@@ -10,6 +10,8 @@ import ctypes as C
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxvram_cuda_compat.so"
+# The same code linked as the SDK drop-in (exports xvram_get_api only).
+SDK_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxvram.so"
 
 u32, u64, i32, i64 = C.c_uint32, C.c_uint64, C.c_int32, C.c_int64
 f32, f64 = C.c_float, C.c_double
@@ -89,6 +91,10 @@ def _load() -> C.CDLL:
     lib.xvram_b200_compat_runtime_info.restype = u32
     lib.xvram_cuda_compat_get_api.argtypes = [u32, u32, vp]
     lib.xvram_cuda_compat_get_api.restype = u32
+    lib.xvram_get_api.argtypes = [u32, u32, vp]
+    lib.xvram_get_api.restype = u32
+    lib.xvram_b200_bias_activation.argtypes = [u64, i64, i64, i64, u64, u32, u64]
+    lib.xvram_b200_bias_activation.restype = u32
     return lib
 
 
@@ -97,6 +103,8 @@ lib = _load()
 # Every symbol include/*.h declares (checked by tests/test_native_load.py).
 EXPORTED = (
     "xvram_cuda_compat_get_api",
+    "xvram_get_api",
+    "xvram_b200_bias_activation",
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",

@@ -22,12 +22,15 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "lib" / "libxvram_cuda_compat.so"
+# The same objects linked as the SDK drop-in: exports xvram_get_api only.
+SDK_LIB = PKG / "lib" / "libxvram.so"
 INCLUDE = ROOT / "include"
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.environ.get("NVCC", f"{CUDA_HOME}/bin/nvcc")
 CXX = os.environ.get("CXX", "g++")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-COMMON = ["-O3", "-DXVRAM_BUILDING_CUDA_COMPAT", f"-I{INCLUDE}", f"-I{CSRC}"]
+COMMON = ["-O3", "-DXVRAM_BUILDING_CUDA_COMPAT", "-DXVRAM_BUILDING_LIBRARY", f"-I{INCLUDE}",
+          f"-I{CSRC}"]
 
 
 def _sources():
@@ -69,10 +72,12 @@ def build(verbose: bool = False) -> Path:
             print(" ".join(cmd))
         _run(cmd)
     newest = max(o.stat().st_mtime for o in objs)
-    if not LIB.exists() or LIB.stat().st_mtime < newest:
+    for lib, script in ((LIB, "exports.map"), (SDK_LIB, "sdk.exports.map")):
+        if lib.exists() and lib.stat().st_mtime >= max(newest, (CSRC / script).stat().st_mtime):
+            continue
         cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC",
-               f"-Xlinker=--version-script={CSRC / 'exports.map'}", "-Xlinker=--no-undefined",
-               *map(str, objs), "-o", str(LIB), "-lpthread", "-ldl", "-lrt"]
+               f"-Xlinker=--version-script={CSRC / script}", "-Xlinker=--no-undefined",
+               *map(str, objs), "-o", str(lib), "-lpthread", "-ldl", "-lrt"]
         if verbose:
             print(" ".join(cmd))
         _run(cmd)
@@ -86,8 +91,9 @@ def main() -> None:
     a = ap.parse_args()
     if a.clean:
         shutil.rmtree(BUILD, ignore_errors=True)
-        if LIB.exists():
-            LIB.unlink()
+        for lib in (LIB, SDK_LIB):
+            if lib.exists():
+                lib.unlink()
     print(build(a.verbose))
 
 

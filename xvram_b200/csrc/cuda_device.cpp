@@ -324,6 +324,8 @@ public:
     return {};
   }
 
+  uint64_t native_stream(StreamId s) override { return reinterpret_cast<uint64_t>(stream(s)); }
+
 private:
   static CUmemAllocationProp alloc_prop_for(int ordinal) {
     CUmemAllocationProp p{};

@@ -80,6 +80,8 @@ public:
                                    bool tensor_cores) = 0;
   // Reads and clears the sticky error word of the library's kernels (synchronising s).
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
+  // The native handle of stream s (a cudaStream_t) handed to transaction callbacks.
+  virtual uint64_t native_stream(StreamId s) = 0;
 };
 
 using DeviceFactory = std::unique_ptr<Device> (*)();

@@ -32,6 +32,7 @@ struct Alloc {
   void* host = nullptr;
   std::vector<Chunk> chunks;
   bool live = true;
+  bool zero_fill = false; // never-written bytes read as zero (host and device)
 };
 
 struct Frame {
@@ -40,8 +41,10 @@ struct Frame {
   uint32_t chunk = 0;
   uint64_t touch = 0;
   EventId last_use = 0;
+  EventId ready = 0;      // recorded on the H2D stream after the frame's last upload
   bool used = false;      // has held data before (the next owner is a handle reuse)
   bool pending = false;   // last_use has been recorded
+  bool uploading = false; // ready has been recorded and not yet observed complete
 };
 
 } // namespace
@@ -95,6 +98,8 @@ struct Runtime::Impl {
     void* p = nullptr;
     if (Error e = dev->host_alloc(a.bytes, &p))
       return e;
+    if (a.zero_fill)
+      std::memset(p, 0, a.bytes);
     a.host = p;
     x.host_backing_bytes += a.bytes;
     x.host_backing_peak_bytes = std::max(x.host_backing_peak_bytes, x.host_backing_bytes);
@@ -102,12 +107,45 @@ struct Runtime::Impl {
     return {};
   }
 
+  // Waits until the device is done with frame f: its last kernel use and its last upload.
   Error wait_idle(Frame& f) {
     if (f.pending) {
       if (Error e = dev->event_sync(f.last_use))
         return e;
       f.pending = false;
       ++t.event_boundaries;
+    }
+    if (f.uploading) {
+      if (Error e = dev->event_sync(f.ready))
+        return e;
+      f.uploading = false;
+    }
+    return {};
+  }
+
+  Error new_frame(Frame* f) {
+    if (Error e = dev->handle_create(cb, &f->handle))
+      return e;
+    if (Error e = dev->event_create(&f->last_use)) {
+      dev->handle_release(f->handle);
+      return e;
+    }
+    if (Error e = dev->event_create(&f->ready)) {
+      dev->event_destroy(f->last_use);
+      dev->handle_release(f->handle);
+      return e;
+    }
+    ++t.physical_handles_created;
+    return {};
+  }
+
+  // Makes stream s wait for every upload still in flight into the chunks of `keep`.
+  Error await_uploads(const std::set<std::pair<uint64_t, uint32_t>>& keep, StreamId s) {
+    for (const auto& [id, c] : keep) {
+      const int32_t fi = allocs.at(id).chunks[c].frame;
+      if (fi >= 0 && frames[static_cast<size_t>(fi)].uploading)
+        if (Error e = dev->stream_wait_event(s, frames[static_cast<size_t>(fi)].ready))
+          return e;
     }
     return {};
   }
@@ -162,13 +200,8 @@ struct Runtime::Impl {
     }
     if (frames.size() < capacity) {
       Frame f;
-      if (Error e = dev->handle_create(cb, &f.handle))
+      if (Error e = new_frame(&f))
         return e;
-      if (Error e = dev->event_create(&f.last_use)) {
-        dev->handle_release(f.handle);
-        return e;
-      }
-      ++t.physical_handles_created;
       frames.push_back(f);
       *out = frames.size() - 1;
       return {};
@@ -228,6 +261,18 @@ struct Runtime::Impl {
       t.bytes_h2d += len;
       ch.dev_valid = true;
       *uploaded = true;
+      if (Error e = dev->event_record(f.ready, s_h2d))
+        return e;
+      f.uploading = true;
+    } else if (!ch.written && a.zero_fill) {
+      // A reused frame holds someone else's bytes: zero it (on the H2D stream, so a
+      // partial write that follows lands on top).
+      if (Error e = dev->memset_d32(a.va + off, 0, cb / 4, s_h2d))
+        return e;
+      *uploaded = true;
+      if (Error e = dev->event_record(f.ready, s_h2d))
+        return e;
+      f.uploading = true;
     }
     update_resident();
     return {};
@@ -252,6 +297,53 @@ struct Runtime::Impl {
   Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
                       const std::set<std::pair<uint64_t, uint32_t>>& keep, uint64_t ws);
   Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
+  void gemm_chunks(const GemmCall& call, std::set<std::pair<uint64_t, uint32_t>>* keep,
+                   uint64_t* ws, bool* in_place);
+  PlanLimits streamed_limits(const GemmCall& call) const;
+  static PlanProblem plan_problem(const GemmCall& call);
+
+  // The chunks [offset, offset + length) of allocation `a` covers.
+  void range_chunks(const Alloc& a, uint64_t offset, uint64_t length,
+                    std::set<std::pair<uint64_t, uint32_t>>* keep) const {
+    for (uint64_t c = offset / cb; c <= (offset + length - 1) / cb; ++c)
+      keep->insert({a.id, static_cast<uint32_t>(c)});
+  }
+  Error check_ranges(const std::vector<AccessRange>& ranges, const char* op) const {
+    for (const AccessRange& r : ranges) {
+      auto it = allocs.find(r.allocation_id);
+      if (it == allocs.end() || !it->second.live || r.allocation_id == kScratchId)
+        return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "residency", op, "unknown allocation");
+      if (r.length_bytes == 0 || r.offset_bytes > it->second.bytes ||
+          r.length_bytes > it->second.bytes - r.offset_bytes || r.mode < 0 || r.mode > 2)
+        return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "residency", op,
+                          "access range lies outside its allocation");
+    }
+    return {};
+  }
+  // Whether chunk c needs its current contents on the device for `ranges`: anything but
+  // write-only ranges that cover the whole chunk.
+  bool chunk_needs_upload(const Alloc& a, uint32_t c, const std::vector<AccessRange>& ranges) const {
+    const uint64_t cbeg = static_cast<uint64_t>(c) * cb, cend = cbeg + chunk_len(a, c);
+    for (const AccessRange& r : ranges) {
+      if (r.allocation_id != a.id || r.offset_bytes >= cend ||
+          r.offset_bytes + r.length_bytes <= cbeg)
+        continue;
+      if (r.mode != 2)
+        return true;
+    }
+    uint64_t covered_to = cbeg; // write-only ranges: is the chunk covered completely?
+    bool progress = true;
+    while (progress && covered_to < cend) {
+      progress = false;
+      for (const AccessRange& r : ranges)
+        if (r.allocation_id == a.id && r.offset_bytes <= covered_to &&
+            r.offset_bytes + r.length_bytes > covered_to) {
+          covered_to = r.offset_bytes + r.length_bytes;
+          progress = true;
+        }
+    }
+    return covered_to < cend;
+  }
 };
 
 Runtime::Runtime() : impl_(std::make_unique<Impl>()) {}
@@ -352,6 +444,7 @@ Error Runtime::close() {
     keep(m.dev->handle_release(f.handle));
     ++m.t.physical_handles_released;
     keep(m.dev->event_destroy(f.last_use));
+    keep(m.dev->event_destroy(f.ready));
   }
   m.frames.clear();
   for (EventId e : m.event_pool)
@@ -363,13 +456,14 @@ Error Runtime::close() {
   return first;
 }
 
-Error Runtime::allocate(uint64_t bytes, uint64_t* id, uint64_t* va) {
+Error Runtime::allocate(uint64_t bytes, uint64_t* id, uint64_t* va, bool zero_fill) {
   Impl& m = *impl_;
   if (bytes == 0 || bytes > UINT64_MAX - m.cb)
     return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "runtime", "allocate", "invalid size");
   Alloc a;
   a.id = m.next_id++;
   a.bytes = bytes;
+  a.zero_fill = zero_fill;
   a.reserved = round_up(bytes, m.cb);
   if (Error e = m.dev->va_reserve(a.reserved, &a.va))
     return e;
@@ -494,6 +588,13 @@ Error Runtime::read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes) {
     return e;
   if (Error e = m.dev->stream_wait_event(m.s_d2h, m.e_a))
     return e;
+  // Chunks still being uploaded (a prefetch) are read after their upload.
+  for (uint64_t c = offset / m.cb; c <= (end - 1) / m.cb; ++c) {
+    const int32_t fi = a.chunks[static_cast<size_t>(c)].frame;
+    if (fi >= 0 && m.frames[static_cast<size_t>(fi)].uploading)
+      if (Error e = m.dev->stream_wait_event(m.s_d2h, m.frames[static_cast<size_t>(fi)].ready))
+        return e;
+  }
   uint64_t pos = offset;
   while (pos < end) {
     const uint32_t c = static_cast<uint32_t>(pos / m.cb);
@@ -549,6 +650,89 @@ Error Runtime::mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes) {
   return {};
 }
 
+// The chunks an in-place GEMM pins (operands, then kernel workspace from the scratch
+// pseudo-allocation) and the workspace bytes; in_place says whether they fit the pool.
+void Runtime::Impl::gemm_chunks(const GemmCall& call, std::set<std::pair<uint64_t, uint32_t>>* keep,
+                                uint64_t* ws, bool* in_place) {
+  const MatrixRef* mats[3] = {&call.shape.a, &call.shape.b, &call.shape.c};
+  for (int i = 0; i < 3; ++i) {
+    uint64_t b = 0, e = 0;
+    matrix_byte_span(*mats[i], &b, &e);
+    for (uint64_t c = b / cb; c <= (e - 1) / cb; ++c)
+      keep->insert({mats[i]->allocation_id, static_cast<uint32_t>(c)});
+  }
+  // The kernel's canonicalisation workspace comes out of the same frame budget.
+  const GemmShape& sh = call.shape;
+  *ws = dev->sgemm_workspace(sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
+                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k),
+                             call.tensor_cores);
+  const uint64_t ws_chunks = (*ws + cb - 1) / cb;
+  const size_t data_chunks = keep->size();
+  for (uint64_t c = 0; c < ws_chunks && c < capacity; ++c)
+    keep->insert({kScratchId, static_cast<uint32_t>(c)});
+  *in_place = data_chunks + ws_chunks <= capacity;
+}
+
+PlanLimits Runtime::Impl::streamed_limits(const GemmCall& call) const {
+  const GemmShape& s = call.shape;
+  PlanLimits lim;
+  lim.budget_bytes = capacity * cb;
+  lim.quantum_bytes = cb;
+  lim.flops_per_s = call.flops_per_s > 0 ? call.flops_per_s : cfg.flops_per_s;
+  lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
+  lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
+  lim.transpose_a = !call.tensor_cores && s.op_a != 0;
+  lim.transpose_b = !call.tensor_cores && s.op_b == 0;
+  lim.tf32x3 = call.tensor_cores;
+  return lim;
+}
+
+PlanProblem Runtime::Impl::plan_problem(const GemmCall& call) {
+  const GemmShape& s = call.shape;
+  PlanProblem pp;
+  pp.op_a = s.op_a;
+  pp.op_b = s.op_b;
+  pp.m = static_cast<int64_t>(s.m);
+  pp.n = static_cast<int64_t>(s.n);
+  pp.k = static_cast<int64_t>(s.k);
+  pp.beta_nonzero = call.beta != 0.0f;
+  return pp;
+}
+
+Error Runtime::describe_gemm(const GemmCall& call, GemmLayout* out) {
+  Impl& m = *impl_;
+  std::set<std::pair<uint64_t, uint32_t>> keep;
+  uint64_t ws = 0;
+  bool in_place = false;
+  m.gemm_chunks(call, &keep, &ws, &in_place);
+  *out = GemmLayout{};
+  if (in_place) {
+    out->in_place = true;
+    out->tile_m = call.shape.m;
+    out->tile_n = call.shape.n;
+    out->tile_k = call.shape.k;
+    out->tiles = 1;
+    out->working_set_bytes = keep.size() * m.cb;
+    out->workspace_bytes = ws;
+    return {};
+  }
+  Plan plan;
+  const PlanStatus ps = make_panel_plan(Impl::plan_problem(call), m.streamed_limits(call), &plan);
+  if (ps != PlanStatus::ok)
+    return make_error(ps == PlanStatus::budget_too_small ? XVRAM_STATUS_BUDGET_PRESSURE
+                                                         : XVRAM_STATUS_INVALID_ARGUMENT,
+                      "planner", "make_panel_plan", "no panel geometry fits the device budget");
+  out->tile_m = static_cast<uint64_t>(plan.mb);
+  out->tile_n = static_cast<uint64_t>(plan.nb);
+  out->tile_k = static_cast<uint64_t>(plan.kb);
+  out->tiles = plan.steps.size();
+  out->working_set_bytes = plan.slot_bytes * static_cast<uint64_t>(plan.panel_slots) +
+                           plan.c_slot_bytes * static_cast<uint64_t>(plan.c_slots) +
+                           plan.workspace_bytes;
+  out->workspace_bytes = plan.workspace_bytes;
+  return {};
+}
+
 Error Runtime::gemm(const GemmCall& call) {
   Impl& m = *impl_;
   const auto t0 = std::chrono::steady_clock::now();
@@ -556,25 +740,10 @@ Error Runtime::gemm(const GemmCall& call) {
   Alloc& B = m.allocs.at(call.shape.b.allocation_id);
   Alloc& C = m.allocs.at(call.shape.c.allocation_id);
   std::set<std::pair<uint64_t, uint32_t>> keep;
-  const MatrixRef* mats[3] = {&call.shape.a, &call.shape.b, &call.shape.c};
-  Alloc* owners[3] = {&A, &B, &C};
-  for (int i = 0; i < 3; ++i) {
-    uint64_t b = 0, e = 0;
-    matrix_byte_span(*mats[i], &b, &e);
-    for (uint64_t c = b / m.cb; c <= (e - 1) / m.cb; ++c)
-      keep.insert({owners[i]->id, static_cast<uint32_t>(c)});
-  }
-  // The kernel's canonicalisation workspace comes out of the same frame budget.
-  const GemmShape& sh = call.shape;
-  const uint64_t ws = m.dev->sgemm_workspace(sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
-                                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k),
-                                             call.tensor_cores);
-  const uint64_t ws_chunks = (ws + m.cb - 1) / m.cb;
-  const size_t data_chunks = keep.size();
-  for (uint64_t c = 0; c < ws_chunks && c < m.capacity; ++c)
-    keep.insert({kScratchId, static_cast<uint32_t>(c)});
-  Error err = data_chunks + ws_chunks <= m.capacity ? m.gemm_in_place(call, A, B, C, keep, ws)
-                                                    : m.gemm_streamed(call, A, B, C);
+  uint64_t ws = 0;
+  bool in_place = false;
+  m.gemm_chunks(call, &keep, &ws, &in_place);
+  Error err = in_place ? m.gemm_in_place(call, A, B, C, keep, ws) : m.gemm_streamed(call, A, B, C);
   m.x.last_gemm_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   m.t.last_transaction_ms = m.x.last_gemm_ms;
@@ -590,12 +759,10 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   for (const auto& [id, c] : keep)
     if (Error e = make_resident(allocs.at(id), c, true, keep, &uploaded))
       return e;
-  if (uploaded) {
-    if (Error e = dev->event_record(e_a, s_h2d))
-      return e;
-    if (Error e = dev->stream_wait_event(s_compute, e_a))
-      return e;
-  }
+  // Wait only for this GEMM's own chunks: uploads for later operations (prefetches) stay
+  // in flight behind the kernel.
+  if (Error e = await_uploads(keep, s_compute))
+    return e;
   const GemmShape& s = call.shape;
   ++x.tiles_submitted;
   ++x.gemm_in_place;
@@ -642,26 +809,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     if (Error e = ensure_backing(*a))
       return e;
   // 2. Plan against the whole pool.
-  PlanProblem pp;
-  pp.op_a = s.op_a;
-  pp.op_b = s.op_b;
-  pp.m = static_cast<int64_t>(s.m);
-  pp.n = static_cast<int64_t>(s.n);
-  pp.k = static_cast<int64_t>(s.k);
-  pp.beta_nonzero = call.beta != 0.0f;
-  PlanLimits lim;
-  lim.budget_bytes = capacity * cb;
-  lim.quantum_bytes = cb;
-  lim.flops_per_s = cfg.flops_per_s;
-  lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
-  lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
-  lim.transpose_a = !call.tensor_cores && s.op_a != 0;
-  lim.transpose_b = !call.tensor_cores && s.op_b == 0;
-  lim.tf32x3 = call.tensor_cores;
-  if (call.flops_per_s > 0)
-    lim.flops_per_s = call.flops_per_s;
   Plan plan;
-  const PlanStatus ps = make_panel_plan(pp, lim, &plan);
+  const PlanStatus ps = make_panel_plan(plan_problem(call), streamed_limits(call), &plan);
   if (ps != PlanStatus::ok)
     return make_error(ps == PlanStatus::budget_too_small ? XVRAM_STATUS_BUDGET_PRESSURE
                                                          : XVRAM_STATUS_INTERNAL,
@@ -680,13 +829,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
                            fpc * static_cast<uint64_t>(plan.c_slots) + plan.workspace_bytes / cb;
   while (frames.size() < nframes) {
     Frame f;
-    if (Error e = dev->handle_create(cb, &f.handle))
+    if (Error e = new_frame(&f))
       return e;
-    if (Error e = dev->event_create(&f.last_use)) {
-      dev->handle_release(f.handle);
-      return e;
-    }
-    ++t.physical_handles_created;
     frames.push_back(f);
   }
   uint64_t arena = 0;
@@ -883,6 +1027,101 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     ch.backing_valid = true;
     ch.dev_valid = false;
   }
+  return {};
+}
+
+} // namespace xvram
+
+namespace xvram {
+
+bool Runtime::live(uint64_t id) const {
+  auto it = impl_->allocs.find(id);
+  return it != impl_->allocs.end() && it->second.live && id != kScratchId;
+}
+
+uint64_t Runtime::allocation_bytes(uint64_t id) const {
+  auto it = impl_->allocs.find(id);
+  return it == impl_->allocs.end() ? 0 : it->second.bytes;
+}
+
+Error Runtime::prefetch(const std::vector<AccessRange>& ranges) {
+  Impl& m = *impl_;
+  if (Error e = m.check_ranges(ranges, "prefetch"))
+    return e;
+  std::set<std::pair<uint64_t, uint32_t>> keep;
+  for (const AccessRange& r : ranges)
+    m.range_chunks(m.allocs.at(r.allocation_id), r.offset_bytes, r.length_bytes, &keep);
+  if (keep.size() > m.capacity)
+    return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "residency", "prefetch",
+                      "the ranges exceed the device budget");
+  bool uploaded = false;
+  for (const auto& [id, c] : keep) {
+    Alloc& a = m.allocs.at(id);
+    if (Error e = m.make_resident(a, c, m.chunk_needs_upload(a, c, ranges), keep, &uploaded))
+      return e;
+  }
+  return {};
+}
+
+Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t workspace_bytes,
+                           const TransactionBody& body) {
+  Impl& m = *impl_;
+  const auto t0 = std::chrono::steady_clock::now();
+  if (Error e = m.check_ranges(ranges, "transaction"))
+    return e;
+  std::set<std::pair<uint64_t, uint32_t>> keep;
+  for (const AccessRange& r : ranges)
+    m.range_chunks(m.allocs.at(r.allocation_id), r.offset_bytes, r.length_bytes, &keep);
+  const uint64_t ws_chunks = (workspace_bytes + m.cb - 1) / m.cb;
+  if (keep.size() + ws_chunks > m.capacity)
+    return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "residency", "transaction",
+                      "the ranges and workspace exceed the device budget");
+  for (uint64_t c = 0; c < ws_chunks; ++c)
+    keep.insert({kScratchId, static_cast<uint32_t>(c)});
+  bool uploaded = false;
+  for (const auto& [id, c] : keep) {
+    Alloc& a = m.allocs.at(id);
+    const bool upload = id != kScratchId && m.chunk_needs_upload(a, c, ranges);
+    if (Error e = m.make_resident(a, c, upload, keep, &uploaded))
+      return e;
+  }
+  if (Error e = m.await_uploads(keep, m.s_compute))
+    return e;
+  std::vector<ResolvedRange> resolved;
+  resolved.reserve(ranges.size());
+  for (const AccessRange& r : ranges)
+    resolved.push_back(ResolvedRange{r.allocation_id, r.offset_bytes, r.length_bytes,
+                                     m.allocs.at(r.allocation_id).va + r.offset_bytes, r.mode});
+  const uint64_t ws_addr = ws_chunks ? m.allocs.at(kScratchId).va : 0;
+  Error body_error = body(resolved, ws_addr, workspace_bytes, m.dev->native_stream(m.s_compute));
+  // Whatever the body enqueued may have written its read-write and write-only ranges.
+  for (const auto& [id, c] : keep) {
+    Frame& f = m.frames[static_cast<size_t>(m.allocs.at(id).chunks[c].frame)];
+    if (Error e = m.dev->event_record(f.last_use, m.s_compute))
+      return e;
+    f.pending = true;
+  }
+  for (const AccessRange& r : ranges) {
+    if (r.mode == 0)
+      continue;
+    Alloc& a = m.allocs.at(r.allocation_id);
+    for (uint64_t c = r.offset_bytes / m.cb; c <= (r.offset_bytes + r.length_bytes - 1) / m.cb;
+         ++c) {
+      Chunk& ch = a.chunks[static_cast<size_t>(c)];
+      ch.written = true;
+      ch.dev_valid = true;
+      ch.backing_valid = false;
+    }
+  }
+  if (Error e = m.dev->stream_sync(m.s_compute))
+    return body_error ? body_error : e;
+  for (const auto& [id, c] : keep)
+    m.frames[static_cast<size_t>(m.allocs.at(id).chunks[c].frame)].pending = false;
+  m.t.last_transaction_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  if (body_error)
+    return body_error;
+  ++m.t.transactions_completed;
   return {};
 }
 

@@ -32,6 +32,7 @@
 #include "validate.hpp"
 
 #include <cstdint>
+#include <functional>
 #include <memory>
 #include <vector>
 
@@ -56,6 +57,38 @@ struct GemmCall {
   bool tensor_cores = false;
   // Rates for planning this call (0 = the runtime's configured rates).
   double flops_per_s = 0;
+};
+
+// A byte range of an allocation that an operation touches (reference
+// src/residency/core.cpp:128-277 access ranges).  mode: 0 read, 1 read-write, 2 write-only.
+struct AccessRange {
+  uint64_t allocation_id = 0;
+  uint64_t offset_bytes = 0;
+  uint64_t length_bytes = 0;
+  int mode = 0;
+};
+
+// The same range once resident: device_address is where offset_bytes lives in HBM.
+struct ResolvedRange {
+  uint64_t allocation_id = 0;
+  uint64_t offset_bytes = 0;
+  uint64_t length_bytes = 0;
+  uint64_t device_address = 0;
+  int mode = 0;
+};
+
+// Device-side work of a transaction: enqueue only, on native_stream.
+using TransactionBody = std::function<Error(const std::vector<ResolvedRange>& ranges,
+                                            uint64_t workspace_address, uint64_t workspace_bytes,
+                                            uint64_t native_stream)>;
+
+// How gemm() would run a problem (for plan descriptions; nothing is executed).
+struct GemmLayout {
+  bool in_place = false;
+  uint64_t tile_m = 0, tile_n = 0, tile_k = 0;
+  uint64_t tiles = 0;
+  uint64_t working_set_bytes = 0;
+  uint64_t workspace_bytes = 0;
 };
 
 // Counters that are not part of xvram_session_telemetry_v1.
@@ -85,11 +118,23 @@ public:
   Error open(const RuntimeConfig& cfg, std::unique_ptr<Device> device);
   Error close();
 
-  Error allocate(uint64_t bytes, uint64_t* id, uint64_t* va);
+  // zero_fill: bytes never written read as zero, on the host and on the device.
+  Error allocate(uint64_t bytes, uint64_t* id, uint64_t* va, bool zero_fill = false);
   Error release(uint64_t id);
   Error write(uint64_t id, uint64_t offset, const void* src, uint64_t bytes);
   Error read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes);
   Error gemm(const GemmCall& call);
+  Error describe_gemm(const GemmCall& call, GemmLayout* out);
+  // Starts making the ranges resident (uploads run on the H2D stream); returns without
+  // waiting.  Later operations on these chunks wait for exactly their uploads.
+  Error prefetch(const std::vector<AccessRange>& ranges);
+  // Makes the ranges resident, gives `body` their device addresses, a workspace of
+  // workspace_bytes and the compute stream, marks written ranges dirty and waits for the
+  // stream.  BUDGET_PRESSURE when the ranges and workspace exceed the device budget.
+  Error transaction(const std::vector<AccessRange>& ranges, uint64_t workspace_bytes,
+                    const TransactionBody& body);
+  bool live(uint64_t id) const;
+  uint64_t allocation_bytes(uint64_t id) const;
   Error synchronize();
   Error mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes);
 
