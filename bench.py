@@ -207,7 +207,7 @@ def run_out_of_core(args) -> None:
     dev = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=dev)
     peak_tflops = measure_ffma_peak(dev, stream)
-    h2d_gbs, d2h_gbs = measure_link(dev, stream)
+    h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
 
     api = cp.CompatApi()
     cfg = cp.compat_config_init()
@@ -266,6 +266,114 @@ def run_out_of_core(args) -> None:
                       "handle_reuses": int(tel.runtime.handle_reuses),
                       "mappings": int(tel.runtime.mappings), "unmaps": int(tel.runtime.unmaps),
                       "tiles_retired": int(tel.tiles_retired)},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- MLP workload (C5)
+def run_mlp(args) -> None:
+    """BASELINE config 5 through the SDK (include/xvram.h): 24 x Linear(16384 -> 16384,
+    bias) + ReLU, batch 512, weights N(0, 1/16384), input uniform[-1,1], device budget
+    8 GiB.  The 24 GiB of weights live in the session's pinned host backing; every forward
+    streams each layer's weight through the frame cache.  Per layer the host submits, in
+    order: prefetch of the next layer's weight, the GEMM (strict FP32), and a transaction
+    whose callback runs bias + ReLU on the resident output, then waits only at the end.
+    Activations are column-major features x batch (= row-major batch x features); weights
+    are stored column-major out x in, so op(A) = N.  A step is one forward pass including
+    the input upload and the output download."""
+    import numpy as np
+    import torch
+
+    from xvram_b200 import sdk
+    from xvram_b200.mlp import StreamedMLP
+
+    F, BATCH, LAYERS = args.mlp_features, args.mlp_batch, args.mlp_layers
+    budget = int(args.mlp_budget_gib * (1 << 30))
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(device=dev)
+    peak_tflops = measure_ffma_peak(dev, stream)
+    h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
+    wbytes = F * F * 4
+    abytes = F * BATCH * 4
+
+    def weight(i):  # column-major out x in, N(0, 1/F), regenerated on demand for the check
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + i)
+        return torch.randn((F, F), generator=g, device=dev) / np.sqrt(F)  # [in][out] = col-major
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(999)
+    bias_all = ((torch.rand((LAYERS, F), generator=g, device=dev) * 2 - 1) / np.sqrt(F))
+    x = (torch.rand((BATCH, F), generator=g, device=dev) * 2 - 1)
+
+    s = sdk.Sdk(sdk.session_config(cache_target_bytes=budget))
+    net = StreamedMLP(s, F, BATCH, LAYERS)
+    stage = torch.empty(F * F, dtype=torch.float32).pin_memory()
+    for i in range(LAYERS):
+        stage.copy_(weight(i).reshape(-1))
+        net.load_weight(i, stage)
+    del stage
+    net.load_biases(bias_all.cpu().contiguous().pin_memory())
+    x_h = x.cpu().contiguous().pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+
+    def forward():
+        net.forward(x_h, out_h)
+
+    for _ in range(args.warmup):
+        forward()
+    times = []
+    t0 = s.telemetry()
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            start = time.perf_counter()
+            forward()
+            times.append(time.perf_counter() - start)
+    t1 = s.telemetry()
+    assert net.statuses and all(st == 0 for st in net.statuses)
+
+    # FP64 check of sampled batch rows against the same weights (regenerated on the GPU)
+    cols = [0, 1, BATCH // 2, BATCH - 1]
+    ref = x[cols].double()
+    for i in range(LAYERS):
+        ref = torch.relu(ref @ weight(i).double() + bias_all[i].double())
+    got = out_h[cols].to(dev).double()
+    err = float((got - ref).abs().max())
+    scale = float(ref.abs().max())
+
+    sec = statistics.median(times)
+    flop = LAYERS * 2.0 * F * F * BATCH
+    h2d_moved = (t1.bytes_h2d - t0.bytes_h2d) / args.steps
+    alg_h2d = LAYERS * wbytes + abytes + LAYERS * F * 4   # weights, input, biases, once each
+    alg_d2h = abytes
+    t_roof = max(flop / (peak_tflops * 1e12), alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
+    net.close()
+    tel = s.telemetry()
+    s.close()
+    line = {
+        "metric": METRIC,
+        "workload": f"C5: {LAYERS} x Linear({F}->{F}, bias) + ReLU, batch {BATCH}, "
+                    f"device budget {args.mlp_budget_gib} GiB, through the SDK (xvram_get_api)",
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * sec, "higher_is_better": True,
+        "dtype": "f32", "data": "synthetic (seeded torch generators on the GPU)",
+        "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
+                     "bound": "host-link" if alg_h2d / (h2d_gbs * 1e9) > flop / (peak_tflops * 1e12)
+                     else "fp32",
+                     "p_fp32_tflops": peak_tflops, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs},
+        "host_link": {"h2d_bytes_per_step": h2d_moved, "algorithmic_h2d_bytes": alg_h2d,
+                      "achieved_h2d_gbs": h2d_moved / sec / 1e9},
+        "check": {"sampled_batch_rows": cols, "max_abs_err_vs_fp64": err,
+                  "max_abs_ref": scale},
+        "residency": {"cache_target_bytes": int(tel.cache_target_bytes),
+                      "resident_bytes_peak": int(tel.resident_bytes_peak),
+                      "clean_evictions": int(tel.clean_evictions),
+                      "dirty_evictions": int(tel.dirty_evictions),
+                      "handle_reuses": int(tel.handle_reuses), "mappings": int(tel.mappings),
+                      "transactions_completed": int(tel.transactions_completed)},
+        "step_ms": [1e3 * t for t in times],
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -608,8 +716,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c2", "c3s"], default="c2",
-                    help="c2: the headline (BASELINE config 2); c3s: one out-of-core GEMM")
+    ap.add_argument("--workload", choices=["c2", "c3s", "c5"], default="c2",
+                    help="c2: the headline (BASELINE config 2); c3s: one out-of-core GEMM; "
+                         "c5: the 24-layer MLP (BASELINE config 5) through the SDK")
+    ap.add_argument("--mlp-features", type=int, default=16384)
+    ap.add_argument("--mlp-batch", type=int, default=512)
+    ap.add_argument("--mlp-layers", type=int, default=24)
+    ap.add_argument("--mlp-budget-gib", type=float, default=8.0)
     ap.add_argument("--ooc-n", type=int, default=65536)
     ap.add_argument("--ooc-budget-gib", type=float, default=10.0)
     args = ap.parse_args()
@@ -620,6 +733,9 @@ def main() -> None:
         return
     if args.workload == "c3s":
         run_out_of_core(args)
+        return
+    if args.workload == "c5":
+        run_mlp(args)
         return
     main_gpu(args)
 

@@ -45,6 +45,7 @@ struct Frame {
   bool used = false;      // has held data before (the next owner is a handle reuse)
   bool pending = false;   // last_use has been recorded
   bool uploading = false; // ready has been recorded and not yet observed complete
+  bool prefetched = false; // made resident by a prefetch and not yet used by an operation
 };
 
 } // namespace
@@ -206,15 +207,21 @@ struct Runtime::Impl {
       *out = frames.size() - 1;
       return {};
     }
+    // Least recently used first, but a frame that a prefetch filled for an operation that
+    // has not run yet goes only when nothing else can: evicting it would make that
+    // operation upload it again.
     size_t victim = frames.size();
-    uint64_t oldest = UINT64_MAX;
-    for (size_t i = 0; i < frames.size(); ++i) {
-      const Frame& f = frames[i];
-      if (f.owner == kArenaOwner || keep.count({f.owner, f.chunk}))
-        continue;
-      if (f.touch < oldest) {
-        oldest = f.touch;
-        victim = i;
+    for (int pass = 0; pass < 2 && victim == frames.size(); ++pass) {
+      uint64_t oldest = UINT64_MAX;
+      for (size_t i = 0; i < frames.size(); ++i) {
+        const Frame& f = frames[i];
+        if (f.owner == kArenaOwner || keep.count({f.owner, f.chunk}) ||
+            (pass == 0 && f.prefetched))
+          continue;
+        if (f.touch < oldest) {
+          oldest = f.touch;
+          victim = i;
+        }
       }
     }
     if (victim == frames.size())
@@ -242,6 +249,7 @@ struct Runtime::Impl {
     if (Error e = acquire_frame(keep, &fi))
       return e;
     Frame& f = frames[fi];
+    f.prefetched = false;
     const uint64_t off = static_cast<uint64_t>(c) * cb;
     if (Error e = dev->map(a.va + off, cb, f.handle))
       return e;
@@ -763,6 +771,8 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   // in flight behind the kernel.
   if (Error e = await_uploads(keep, s_compute))
     return e;
+  for (const auto& [id, c] : keep)
+    frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)].prefetched = false;
   const GemmShape& s = call.shape;
   ++x.tiles_submitted;
   ++x.gemm_in_place;
@@ -848,6 +858,7 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     if (frames[i].used)
       ++t.handle_reuses;
     frames[i].owner = kArenaOwner;
+    frames[i].prefetched = false;
     frames[i].used = true;
     arena_frames.push_back(i);
   }
@@ -1059,6 +1070,7 @@ Error Runtime::prefetch(const std::vector<AccessRange>& ranges) {
     Alloc& a = m.allocs.at(id);
     if (Error e = m.make_resident(a, c, m.chunk_needs_upload(a, c, ranges), keep, &uploaded))
       return e;
+    m.frames[static_cast<size_t>(a.chunks[c].frame)].prefetched = true;
   }
   return {};
 }
@@ -1087,6 +1099,8 @@ Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t work
   }
   if (Error e = m.await_uploads(keep, m.s_compute))
     return e;
+  for (const auto& [id, c] : keep)
+    m.frames[static_cast<size_t>(m.allocs.at(id).chunks[c].frame)].prefetched = false;
   std::vector<ResolvedRange> resolved;
   resolved.reserve(ranges.size());
   for (const AccessRange& r : ranges)
