@@ -680,6 +680,8 @@ def main_gpu(args) -> None:
                             "ms_per_step": 1e3 * sharded_s, "h2d_bytes_per_step": sh_h2d,
                             "d2h_bytes_per_step": sh_d2h, "panel_k": 1024,
                             "frac_of_roofline": t_roof_sharded / sharded_s,
+                            "median_ms": 1e3 * statistics.median(sh_times),
+                            "step_ms": [round(1e3 * t, 3) for t in sh_times],
                             "path": "xvram_b200_sgemm_sharded (copies overlap compute)"},
             # per step: the SGEMM kernel plus one transpose per K-major operand (TN: 2)
             "tf32x3": {

@@ -224,3 +224,19 @@ def test_workspace_query():
     assert device.workspace_bytes(0, 1, 100, 100, 100) == 0
     assert device.workspace_bytes(1, 1, 100, 100, 100) == 100 * 100 * 4 + (256 - 100 * 100 * 4 % 256) % 256
     assert device.workspace_bytes(1, 0, 101, 99, 7) >= (104 * 7 + 100 * 7) * 4
+
+
+@pytest.mark.parametrize("op_a,op_b", [(0, 1), (1, 0)])
+@pytest.mark.parametrize("shape", [(2560, 2048, 96),   # 160 tiles: 12-tile tail, split
+                                   (1300, 700, 64),    # 33 tiles: all half-width
+                                   (2560, 1280, 64)])  # 100 tiles: tail too big to split
+def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape):
+    """The TMA kernel runs a last, at most half-full wave as half-width tiles; every output
+    is still one FFMA chain in k order, so its bits equal the generic kernel's."""
+    m, n, k = shape
+    outs = []
+    for path in (TMA, GENERIC):
+        out, ref, c, a, b = run(oracle, op_a, op_b, m, n, k, 0.5, 1.5, seed=70, path=path)
+        outs.append(out)
+    assert np.array_equal(outs[0], outs[1])
+    check(outs[0], ref, c, m, k, a, b)

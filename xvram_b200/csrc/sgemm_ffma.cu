@@ -56,8 +56,11 @@ namespace {
 #ifndef XVRAM_FFMA_STAGES
 #define XVRAM_FFMA_STAGES 4
 #endif
+// Groups of 4 k unrolled per loop iteration: 2 keeps the loop body (~1,100 instructions)
+// small enough for the instruction cache; the fully unrolled 32-k stage (8) stalls on
+// instruction fetch (ncu: no_instruction 0.61 per issue) and runs ~2 % slower.
 #ifndef XVRAM_FFMA_GROUP_UNROLL
-#define XVRAM_FFMA_GROUP_UNROLL 8
+#define XVRAM_FFMA_GROUP_UNROLL 2
 #endif
 constexpr int kBM = 128;
 constexpr int kBK = 32;
@@ -80,6 +83,9 @@ struct FfmaParams {
   int m, n, k;
   int k_tiles;
   int tiles_m, tiles_n;
+  // Blocks [0, full_tiles) compute whole tiles; every later pair of blocks splits one of
+  // the remaining tiles into two half-width tiles (see launch_tma).
+  int full_tiles;
   float alpha, beta;
   float* c;
   long long ldc;
@@ -131,12 +137,13 @@ template <bool KMAJOR> __device__ __forceinline__ int frag_index(int t, int i) {
 
 // One k-group (4 consecutive k) of the B fragment, streamed: calls body(j, b[0..3]) for
 // a K-major tile (b = 4 k of column j) -- see group_ffma below for the N-major form.
-template <int TN>
+// NJ <= TN: a half-width tile computes only the thread's first NJ columns.
+template <int TN, int NJ>
 __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const float* bs, int g,
-                                              int tn, float (&acc)[8][TN]) {
+                                              int tn, float (&acc)[8][NJ]) {
   const int chunk = (g ^ (tn & 7)) * 4;
 #pragma unroll
-  for (int j = 0; j < TN; ++j) {
+  for (int j = 0; j < NJ; ++j) {
     const float4 v = *reinterpret_cast<const float4*>(bs + (tn + 16 * j) * kBK + chunk);
     const float b[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -148,16 +155,16 @@ __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const floa
 }
 
 // N-major B tile [32 k][BN]: one k row of the thread's TN columns at a time.
-template <int TN>
+template <int TN, int NJ>
 __device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const float* bs, int g,
-                                              int tn, float (&acc)[8][TN]) {
+                                              int tn, float (&acc)[8][NJ]) {
   constexpr int BN = 16 * TN;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const float* row = bs + (4 * g + kk) * BN + 4 * tn;
-    float b[TN];
+    float b[NJ];
 #pragma unroll
-    for (int q = 0; q < TN / 4; ++q) {
+    for (int q = 0; q < NJ / 4; ++q) {
       const float4 v = *reinterpret_cast<const float4*>(row + 64 * q);
       b[4 * q + 0] = v.x;
       b[4 * q + 1] = v.y;
@@ -167,8 +174,112 @@ __device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const floa
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < TN; ++j)
+      for (int j = 0; j < NJ; ++j)
         acc[i][j] = fmaf(a[kk][i], b[j], acc[i][j]);
+  }
+}
+
+// Arms stage s of the ring with K tile kt: expected bytes, then the A and B TMA loads.
+template <bool A_KMAJOR, bool B_KMAJOR, int TN>
+__device__ __forceinline__ void issue_stage(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                            float* smem_a, float* smem_b, uint64_t* full, int kt,
+                                            int m0, int n0) {
+  using Cfg = TileCfg<TN>;
+  const int s = kt % kStages;
+  mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+  const int k0 = kt * kBK;
+  float* sa = smem_a + s * kAStageFloats;
+  float* sb = smem_b + s * Cfg::BStageFloats;
+  if constexpr (A_KMAJOR)
+    tma_load_2d(sa, tmap_a, &full[s], k0, m0);
+  else
+    tma_load_2d(sa, tmap_a, &full[s], m0, k0);
+  if constexpr (B_KMAJOR)
+    tma_load_2d(sb, tmap_b, &full[s], k0, n0);
+  else
+    tma_load_2d(sb, tmap_b, &full[s], n0, k0);
+}
+
+// The K loop and epilogue of one CTA tile computing the thread's first NJ columns (NJ = TN
+// for a whole tile, TN / 2 for a half-width tile).  Every output element is one FFMA chain
+// in k order whichever NJ computes it, so whole and half tiles give identical bits.
+template <bool A_KMAJOR, bool B_KMAJOR, int TN, int NJ>
+__device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                          float* smem_a, float* smem_b, uint64_t* full,
+                                          uint64_t* empty, const FfmaParams& p, int m0, int n0,
+                                          int issued) {
+  using Cfg = TileCfg<TN>;
+  const int tid = threadIdx.x;
+  const int tm = tid & 15;
+  const int tn = tid >> 4;
+  float acc[8][NJ];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+      acc[i][j] = 0.0f;
+
+  bool aborted = false;
+  for (int kt = 0; kt < p.k_tiles; ++kt) {
+    const int s = kt % kStages;
+    const uint32_t phase = (kt / kStages) & 1;
+    if (!mbar_wait_bounded(&full[s], phase, p.timeout_ns)) {
+      atomicOr(&xvram_kernel_error, 1u);
+      aborted = true;
+      break;
+    }
+    const float* as = smem_a + s * kAStageFloats;
+    const float* bs = smem_b + s * Cfg::BStageFloats;
+#pragma unroll kGroupUnroll
+    for (int g = 0; g < kBK / 4; ++g) {
+      float a[4][8];
+      load_frag<A_KMAJOR>(as, g, tm, a);
+      if constexpr (B_KMAJOR)
+        ffma_group_bk<TN, NJ>(a, bs, g, tn, acc);
+      else
+        ffma_group_bn<TN, NJ>(a, bs, g, tn, acc);
+    }
+    __syncwarp();
+    if ((tid & 31) == 0)
+      mbar_arrive(&empty[s]);
+    // Refill this stage with tile kt + 4 once every warp has released tile kt.
+    if (tid == 0 && issued < p.k_tiles) {
+      if (!mbar_wait_bounded(&empty[s], phase, p.timeout_ns)) {
+        atomicOr(&xvram_kernel_error, 2u);
+        aborted = true;
+        break;
+      }
+      issue_stage<A_KMAJOR, B_KMAJOR, TN>(tmap_a, tmap_b, smem_a, smem_b, full, issued++, m0, n0);
+    }
+  }
+  if (aborted) {
+    // Never leave the CTA with copies still landing in its shared memory: thread 0 waits
+    // (bounded) for the last fill of every stage it armed; then everyone returns.
+    if (tid == 0)
+      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
+        if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
+          atomicOr(&xvram_kernel_error, 4u);
+          break;
+        }
+    return;
+  }
+
+  // ------------------------------------------------------------------- epilogue
+  const float alpha = p.alpha, beta = p.beta;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
+    if (col >= p.n)
+      continue;
+    float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+      if (row < p.m) {
+        const float v = alpha * acc[i][j];
+        cc[row] = (beta == 0.0f) ? v : fmaf(beta, cc[row], v);
+      }
+    }
   }
 }
 
@@ -188,19 +299,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * Cfg::BStageFloats);
   uint64_t* empty = full + kStages;
 
+  // Blocks past full_tiles come in pairs that share one tile, each taking half of its
+  // columns: the last, partial wave then lasts about half a tile.
+  const int bid = blockIdx.x;
+  const bool half = bid >= p.full_tiles;
+  const int tile_lin = half ? p.full_tiles + ((bid - p.full_tiles) >> 1) : bid;
+  const int half_index = half ? ((bid - p.full_tiles) & 1) : 0;
   // Grouped rasterisation: 8 consecutive M tiles sweep the N tiles together so the
   // B stage tiles they share stay in L2.
-  const int bid = blockIdx.x;
   const int group_span = 8 * p.tiles_n;
-  const int first_m = (bid / group_span) * 8;
+  const int first_m = (tile_lin / group_span) * 8;
   const int group_m = min(8, p.tiles_m - first_m);
-  const int tile_m = first_m + (bid % group_span) % group_m;
-  const int tile_n = (bid % group_span) / group_m;
+  const int tile_m = first_m + (tile_lin % group_span) % group_m;
+  const int tile_n = (tile_lin % group_span) / group_m;
   const int m0 = tile_m * kBM;
-  const int n0 = tile_n * BN;
+  // A half tile's TMA box starts at its own first column; the box's second half (columns
+  // of the partner, or past N where TMA fills zeros) is loaded and not used.
+  const int n0 = tile_n * BN + half_index * (BN / 2);
 
   const int tid = threadIdx.x;
-
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -210,101 +327,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
-  // Thread 0 arms stage s for K tile kt: expected bytes, then the two TMA loads.
-  auto issue = [&](int kt) {
-    const int s = kt % kStages;
-    mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
-    const int k0 = kt * kBK;
-    float* sa = smem_a + s * kAStageFloats;
-    float* sb = smem_b + s * Cfg::BStageFloats;
-    if constexpr (A_KMAJOR)
-      tma_load_2d(sa, &tmap_a, &full[s], k0, m0);
-    else
-      tma_load_2d(sa, &tmap_a, &full[s], m0, k0);
-    if constexpr (B_KMAJOR)
-      tma_load_2d(sb, &tmap_b, &full[s], k0, n0);
-    else
-      tma_load_2d(sb, &tmap_b, &full[s], n0, k0);
-  };
   int issued = 0; // meaningful in thread 0 only
   if (tid == 0) {
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
     for (; issued < kStages && issued < p.k_tiles; ++issued)
-      issue(issued);
+      issue_stage<A_KMAJOR, B_KMAJOR, TN>(&tmap_a, &tmap_b, smem_a, smem_b, full, issued, m0, n0);
   }
-
-  const int tm = tid & 15;
-  const int tn = tid >> 4;
-  float acc[8][TN];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < TN; ++j)
-      acc[i][j] = 0.0f;
-
-  bool aborted = false;
-  for (int kt = 0; kt < p.k_tiles; ++kt) {
-    const int s = kt % kStages;
-    const uint32_t phase = (kt / kStages) & 1;
-    if (!mbar_wait_bounded(&full[s], phase, p.timeout_ns)) {
-      atomicOr(&xvram_kernel_error, 1u);
-      aborted = true;
-      break;
-    }
-    const float* as = smem_a + s * kAStageFloats;
-    const float* bs = smem_b + s * Cfg::BStageFloats;
-#pragma unroll kGroupUnroll
-    for (int g = 0; g < kBK / 4; ++g) {
-      float a[4][8];
-      load_frag<A_KMAJOR>(as, g, tm, a);
-      if constexpr (B_KMAJOR)
-        ffma_group_bk<TN>(a, bs, g, tn, acc);
-      else
-        ffma_group_bn<TN>(a, bs, g, tn, acc);
-    }
-    __syncwarp();
-    if ((tid & 31) == 0)
-      mbar_arrive(&empty[s]);
-    // Refill this stage with tile kt + 4 once every warp has released tile kt.
-    if (tid == 0 && issued < p.k_tiles) {
-      if (!mbar_wait_bounded(&empty[s], phase, p.timeout_ns)) {
-        atomicOr(&xvram_kernel_error, 2u);
-        aborted = true;
-        break;
-      }
-      issue(issued++);
-    }
-  }
-  if (aborted) {
-    // Never leave the CTA with copies still landing in its shared memory: thread 0 waits
-    // (bounded) for the last fill of every stage it armed; then everyone returns.
-    if (tid == 0)
-      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
-        if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
-          atomicOr(&xvram_kernel_error, 4u);
-          break;
-        }
-    return;
-  }
-
-  // ------------------------------------------------------------------- epilogue
-  const float alpha = p.alpha, beta = p.beta;
-#pragma unroll
-  for (int j = 0; j < TN; ++j) {
-    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
-    if (col >= p.n)
-      continue;
-    float* cc = p.c + static_cast<long long>(col) * p.ldc;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = m0 + frag_index<A_KMAJOR>(tm, i);
-      if (row < p.m) {
-        const float v = alpha * acc[i][j];
-        cc[row] = (beta == 0.0f) ? v : fmaf(beta, cc[row], v);
-      }
-    }
-  }
+  if (half)
+    tile_main<A_KMAJOR, B_KMAJOR, TN, TN / 2>(&tmap_a, &tmap_b, smem_a, smem_b, full, empty, p,
+                                              m0, n0, issued);
+  else
+    tile_main<A_KMAJOR, B_KMAJOR, TN, TN>(&tmap_a, &tmap_b, smem_a, smem_b, full, empty, p, m0,
+                                          n0, issued);
 }
 
 // ---------------------------------------------------------------------------------
@@ -450,13 +485,41 @@ template <bool AK, bool BK, int TN> cudaError_t configure_once() {
   return status;
 }
 
+int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// One CTA per SM (the ring takes ~193 KB of shared memory), so tiles run in waves of the
+// SM count.  When the last wave would be at most half full, its tiles are launched as
+// two half-width blocks each: the same work on twice the SMs, half the tail time.
 template <bool AK, bool BK, int TN>
-cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, const FfmaParams& p,
+cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, FfmaParams p,
                        cudaStream_t stream) {
   if (cudaError_t e = configure_once<AK, BK, TN>(); e != cudaSuccess)
     return e;
-  const unsigned grid = static_cast<unsigned>(p.tiles_m) * static_cast<unsigned>(p.tiles_n);
-  sgemm_ffma_tma<AK, BK, TN><<<grid, kThreads, TileCfg<TN>::SmemBytes, stream>>>(ta, tb, p);
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long sms = sm_count();
+  const long long tail = tiles % sms;
+  long long grid = tiles;
+  p.full_tiles = static_cast<int>(tiles);
+  if (tail > 0 && 2 * tail <= sms) {
+    p.full_tiles = static_cast<int>(tiles - tail);
+    grid = tiles + tail;
+  }
+  if (grid > 0x7fffffffll)
+    return cudaErrorInvalidConfiguration;
+  sgemm_ffma_tma<AK, BK, TN>
+      <<<static_cast<unsigned>(grid), kThreads, TileCfg<TN>::SmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
