@@ -20,13 +20,19 @@
 // Pipeline:
 //   split pass : operands -> hi/lo arrays in K-major layout [rows][K] (one HBM pass, also
 //                transposing M-/N-major operands), in caller-provided scratch.
-//   GEMM kernel: CTA tile 128 x 256, K in stages of 16 (64-byte rows, 64-byte swizzle);
-//     warp 0      one lane: 2D TMA loads of A_hi, A_lo, B_hi, B_lo into a 4-deep ring;
-//     warp 1      allocates 256 TMEM columns; one lane issues, per k8 step,
-//                 tcgen05.mma.kind::tf32 lo*hi, hi*lo, hi*hi (M=128, N=256) into the TMEM
-//                 accumulator and commits each stage back to the producer;
-//     warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns at a time, alpha/beta, stores
-//                 coalesced along M.
+//   GEMM kernel: a CTA pair (cluster of 2, one per SM) computes a 256 x 256 tile of C;
+//     each CTA stages its 128 rows of A and its 128-row half of B, K in stages of 32
+//     (128-byte rows, 128-byte swizzle) through a 3-deep ring of 64 KB stages.  Rows of
+//     128 bytes halve the TMA row requests per MMA against 64-byte rows, and the pair
+//     halves each SM's B bytes against a single-CTA 128 x 256 tile;
+//     warp 0      one lane per CTA: 2D TMA loads (cta_group::2 form) of A_hi, A_lo, B_hi,
+//                 B_lo, completion counted on the leader's barrier;
+//     warp 1      allocates 512 TMEM columns in each CTA; on the leader one lane issues,
+//                 per k8 step, tcgen05.mma.cta_group::2.kind::tf32 lo*hi, hi*lo (cross-term
+//                 accumulator) and hi*hi (M=256, N=256), and commits each stage back to
+//                 both CTAs' producers;
+//     warps 2..5  epilogue per CTA: tcgen05.ld 32 lanes x 16 columns of both accumulators,
+//                 sum, alpha/beta, stores coalesced along M.
 // All waits are bounded; a timeout sets a bit in the kernel error word, the CTA drains
 // what it issued, frees its TMEM and returns.
 #include "device_common.cuh"
@@ -43,51 +49,88 @@ __device__ unsigned int xvram_kernel_error_tc = 0;
 
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBN = 256;
-constexpr int kBK = 16;                 // tf32 elements per stage row (64 bytes)
-constexpr int kStages = 4;
+// A CTA pair (cluster of 2) computes one 256 x 256 tile of C: CTA rank r holds rows
+// [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile (N half),
+// and its TMEM holds its 128 rows x 256 columns of the accumulators.  Only the pair's
+// leader (rank 0) issues the MMAs (cta_group::2, M = 256, N = 256); the hardware reads
+// the A and B halves from both CTAs' shared memory at the same offsets.
+constexpr int kPairM = 256;
+constexpr int kPairN = 256;
+constexpr int kRows = 128;              // rows of A and of B each CTA stages
+constexpr int kBK = 32;                 // tf32 elements per stage row (128 bytes)
+constexpr int kStages = 3;
 constexpr int kThreads = 192;           // 6 warps
-constexpr uint32_t kTileA = kBM * kBK * 4; // 8 KB
-constexpr uint32_t kTileB = kBN * kBK * 4; // 16 KB
-constexpr uint32_t kStageBytes = 2 * kTileA + 2 * kTileB;
+constexpr uint32_t kTile = kRows * kBK * 4;          // 16 KB: one of A_hi, A_lo, B_hi, B_lo
+constexpr uint32_t kStageBytes = 4 * kTile;          // 64 KB per CTA per stage
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;    // two 128 x 256 FP32 accumulators
+constexpr uint32_t kTmemCols = 512;    // two 128 x 256 FP32 accumulators per CTA
 constexpr uint32_t kSmallCol = 256;     // column of the cross-term accumulator
 constexpr int kChunkK = 2048;           // longest tensor-core accumulation chain
 
-// Instruction descriptor: D F32, A/B TF32, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kBN >> 3) << 17) |
-                            ((kBM >> 4) << 24);
+// Instruction descriptor: D F32, A/B TF32, both K-major, N = 256, M = 256 (CTA pair).
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kPairN >> 3) << 17) |
+                            ((kPairM >> 4) << 24);
 
-// Shared-memory matrix descriptor for a K-major tile with 64-byte swizzle: core matrices
-// of 8 rows x 64 bytes, 512 bytes apart (stride byte offset); leading byte offset unused.
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+// Shared-memory matrix descriptor for a K-major tile with 128-byte swizzle: core matrices
+// of 8 rows x 128 bytes, 1024 bytes apart (stride byte offset); leading byte offset unused.
+// A K step of 8 tf32 inside the 128-byte row advances the start address by 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
   d |= static_cast<uint64_t>(1) << 16;              // LBO (ignored for swizzled K-major)
-  d |= static_cast<uint64_t>(512 >> 4) << 32;       // SBO
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;      // SBO
   d |= static_cast<uint64_t>(1) << 46;              // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(4) << 61;              // SWIZZLE_64B
+  d |= static_cast<uint64_t>(2) << 61;              // SWIZZLE_128B
   return d;
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t accumulate) {
   asm volatile(
       "{\n"
       "  .reg .pred p;\n"
       "  setp.ne.b32 p, %4, 0;\n"
-      "  tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n"
+      "  tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n"
       "}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
+// Arrives on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's) once
+// every tensor-core operation issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
                : "memory");
+}
+
+// shared::cluster address of the same shared::cta offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2D TMA load into this CTA's shared memory whose completion bytes are counted on the
+// mbarrier at shared::cluster address `bar` (the pair leader's barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -122,7 +165,7 @@ struct Tf32Params {
   unsigned long long timeout_ns;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sgemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_ahi,
                         const __grid_constant__ CUtensorMap tm_alo,
                         const __grid_constant__ CUtensorMap tm_bhi,
@@ -136,12 +179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int bid = blockIdx.x;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
   const int group_span = 8 * p.tiles_n;
-  const int first_m = (bid / group_span) * 8;
+  const int first_m = (pair / group_span) * 8;
   const int group_m = min(8, p.tiles_m - first_m);
-  const int m0 = (first_m + (bid % group_span) % group_m) * kBM;
-  const int n0 = ((bid % group_span) / group_m) * kBN;
+  const int pm0 = (first_m + (pair % group_span) % group_m) * kPairM;
+  const int pn0 = ((pair % group_span) / group_m) * kPairN;
+  const int m0 = pm0 + kRows * static_cast<int>(rank); // this CTA's A rows (and C rows)
+  const int nb0 = pn0 + kRows * static_cast<int>(rank); // this CTA's B rows (N half)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -149,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1); // used on the leader: its producer's expect_tx arrival
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -157,21 +204,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync(); // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   auto stage_ptr = [&](int s, int which) -> unsigned char* {
-    // which: 0 A_hi, 1 A_lo, 2 B_hi, 3 B_lo
-    unsigned char* base = smem + s * kStageBytes;
-    return base + (which < 2 ? which * kTileA : 2 * kTileA + (which - 2) * kTileB);
+    return smem + s * kStageBytes + which * kTile; // 0 A_hi, 1 A_lo, 2 B_hi, 3 B_lo
   };
 
   if (warp == 0) {
@@ -192,24 +237,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        const uint32_t bar = cluster_addr(&full[s], 0);
+        if (leader)
+          mbar_arrive_expect_tx(&full[s], 2 * kStageBytes); // both CTAs' copies
         const int k0 = (p.k_begin + kt) * kBK;
-        tma_load_2d(stage_ptr(s, 0), &tm_ahi, &full[s], k0, m0);
-        tma_load_2d(stage_ptr(s, 1), &tm_alo, &full[s], k0, m0);
-        tma_load_2d(stage_ptr(s, 2), &tm_bhi, &full[s], k0, n0);
-        tma_load_2d(stage_ptr(s, 3), &tm_blo, &full[s], k0, n0);
+        tma_load_2d_pair(stage_ptr(s, 0), &tm_ahi, bar, k0, m0);
+        tma_load_2d_pair(stage_ptr(s, 1), &tm_alo, bar, k0, m0);
+        tma_load_2d_pair(stage_ptr(s, 2), &tm_bhi, bar, k0, nb0);
+        tma_load_2d_pair(stage_ptr(s, 3), &tm_blo, bar, k0, nb0);
         ++issued;
       }
-      // Drain: every armed fill has landed before this CTA may exit.
-      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
-        if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
+      // Drain: every stage this CTA filled has been consumed (or times out) before exit.
+      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt) {
+        if (!mbar_wait_bounded(&empty[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
           atomicOr(&xvram_kernel_error_tc, 4u);
           break;
         }
+      }
     }
   } else if (warp == 1) {
-    // -------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------- MMA issuer (pair leader)
+    if (leader && lane == 0) {
+      const uint32_t empty_peer0 = cluster_addr(&empty[0], 1);
+      const uint32_t empty_self0 = cluster_addr(&empty[0], 0);
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         const int s = kt % kStages;
         if (*abort_flag)
@@ -226,29 +276,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kBK / 8; ++kk) {
           const uint32_t off = kk * 32; // 8 tf32 = 32 bytes along K inside the swizzle atom
           const uint32_t acc = (kt == 0 && kk == 0) ? 0u : 1u; // first MMA overwrites
-          mma_tf32(tmem + kSmallCol, smem_desc_sw64(a_lo + off), smem_desc_sw64(b_hi + off), acc);
-          mma_tf32(tmem + kSmallCol, smem_desc_sw64(a_hi + off), smem_desc_sw64(b_lo + off), 1u);
-          mma_tf32(tmem, smem_desc_sw64(a_hi + off), smem_desc_sw64(b_hi + off), acc);
+          mma_tf32_pair(tmem + kSmallCol, smem_desc_sw128(a_lo + off), smem_desc_sw128(b_hi + off),
+                        acc);
+          mma_tf32_pair(tmem + kSmallCol, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_lo + off),
+                        1u);
+          mma_tf32_pair(tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_hi + off), acc);
         }
-        mma_commit(&empty[s]); // stage free once these MMAs have read it
+        // Stage s is free in both CTAs once these MMAs have read it.
+        const uint32_t soff = static_cast<uint32_t>(s) * sizeof(uint64_t);
+        mma_commit_pair(empty_self0 + soff);
+        mma_commit_pair(empty_peer0 + soff);
       }
-      mma_commit(acc_full); // accumulator complete (or everything issued has drained)
+      mma_commit_pair(cluster_addr(acc_full, 0));
+      mma_commit_pair(cluster_addr(acc_full, 1));
     }
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3; // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
+    const int row = m0 + 32 * quad + lane;
+    // While the MMAs run, pull this thread's row of the C tile into L2: a warp's 32 rows of
+    // one column are one 128-byte line, so the epilogue's reads below hit L2.
+    if (p.beta != 0.0f && row < p.m) {
+      for (int c = 0; c < kPairN; ++c) {
+        const int col = pn0 + c;
+        if (col < p.n)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(p.c + row + static_cast<long long>(col) * p.ldc));
+      }
+    }
     const bool ok = mbar_wait_bounded(acc_full, 0, p.timeout_ns * 4);
     if (!ok) {
       atomicOr(&xvram_kernel_error_tc, 8u);
       *abort_flag = 1;
     }
     tc_fence_after();
-    const int quad = warp & 3; // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
-    const int row = m0 + 32 * quad + lane;
     // tcgen05.ld is warp-collective: decide for the whole warp at once.
     if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
       const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-      for (int c0 = 0; c0 < kBN; c0 += 16) {
+      for (int c0 = 0; c0 < kPairN; c0 += 16) {
         float v[16], w[16];
         tmem_ld16(t_row + c0, v);
         tmem_ld16(t_row + kSmallCol + c0, w);
@@ -256,13 +321,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16; ++j)
           v[j] += w[j];
         if (row < p.m) {
+          // All sixteen C reads are issued before any store: read-then-write per column
+          // would make each read wait for the previous column's store (the columns' addresses
+          // are not provably distinct), one memory round trip per column.
+          float cv[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int col = n0 + c0 + j;
+            const int col = pn0 + c0 + j;
+            cv[j] = (p.beta != 0.0f && col < p.n)
+                        ? p.c[row + static_cast<long long>(col) * p.ldc]
+                        : 0.0f;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = pn0 + c0 + j;
             if (col < p.n) {
-              float* cp = p.c + row + static_cast<long long>(col) * p.ldc;
               const float r = p.alpha * v[j];
-              *cp = (p.beta == 0.0f) ? r : fmaf(p.beta, *cp, r);
+              p.c[row + static_cast<long long>(col) * p.ldc] =
+                  (p.beta == 0.0f) ? r : fmaf(p.beta, cv[j], r);
             }
           }
         }
@@ -271,10 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
   }
 
+  // Neither CTA leaves (or frees TMEM) while its partner may still use its shared memory
+  // or TMEM: every wait above is bounded, so both CTAs reach this point.
   __syncthreads();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
   }
@@ -340,7 +419,7 @@ bool encode_kmajor(CUtensorMap* map, const float* base, uint64_t kdim, uint64_t 
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
   const cuuint32_t es[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
-                box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -392,8 +471,10 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
     return e;
 
   CUtensorMap t_ahi, t_alo, t_bhi, t_blo;
-  if (!encode_kmajor(&t_ahi, a_hi, k, m, kp, kBM) || !encode_kmajor(&t_alo, a_lo, k, m, kp, kBM) ||
-      !encode_kmajor(&t_bhi, b_hi, k, n, kp, kBN) || !encode_kmajor(&t_blo, b_lo, k, n, kp, kBN))
+  if (!encode_kmajor(&t_ahi, a_hi, k, m, kp, kRows) ||
+      !encode_kmajor(&t_alo, a_lo, k, m, kp, kRows) ||
+      !encode_kmajor(&t_bhi, b_hi, k, n, kp, kRows) ||
+      !encode_kmajor(&t_blo, b_lo, k, n, kp, kRows))
     return cudaErrorInvalidValue;
   static cudaError_t attr = cudaFuncSetAttribute(
       sgemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -403,13 +484,13 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
   p.m = m;
   p.n = n;
   p.k = k;
-  p.tiles_m = (m + kBM - 1) / kBM;
-  p.tiles_n = (n + kBN - 1) / kBN;
+  p.tiles_m = (m + kPairM - 1) / kPairM;
+  p.tiles_n = (n + kPairN - 1) / kPairN;
   p.alpha = alpha;
   p.c = c;
   p.ldc = ldc;
   p.timeout_ns = kernel_wait_limit_ns();
-  const long long grid = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long grid = 2ll * p.tiles_m * p.tiles_n; // two CTAs per tile (cluster pairs)
   if (grid > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
   const int total_tiles = (k + kBK - 1) / kBK;
