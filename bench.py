@@ -399,6 +399,33 @@ def measure_ffma_peak(dev, stream, iters: int = 8000) -> float:
     return best / 1e12
 
 
+def cublas_tf32_tflops(dev) -> float:
+    """cuBLAS TF32 GEMM throughput measured here (8192^3, best of 5, CUDA events): the
+    library ceiling for the tensor-core path, beside the BF16 / 2 figure below."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        for _ in range(2):
+            torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            e1.synchronize()
+            best = max(best, 2.0 * n ** 3 / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        del a, b
+        return best
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def measured_tf32_peak():
     """Dense TF32 tensor peak implied by the driver-measured BF16 GEMM burst figure."""
     try:
@@ -541,6 +568,7 @@ def main_gpu(args) -> None:
     assert xd.kernel_status(stream) == 0
     tc_ms = max_over_ranks(t0e.elapsed_time(t1e) / args.steps)
     del tc_ws, C_tc
+    tf32_cublas = cublas_tf32_tflops(dev)
 
     # ---------------- end to end, sharded path: C rows per rank, B panels read 1/N per rank
     # from host memory and all-gathered over NVLink (xvram_b200_sgemm_sharded)
@@ -694,7 +722,11 @@ def main_gpu(args) -> None:
                                 "achieved_tf32_tflops": 3 * FLOP / (tc_ms * 1e-3) / 1e12,
                                 "peak_tf32_tflops": measured_tf32_peak(),
                                 "peak_source": "MEASURED_PEAKS.json bf16_tflops / 2 (TF32 runs "
-                                               "at half the BF16 tensor rate)"},
+                                               "at half the BF16 tensor rate)",
+                                "frac": 3 * FLOP / (tc_ms * 1e-3) / 1e12 / measured_tf32_peak(),
+                                "cublas_tf32_tflops_this_run": tf32_cublas,
+                                "frac_of_cublas_tf32": 3 * FLOP / (tc_ms * 1e-3) / 1e12
+                                                       / tf32_cublas},
                 "e2e": {"value": FLOP / e2e_tc_s / 1e12, "unit": "TFLOP/s",
                         "ms_per_step": 1e3 * e2e_tc_s,
                         "path": "compat ABI, blas_set_math_mode(3)"},

@@ -212,6 +212,23 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
   const int tid = threadIdx.x;
   const int tm = tid & 15;
   const int tn = tid >> 4;
+  // The epilogue reads this thread's C entries; ask L2 for their lines now, so those reads
+  // hit L2 after the K loop instead of waiting on DRAM.
+  if (p.beta != 0.0f) {
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int col = n0 + frag_index<B_KMAJOR>(tn, j);
+      if (col < p.n) {
+        const float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+        for (int i = 0; i < 8; i += (A_KMAJOR ? 1 : 4)) { // M-major rows come in fours
+          const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+          if (row < p.m)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(cc + row));
+        }
+      }
+    }
+  }
   float acc[8][NJ];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -265,19 +282,35 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
   }
 
   // ------------------------------------------------------------------- epilogue
+  // Two columns at a time: their 16 C reads are issued before any store (a read after a
+  // store to another column would wait for it -- the addresses are not provably distinct).
   const float alpha = p.alpha, beta = p.beta;
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
-    if (col >= p.n)
-      continue;
-    float* cc = p.c + static_cast<long long>(col) * p.ldc;
+  for (int j0 = 0; j0 < NJ; j0 += 2) {
+    float cv[2][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = m0 + frag_index<A_KMAJOR>(tm, i);
-      if (row < p.m) {
-        const float v = alpha * acc[i][j];
-        cc[row] = (beta == 0.0f) ? v : fmaf(beta, cc[row], v);
+    for (int jj = 0; jj < 2; ++jj) {
+      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      const float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+        cv[jj][i] = (beta != 0.0f && col < p.n && row < p.m) ? cc[row] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      if (col >= p.n)
+        continue;
+      float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+        if (row < p.m) {
+          const float v = alpha * acc[i][j0 + jj];
+          cc[row] = (beta == 0.0f) ? v : fmaf(beta, cv[jj][i], v);
+        }
       }
     }
   }
