@@ -41,6 +41,8 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 namespace xvram {
 
 // Sticky error word of the tensor-core kernel (bits as in the FFMA kernel's word, plus
@@ -401,6 +403,31 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// hi/lo of an operand that is already K-contiguous with K and its leading dimension
+// multiples of 4: a streaming elementwise pass, 16 bytes in and 2 x 16 bytes out per
+// thread and step (no transpose, no shared memory).
+__global__ void __launch_bounds__(256)
+    split_tf32_vec4(const float4* __restrict__ src, long long lds4, int rows, int k4,
+                    float4* __restrict__ hi, float4* __restrict__ lo, long long ldo4) {
+  const long long total = static_cast<long long>(rows) * k4;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * 256) {
+    const long long r = i / k4, q = i - r * k4;
+    const float4 x = src[q + r * lds4];
+    float4 h, l;
+    h.x = to_tf32(x.x);
+    h.y = to_tf32(x.y);
+    h.z = to_tf32(x.z);
+    h.w = to_tf32(x.w);
+    l.x = to_tf32(x.x - h.x);
+    l.y = to_tf32(x.y - h.y);
+    l.z = to_tf32(x.z - h.z);
+    l.w = to_tf32(x.w - h.w);
+    hi[q + r * ldo4] = h;
+    lo[q + r * ldo4] = l;
+  }
+}
+
 bool encode_kmajor(CUtensorMap* map, const float* base, uint64_t kdim, uint64_t rows, uint64_t ld,
                    uint32_t box_rows) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
@@ -458,6 +485,18 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
   // K-contiguous for op N.
   const auto split = [&](const float* src, long long ld, bool k_contig, int rows, float* hi,
                          float* lo) {
+    if (k_contig && k % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+      int dev = 0, sms = 148;
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const long long work = static_cast<long long>(rows) * (k / 4);
+      const long long blocks = std::min<long long>((work + 255) / 256, 16ll * sms);
+      split_tf32_vec4<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+          reinterpret_cast<const float4*>(src), ld / 4, rows, k / 4,
+          reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo),
+          static_cast<long long>(kp) / 4);
+      return cudaGetLastError();
+    }
     const long long tiles_r = (rows + 31) / 32, tiles_k = (k + 31) / 32;
     if (tiles_r * tiles_k > 0x7fffffffll)
       return cudaErrorInvalidConfiguration;
