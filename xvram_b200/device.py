@@ -47,6 +47,15 @@ def sgemm_ws(op_a: int, op_b: int, m: int, n: int, k: int, alpha: float, a, lda:
                                           _stream_handle(stream), path)
 
 
+def bias_activation(y, ldy: int, rows: int, cols: int, bias=None, relu: bool = False,
+                    stream=None) -> int:
+    """Y = act(Y + bias) on a column-major rows x cols device block (bias: rows floats or
+    None); returns the xvram_status.  Enqueued on `stream` (default: torch's current)."""
+    ptr = lambda x: 0 if x is None else (x if isinstance(x, int) else x.data_ptr())
+    return lib.xvram_b200_bias_activation(ptr(y), ldy, rows, cols, ptr(bias), 1 if relu else 0,
+                                          _stream_handle(stream))
+
+
 def kernel_status(stream=None) -> int:
     """Synchronises the stream and returns (and clears) the kernel error word."""
     w = u32(0)
