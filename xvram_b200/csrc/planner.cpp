@@ -10,11 +10,16 @@
 namespace xvram {
 namespace {
 
-constexpr int64_t kTileM = 128;   // CTA tile of the contraction kernel
-constexpr int64_t kTileN = 128;
+constexpr int64_t kTileM = 128;   // CTA tile rows of the contraction kernel
+constexpr int64_t kTileN = 128;   // block width granularity (the kernel's tiles are 256 wide
+                                  // when the block is wider than 128)
 constexpr int64_t kTileK = 32;
 constexpr int kSmCount = 148;
 constexpr double kStepOverheadS = 15e-6; // launch + event bookkeeping per step
+// Fixed time of one CTA tile besides its FFMAs: the TMA ring filling up and the C
+// epilogue (read, alpha/beta, write).  Every wave of every step pays it, so deep K panels
+// (fewer steps) amortise it; measured at ~1 ms per 16384 x 16384 step (55 waves).
+constexpr double kTileFixedS = 12e-6;
 constexpr int64_t kMaxSteps = 1 << 15;     // steps a plan may have
 constexpr int kMaxSimulations = 96;          // candidates simulated per plan
 constexpr int32_t kNever = INT32_MAX;
@@ -42,10 +47,25 @@ struct Geo {
 };
 
 // Fraction of the SMs a launch of an mr x nr block keeps busy (last-wave quantisation).
+// CTA tiles of one kernel launch on an mr x nr block (128 x 256, or 128 x 128 when nr <=
+// 128) and the waves they take: one CTA per SM, and a last wave of at most half the SMs
+// runs as half-width tiles in about half a tile's time.
+int64_t launch_ctas(int64_t mr, int64_t nr) {
+  return ceil_div(mr, kTileM) * ceil_div(nr, nr > 128 ? 256 : 128);
+}
+double launch_waves(int64_t mr, int64_t nr) {
+  const int64_t ctas = launch_ctas(mr, nr);
+  const int64_t full = ctas / kSmCount, tail = ctas % kSmCount;
+  return static_cast<double>(full) + (tail == 0 ? 0.0 : (2 * tail <= kSmCount ? 0.5 : 1.0));
+}
 double wave_efficiency(int64_t mr, int64_t nr) {
-  const int64_t ctas = ceil_div(mr, kTileM) * ceil_div(nr, kTileN);
-  const int64_t waves = ceil_div(ctas, kSmCount);
-  return static_cast<double>(ctas) / static_cast<double>(waves * kSmCount);
+  return static_cast<double>(launch_ctas(mr, nr)) / (launch_waves(mr, nr) * kSmCount);
+}
+
+// Per-step time that does not scale with kr: launch bookkeeping plus one tile fixed cost
+// per wave of the step's C block.
+double step_fixed_s(int64_t mr, int64_t nr) {
+  return kStepOverheadS + launch_waves(mr, nr) * kTileFixedS;
 }
 
 // Builds the step sequence and replays the slot cache.  With `record` false only the
@@ -219,7 +239,8 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
       pl.h2d_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4u;
     if (st.last_k)
       pl.d2h_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4u;
-    compute_s += 2.0 * mr * nr * kr / lim.flops_per_s / wave_efficiency(mr, nr) + kStepOverheadS;
+    compute_s += 2.0 * mr * nr * kr / lim.flops_per_s / wave_efficiency(mr, nr) +
+                 step_fixed_s(mr, nr);
   }
 
   pl.flops = 2.0 * static_cast<double>(p.m) * static_cast<double>(p.n) * static_cast<double>(p.k);
@@ -292,13 +313,13 @@ PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* ou
             continue;
           // A block smaller than one wave of CTAs wastes SMs on every launch; skip it
           // unless the problem itself is that small (or the geometry is forced).
-          if (!forced && ceil_div(std::min(mb, p.m), kTileM) * ceil_div(std::min(nb, p.n), kTileN) <
-                             kSmCount &&
+          if (!forced && launch_ctas(std::min(mb, p.m), std::min(nb, p.n)) < kSmCount &&
               (mb < p.m || nb < p.n))
             continue;
           const double lb = std::max({flops / lim.flops_per_s /
                                           wave_efficiency(std::min(mb, p.m), std::min(nb, p.n)) +
-                                          steps * kStepOverheadS,
+                                          steps * step_fixed_s(std::min(mb, p.m),
+                                                               std::min(nb, p.n)),
                                       min_h2d / lim.h2d_bytes_per_s,
                                       min_d2h / lim.d2h_bytes_per_s});
           cands.push_back({Geo{mb, nb, kb, order == 1}, lb});
