@@ -271,6 +271,120 @@ def run_out_of_core(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------- strong-scaled partitioned SGEMM (C4)
+def run_sharded_c4(args) -> None:
+    """BASELINE config 4's form (NN, beta 0, C rows sharded over the GPUs, B read from the
+    host once per node and all-gathered over NVLink) as one fixed total problem, M x N x K
+    = --c4-m x --c4-n x --c4-k, split over however many ranks run it (strong scaling).
+    Full C4 (256 GiB of C, 32 GiB of B in every rank's host memory) does not fit the host
+    RAM of one box; the default 65536 x 65536 x 16384 keeps its shape class.  Each step is
+    one xvram_b200_sgemm_sharded call from pinned host memory to pinned host memory,
+    timed between barriers, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from xvram_b200 import device as xd
+    from xvram_b200 import shard
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    Mt, Nt, Kt = args.c4_m, args.c4_n, args.c4_k
+    per = (Mt + world - 1) // world
+    r0 = min(Mt, rank * per)
+    mr = min(Mt, r0 + per) - r0
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.Stream(device=dev)
+    peak = measure_ffma_peak(dev, stream)
+    h2d, d2h = measure_link(dev, stream, barrier)
+    h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
+    # op N operands: A_local is mr x K (rows r0.. of the seeded M x K matrix), B is K x N.
+    a_h = torch.empty((Kt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x K
+    b_h = torch.empty((Nt, Kt), dtype=torch.float32).pin_memory()           # column-major K x N
+    c_h = torch.empty((Nt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x N
+    for kk in range(0, Kt, 1024):  # A_local column k holds rows r0..r0+mr of column k
+        rows = a_h[kk:kk + 1024]
+        for j in range(rows.shape[0]):
+            xd.fill_uniform(rows[j, :mr], 40, first_index=(kk + j) * Mt + r0)
+    xd.fill_uniform(b_h, 41)
+    uid = shard.exchange_unique_id(rank) if world > 1 else shard.unique_id()
+    group = shard.ShardGroup(uid, rank, world)
+
+    def step():
+        st = group.sgemm(0, 0, mr, Nt, Kt, 1.0, a_h, max(mr, 1), b_h, Kt, 0.0, c_h,
+                         max(mr, 1), panel_k=2048)
+        assert st == 0, st
+
+    for _ in range(args.warmup):
+        step()
+    times = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            barrier()
+            t0 = time.perf_counter()
+            step()
+            barrier()
+            times.append(max_over_ranks(time.perf_counter() - t0))
+    group.close()
+    # spot check: a few outputs of this rank against FP64 (the operands' generator is
+    # counter-based, so any element can be recomputed)
+    import numpy as np
+    rng = np.random.default_rng(rank)
+    rows = rng.integers(0, max(mr, 1), 4)
+    cols = rng.integers(0, Nt, 4)
+    worst = 0.0
+    if mr > 0:
+        for r, c in zip(rows, cols):
+            arow = a_h[:, int(r)].double().numpy()
+            bcol = b_h[c].double().numpy()
+            ref = float(arow @ bcol)
+            worst = max(worst, abs(float(c_h[c, r]) - ref) / Kt)
+    worst = max_over_ranks(worst)
+    sec = statistics.median(times)
+    flop = 2.0 * Mt * Nt * Kt
+    t_compute = flop / world / (peak * 1e12)
+    h2d_rank = 4.0 * (per * Kt + Kt * Nt / world)
+    d2h_rank = 4.0 * per * Nt
+    t_roof = max(t_compute, h2d_rank / (h2d * 1e9), d2h_rank / (d2h * 1e9))
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC,
+            "workload": f"C4 form, strong-scaled: {Mt} x {Nt} x {Kt} NN beta 0, C rows over "
+                        f"{world} GPU(s), B from host once per node + NCCL all-gather",
+            "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * sec, "scaling": "strong",
+            "step_ms": [round(1e3 * t, 2) for t in times],
+            "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
+                         "p_fp32_tflops_per_gpu": peak, "h2d_gbs_concurrent": h2d,
+                         "d2h_gbs_concurrent": d2h,
+                         "bound": "fp32" if t_compute >= max(h2d_rank / (h2d * 1e9),
+                                                             d2h_rank / (d2h * 1e9)) else "host-link"},
+            "check": {"sampled_outputs_per_rank": 4, "max_abs_err_over_k_vs_fp64": worst},
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------- MLP workload (C5)
 def run_mlp(args) -> None:
     """BASELINE config 5 through the SDK (include/xvram.h): 24 x Linear(16384 -> 16384,
@@ -750,9 +864,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c2", "c3s", "c5"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3s", "c4s", "c5"], default="c2",
                     help="c2: the headline (BASELINE config 2); c3s: one out-of-core GEMM; "
+                         "c4s: config 4's partitioned form, strong-scaled over the ranks; "
                          "c5: the 24-layer MLP (BASELINE config 5) through the SDK")
+    ap.add_argument("--c4-m", type=int, default=65536)
+    ap.add_argument("--c4-n", type=int, default=65536)
+    ap.add_argument("--c4-k", type=int, default=16384)
     ap.add_argument("--mlp-features", type=int, default=16384)
     ap.add_argument("--mlp-batch", type=int, default=512)
     ap.add_argument("--mlp-layers", type=int, default=24)
@@ -770,6 +888,9 @@ def main() -> None:
         return
     if args.workload == "c5":
         run_mlp(args)
+        return
+    if args.workload == "c4s":
+        run_sharded_c4(args)
         return
     main_gpu(args)
 
