@@ -130,6 +130,7 @@ public:
     rc.chunk_bytes = config->session.chunk_size_bytes;
     rc.cache_target_bytes = config->session.cache_target_bytes;
     rc.headroom_bytes = config->session.device_headroom_bytes;
+    rc.budget_poll_ms = config->session.budget_poll_ms;
     Error err;
     try {
       DeviceScope scope(rc.device_ordinal);

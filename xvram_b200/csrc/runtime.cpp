@@ -57,7 +57,10 @@ struct Runtime::Impl {
   xvram_session_telemetry_v1 t{};
   RuntimeExtra x;
   uint64_t cb = 0;       // chunk bytes
-  uint64_t capacity = 0; // frames the budget allows
+  uint64_t capacity = 0; // frames the budget allows now
+  uint64_t max_capacity = 0; // frames of the budget at open (the scratch range is this big)
+  std::chrono::steady_clock::time_point last_budget_sample{};
+  uint32_t growth_samples = 0;
   std::vector<Frame> frames;
   std::map<uint64_t, Alloc> allocs;
   uint64_t next_id = 1;
@@ -302,6 +305,80 @@ struct Runtime::Impl {
     return {};
   }
 
+  // Live budget (reference src/residency/runtime.cpp:3213-3468): between operations, the
+  // pool may hold at most (free device memory + its own frames - headroom), capped by the
+  // budget it opened with.  A lower figure releases frames at once (free ones first, then
+  // least recently used ones, written back when dirty); a higher one is taken only after
+  // three consecutive samples agree.
+  Error apply_budget(bool force) {
+    const auto now = std::chrono::steady_clock::now();
+    if (!force && cfg.budget_poll_ms > 0 &&
+        now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms))
+      return {};
+    last_budget_sample = now;
+    uint64_t free_b = 0, total_b = 0;
+    if (Error e = dev->mem_get_info(&free_b, &total_b))
+      return e;
+    ++t.budget_sample_count;
+    t.cuda_free_bytes_end = free_b;
+    t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, free_b);
+    const uint64_t reclaimable = free_b + static_cast<uint64_t>(frames.size()) * cb;
+    const uint64_t after = reclaimable > cfg.headroom_bytes ? reclaimable - cfg.headroom_bytes : 0;
+    const uint64_t target = std::max<uint64_t>(2, std::min(after / cb, max_capacity));
+    if (target < capacity) {
+      growth_samples = 0;
+      while (frames.size() > target) {
+        size_t victim = frames.size();
+        uint64_t oldest = UINT64_MAX;
+        for (size_t i = 0; i < frames.size(); ++i) {
+          if (frames[i].owner == kArenaOwner)
+            continue;
+          const uint64_t key = frames[i].owner ? frames[i].touch + 1 : 0; // free frames first
+          if (key < oldest) {
+            oldest = key;
+            victim = i;
+          }
+        }
+        if (victim == frames.size())
+          return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "budget", "shrink",
+                            "no frame can be released");
+        if (Error e = evict_frame(victim))
+          return e;
+        if (Error e = wait_idle(frames[victim]))
+          return e;
+        Frame gone = frames[victim];
+        if (Error e = dev->handle_release(gone.handle))
+          return e;
+        dev->event_destroy(gone.last_use);
+        dev->event_destroy(gone.ready);
+        ++t.physical_handles_released;
+        // Keep the vector dense: the last frame takes the victim's index.
+        if (victim + 1 != frames.size()) {
+          frames[victim] = frames.back();
+          const Frame& moved = frames[victim];
+          if (moved.owner && moved.owner != kArenaOwner)
+            allocs.at(moved.owner).chunks[moved.chunk].frame = static_cast<int32_t>(victim);
+        }
+        frames.pop_back();
+      }
+      capacity = target;
+      ++t.budget_shrinks;
+      t.cache_target_bytes = capacity * cb;
+      t.cache_target_minimum_bytes = std::min(t.cache_target_minimum_bytes, capacity * cb);
+      update_resident();
+    } else if (target > capacity) {
+      if (++growth_samples >= 3) {
+        growth_samples = 0;
+        capacity = target;
+        ++t.budget_grows;
+        t.cache_target_bytes = capacity * cb;
+      }
+    } else {
+      growth_samples = 0;
+    }
+    return {};
+  }
+
   Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
                       const std::set<std::pair<uint64_t, uint32_t>>& keep, uint64_t ws);
   Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
@@ -388,8 +465,10 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
   if (m.capacity < 2)
     return make_error(XVRAM_STATUS_DEVICE_OUT_OF_MEMORY, "runtime", "open",
                       "device budget is smaller than two frames");
+  m.max_capacity = m.capacity;
+  m.last_budget_sample = std::chrono::steady_clock::now();
   m.t.cache_target_bytes = m.capacity * m.cb;
-  m.t.cache_target_minimum_bytes = 2 * m.cb;
+  m.t.cache_target_minimum_bytes = m.capacity * m.cb; // lowest target seen so far
   m.t.cache_target_maximum_bytes = usable;
   m.t.cuda_driver_version = static_cast<uint32_t>(m.info.driver_version);
   m.t.cuda_free_bytes_minimum = free_b;
@@ -741,9 +820,13 @@ Error Runtime::describe_gemm(const GemmCall& call, GemmLayout* out) {
   return {};
 }
 
+Error Runtime::refresh_budget() { return impl_->apply_budget(true); }
+
 Error Runtime::gemm(const GemmCall& call) {
   Impl& m = *impl_;
   const auto t0 = std::chrono::steady_clock::now();
+  if (Error e = m.apply_budget(false))
+    return e;
   Alloc& A = m.allocs.at(call.shape.a.allocation_id);
   Alloc& B = m.allocs.at(call.shape.b.allocation_id);
   Alloc& C = m.allocs.at(call.shape.c.allocation_id);
@@ -1059,6 +1142,8 @@ Error Runtime::prefetch(const std::vector<AccessRange>& ranges) {
   Impl& m = *impl_;
   if (Error e = m.check_ranges(ranges, "prefetch"))
     return e;
+  if (Error e = m.apply_budget(false))
+    return e;
   std::set<std::pair<uint64_t, uint32_t>> keep;
   for (const AccessRange& r : ranges)
     m.range_chunks(m.allocs.at(r.allocation_id), r.offset_bytes, r.length_bytes, &keep);
@@ -1080,6 +1165,8 @@ Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t work
   Impl& m = *impl_;
   const auto t0 = std::chrono::steady_clock::now();
   if (Error e = m.check_ranges(ranges, "transaction"))
+    return e;
+  if (Error e = m.apply_budget(false))
     return e;
   std::set<std::pair<uint64_t, uint32_t>> keep;
   for (const AccessRange& r : ranges)

@@ -43,6 +43,10 @@ struct RuntimeConfig {
   uint64_t chunk_bytes = 64ull << 20;
   uint64_t cache_target_bytes = 0; // 0 = free device memory at open minus headroom
   uint64_t headroom_bytes = 512ull << 20;
+  // Live budget: at operation boundaries, at most this often, the runtime samples the
+  // device's free memory and shrinks (or, after repeated samples with room, regrows up to
+  // the budget it opened with) its frame pool to free + own frames - headroom.
+  uint64_t budget_poll_ms = 100;
   // Planning rates (estimates only; they steer geometry choice, never correctness).
   double flops_per_s = 70e12;
   double h2d_bytes_per_s = 50e9;
@@ -135,6 +139,8 @@ public:
                     const TransactionBody& body);
   bool live(uint64_t id) const;
   uint64_t allocation_bytes(uint64_t id) const;
+  // Samples the device now (ignoring the poll interval) and applies the live budget.
+  Error refresh_budget();
   Error synchronize();
   Error mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes);
 

@@ -219,6 +219,7 @@ public:
       rc.chunk_bytes = cfg_.chunk_size_bytes;
       rc.cache_target_bytes = cfg_.cache_target_bytes;
       rc.headroom_bytes = cfg_.device_headroom_bytes;
+      rc.budget_poll_ms = cfg_.budget_poll_ms;
       DeviceFactory factory = device_factory();
       std::unique_ptr<Device> dev = factory ? factory() : nullptr;
       if (!dev)
