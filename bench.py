@@ -738,6 +738,19 @@ def main_gpu(args) -> None:
     e2e_s = (time.perf_counter() - t0) / args.steps
     barrier()
     e2e_s_max = max_over_ranks(e2e_s)
+    trace_records = None
+    if args.trace and rank == 0:
+        # one more step, outside the timed region, in the reference's trace format
+        from xvram_b200.report import TracedCompat
+        with open(args.trace, "w") as sink:
+            tr = TracedCompat(api, sink)
+            tr.h2d(da, a_h.data_ptr(), a_h.nbytes)
+            tr.h2d(db, b_h.data_ptr(), b_h.nbytes)
+            tr.h2d(dc, c_h.data_ptr(), c_h.nbytes)
+            api.check("sgemm", tr.sgemm(h, OP_A, OP_B, M, N, K, ALPHA, da, K, db, K, BETA, dc, M))
+            tr.d2h(c_out.data_ptr(), dc, c_out.nbytes)
+            tr.close()
+            trace_records = tr.records
     tel = api.telemetry()
     info = cp.runtime_info()
     # the same steps with the handle in TF32 tensor-op math mode (three-term TF32 kernel)
@@ -846,6 +859,9 @@ def main_gpu(args) -> None:
                         "path": "compat ABI, blas_set_math_mode(3)"},
                 "clocks": tc_clocks.summary(),
             },
+            "compat_trace": ({"path": args.trace, "records": trace_records,
+                              "format": "xvram.cuda_compat_trace v1 (JSON lines)"}
+                             if trace_records is not None else None),
             "gpu_launches": args.steps * (1 + int(OP_A == 1) + int(OP_B == 0)),
             "gpu_launches_e2e": launches_e2e,
             "clocks": clocks.summary(),
@@ -864,6 +880,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", default=None,
+                    help="write one extra compat e2e step as xvram.cuda_compat_trace JSON lines")
     ap.add_argument("--workload", choices=["c2", "c3s", "c4s", "c5"], default="c2",
                     help="c2: the headline (BASELINE config 2); c3s: one out-of-core GEMM; "
                          "c4s: config 4's partitioned form, strong-scaled over the ranks; "

@@ -1,0 +1,96 @@
+"""Compat-call trace records in the reference's trace format.
+
+The reference's compat bench writes one JSON object per line for every compat API call it
+makes: a `call` record before, a `return` record after, a `retired_tile` record for each
+GEMM tile retired in between (observed from the telemetry's tile counter) and one `final`
+record (reference src/compat_bench/main.cpp:105-200, src/compat_bench/report.cpp:390-410,
+schemas/cuda-compat-trace-v1.schema.json). `TracedCompat` produces the same records around
+`xvram_b200.compat.CompatApi`, so tools that read the reference's traces read these.
+
+Record fields (all required): schema_version 1, report_type "xvram.cuda_compat_trace",
+sequence (from 1), monotonic_timestamp_ns (since the tracer started), operation_id,
+allocation_id (integer or null), transition ("call" | "return" | "retired_tile" |
+"final"), bytes, tiles_retired (cumulative), reason.
+"""
+from __future__ import annotations
+
+import json
+import time
+from typing import IO, Optional
+
+TRANSITIONS = ("call", "return", "retired_tile", "final")
+
+
+def trace_record(sequence: int, timestamp_ns: int, transition: str, operation_id: int,
+                 allocation_id: Optional[int], nbytes: int, tiles_retired: int,
+                 reason: str) -> dict:
+    if transition not in TRANSITIONS:
+        raise ValueError(f"unknown transition {transition!r}")
+    if sequence < 1 or timestamp_ns < 0 or operation_id < 0 or nbytes < 0 or tiles_retired < 0:
+        raise ValueError("trace counters are non-negative and sequence starts at 1")
+    return {"schema_version": 1, "report_type": "xvram.cuda_compat_trace",
+            "sequence": sequence, "monotonic_timestamp_ns": timestamp_ns,
+            "operation_id": operation_id, "allocation_id": allocation_id,
+            "transition": transition, "bytes": nbytes, "tiles_retired": tiles_retired,
+            "reason": reason}
+
+
+class TracedCompat:
+    """Wraps a CompatApi: every malloc / free / memcpy / sgemm writes call and return
+    records (and the tiles retired in between) to `sink`, one JSON object per line."""
+
+    def __init__(self, api, sink: IO[str]):
+        self.api, self.sink = api, sink
+        self.t0 = time.monotonic_ns()
+        self.sequence = 0
+        self.operation = 0
+        self.tiles = int(api.telemetry().tiles_retired)
+        self.records = 0
+
+    def _emit(self, transition, allocation, nbytes, reason):
+        self.sequence += 1
+        rec = trace_record(self.sequence, time.monotonic_ns() - self.t0, transition,
+                           self.operation if transition != "final" else 0, allocation, nbytes,
+                           self.tiles, reason)
+        self.sink.write(json.dumps(rec, separators=(",", ":")) + "\n")
+        self.records += 1
+
+    def _retired(self):
+        now = int(self.api.telemetry().tiles_retired)
+        while self.tiles < now:
+            self.tiles += 1
+            self._emit("retired_tile", None, 0, "observed_event_retirement")
+
+    def _traced(self, name, allocation, nbytes, fn):
+        self.operation += 1
+        self._emit("call", allocation, nbytes, name)
+        try:
+            out = fn()
+        except Exception:
+            self._retired()
+            self._emit("return", allocation, nbytes, name + ":failed")
+            raise
+        self._retired()
+        self._emit("return", allocation, nbytes, name)
+        return out
+
+    def malloc(self, nbytes):
+        return self._traced("malloc_device", None, nbytes, lambda: self.api.malloc(nbytes))
+
+    def free(self, ptr):
+        return self._traced("free_device", ptr, 0, lambda: self.api.free(ptr))
+
+    def h2d(self, dst, src_ptr, nbytes):
+        return self._traced("memcpy_h2d", dst, nbytes, lambda: self.api.h2d(dst, src_ptr, nbytes))
+
+    def d2h(self, dst_ptr, src, nbytes):
+        return self._traced("memcpy_d2h", src, nbytes, lambda: self.api.d2h(dst_ptr, src, nbytes))
+
+    def sgemm(self, h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc):
+        return self._traced("blas_sgemm", c, 0, lambda: self.api.sgemm(
+            h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc))
+
+    def close(self, ok: bool = True) -> None:
+        self._retired()
+        self._emit("final", None, 0, "completed" if ok else "failed")
+        self.sink.flush()
