@@ -321,3 +321,23 @@ def test_released_allocation_fails_a_plan_and_handles_outlive_close():
     assert keep.release() == sdk.SUCCESS and Cm.release() == sdk.SUCCESS
     t.session_release(s.session)
     s.session = C.c_void_p()
+
+
+def test_sdk_calls_from_a_callback_answer_busy(s):
+    """A transaction callback runs on the session's worker: synchronous SDK calls from it
+    could never run (they queue behind the callback), so they answer BUSY."""
+    Y = s.alloc(4096)
+    seen = {}
+
+    def body(ctx):
+        buf = np.zeros(4, dtype=np.float32)
+        seen["read"] = s.t.allocation_read(Y.handle, 0, buf.ctypes.data, 16)
+        seen["drain"] = s.t.session_drain(s.session, 0)
+        seen["close"] = s.t.session_close(s.session, 0)
+        return 0
+    d = s.transaction_desc([(Y, 0, 4096, sdk.READ)], body)
+    s.check("transaction_execute", s.t.transaction_execute(s.session, C.byref(d),
+                                                           sdk.TIMEOUT_INFINITE))
+    assert seen == {"read": sdk.BUSY, "drain": sdk.BUSY, "close": sdk.BUSY}
+    Y.write(np.ones(1024, dtype=np.float32))  # still open and working
+    assert np.all(download(Y, 1024) == 1.0)

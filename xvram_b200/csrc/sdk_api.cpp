@@ -248,7 +248,13 @@ public:
     return {};
   }
 
+  // True on the session's worker thread, i.e. inside a transaction callback.
+  bool on_worker() const { return worker_.get_id() == std::this_thread::get_id(); }
+
   Error invoke_sync(std::function<Error()> fn) {
+    if (on_worker()) // queued behind the running callback, it could never run
+      return make_error(XVRAM_STATUS_BUSY, "session", "reentrant_call",
+                        "synchronous SDK calls are not allowed from a transaction callback");
     std::shared_ptr<Op> op;
     if (Error e = enqueue([fn = std::move(fn)](Op&) { return fn(); }, 1, 0, &op))
       return e;
@@ -257,6 +263,9 @@ public:
   }
 
   Error drain(uint64_t timeout_ms) {
+    if (on_worker())
+      return make_error(XVRAM_STATUS_BUSY, "session", "reentrant_call",
+                        "session_drain is not allowed from a transaction callback");
     std::unique_lock<std::mutex> lk(qmu_);
     const auto idle = [this] { return queue_.empty() && !active_; };
     if (timeout_ms == XVRAM_TIMEOUT_INFINITE) {
@@ -273,6 +282,9 @@ public:
   Error close(uint64_t timeout_ms) {
     if (closed.load())
       return {};
+    if (on_worker())
+      return make_error(XVRAM_STATUS_BUSY, "session", "reentrant_call",
+                        "session_close is not allowed from a transaction callback");
     std::shared_ptr<Op> op;
     {
       std::lock_guard<std::mutex> lk(qmu_);
@@ -725,6 +737,13 @@ xvram_status XVRAM_CALL session_close_entry(xvram_session session, uint64_t time
 void XVRAM_CALL session_release_entry(xvram_session session) {
   if (!session)
     return;
+  if (session->s && session->s->on_worker()) {
+    // From a transaction callback the session cannot be closed (its worker is running the
+    // callback); the handle stays valid and must be released from another thread.
+    session->s->record(make_error(XVRAM_STATUS_BUSY, "session", "reentrant_call",
+                                  "session_release is not allowed from a transaction callback"));
+    return;
+  }
   try {
     if (session->s && !session->s->closed.load())
       session->s->record(session->s->close(XVRAM_TIMEOUT_INFINITE));
@@ -1096,6 +1115,17 @@ xvram_status XVRAM_CALL operation_wait_entry(xvram_operation op, uint64_t timeou
     return XVRAM_STATUS_INVALID_ARGUMENT;
   return boundary(op->owner, "operation_wait", [&]() -> Error {
     const uint32_t size = out->struct_size;
+    if (op->owner && op->owner->on_worker()) {
+      // Inside a transaction callback every other operation is queued behind it.
+      op->op->poll(out);
+      out->struct_size = size;
+      const bool done = out->state == XVRAM_OPERATION_COMPLETED ||
+                        out->state == XVRAM_OPERATION_CANCELLED ||
+                        out->state == XVRAM_OPERATION_FAILED;
+      return done ? Error{}
+                  : make_error(XVRAM_STATUS_BUSY, "operation", "reentrant_wait",
+                               "waiting from a transaction callback would never finish");
+    }
     Error e = op->op->wait(timeout_ms, out);
     out->struct_size = size;
     return e;
