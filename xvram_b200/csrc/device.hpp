@@ -1,10 +1,9 @@
 // device.hpp -- the runtime's only window onto the GPU.
 //
 // The residency runtime, transfer engine and executor talk to the device through this
-// interface, never to CUDA directly.  CudaDevice (cuda_device.cpp) is the product
-// implementation; tests install a host-memory fake through xvram_b200_test_set_device_factory
-// to drive the scheduling, eviction and failure paths without a GPU, the way the
-// reference's fake driver tables do (reference tests/unit/residency_executor_fake_tests.cpp).
+// interface, never to CUDA directly.  CudaDevice (cuda_device.cpp) is the only
+// implementation; device_factory() is the seam where another one (a host-memory fake, as
+// in the reference's tests/unit/residency_executor_fake_tests.cpp) would be installed.
 //
 // Addresses are plain 64-bit integers (device virtual addresses for the real device).
 #pragma once
