@@ -212,6 +212,16 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_bias_activation(uint64_t y, in
                                                                  uint32_t activation,
                                                                  uint64_t stream);
 
+/*
+ * Testing seam (no reference counterpart, the role of the reference's fake driver tables in
+ * tests/unit/residency_executor_fake_tests.cpp): sessions and the compat adapter created
+ * after this call get their device from `create`, which returns a new object implementing
+ * this library's internal C++ device interface (xvram_b200/csrc/device.hpp) built with
+ * the same compiler -- the host-memory fake in tests/fake_device/.  NULL restores the CUDA
+ * device.  Not for production use.
+ */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_test_set_device_factory(void* (*create)(void));
+
 /* Extra state of the compat adapter's runtime (not in the reference telemetry). */
 typedef struct xvram_b200_runtime_info_v1 {
   uint32_t struct_size;

@@ -95,6 +95,8 @@ def _load() -> C.CDLL:
     lib.xvram_get_api.restype = u32
     lib.xvram_b200_bias_activation.argtypes = [u64, i64, i64, i64, u64, u32, u64]
     lib.xvram_b200_bias_activation.restype = u32
+    lib.xvram_b200_test_set_device_factory.argtypes = [vp]
+    lib.xvram_b200_test_set_device_factory.restype = u32
     return lib
 
 
@@ -105,6 +107,7 @@ EXPORTED = (
     "xvram_cuda_compat_get_api",
     "xvram_get_api",
     "xvram_b200_bias_activation",
+    "xvram_b200_test_set_device_factory",
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",

@@ -7,6 +7,7 @@
 // other CUDA user in the process (PyTorch, NCCL), which is what lets callers mix the
 // adapter with their own device work.
 #include "device.hpp"
+#include "xvram_b200.h"
 #include "kernels.hpp"
 
 #include <cuda.h>
@@ -358,4 +359,19 @@ DeviceFactory& device_factory() {
   return f;
 }
 
+namespace {
+void* (*g_external_factory)(void) = nullptr;
+std::unique_ptr<Device> external_factory() {
+  return std::unique_ptr<Device>(static_cast<Device*>(g_external_factory ? g_external_factory()
+                                                                         : nullptr));
+}
+} // namespace
+
 } // namespace xvram
+
+extern "C" XVRAM_B200_API xvram_status XVRAM_CALL
+xvram_b200_test_set_device_factory(void* (*create)(void)) {
+  xvram::g_external_factory = create;
+  xvram::device_factory() = create ? &xvram::external_factory : &xvram::default_factory;
+  return XVRAM_STATUS_SUCCESS;
+}

@@ -302,53 +302,59 @@ PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* ou
              (p.beta_nonzero ? static_cast<double>(p.m) * p.n : 0.0));
   const double min_d2h = 4.0 * static_cast<double>(p.m) * p.n;
   const bool forced = lim.force_mb || lim.force_nb || lim.force_kb;
-  for (int64_t mb : mbs)
-    for (int64_t nb : nbs)
-      for (int64_t kb : kbs)
-        for (int order = 0; order < 2; ++order) {
-          if (lim.force_order >= 0 && order != lim.force_order)
-            continue;
-          const int64_t steps = ceil_div(p.m, mb) * ceil_div(p.n, nb) * ceil_div(p.k, kb);
-          if (steps > kMaxSteps)
-            continue;
-          // A block smaller than one wave of CTAs wastes SMs on every launch; skip it
-          // unless the problem itself is that small (or the geometry is forced).
-          if (!forced && launch_ctas(std::min(mb, p.m), std::min(nb, p.n)) < kSmCount &&
-              (mb < p.m || nb < p.n))
-            continue;
-          const double lb = std::max({flops / lim.flops_per_s /
-                                          wave_efficiency(std::min(mb, p.m), std::min(nb, p.n)) +
-                                          steps * step_fixed_s(std::min(mb, p.m),
-                                                               std::min(nb, p.n)),
-                                      min_h2d / lim.h2d_bytes_per_s,
-                                      min_d2h / lim.d2h_bytes_per_s});
-          cands.push_back({Geo{mb, nb, kb, order == 1}, lb});
-        }
-  std::stable_sort(cands.begin(), cands.end(),
-                   [](const Cand& x, const Cand& y) { return x.lb < y.lb; });
-
   bool found = false;
   Geo best{};
   Plan trial, best_plan;
   int considered = 0;
-  for (const Cand& cd : cands) {
-    if (found && (cd.lb > best_plan.est_seconds || considered >= kMaxSimulations))
-      break;
-    if (!simulate(p, lim, cd.g, false, &trial))
-      continue;
-    ++considered;
-    const bool better =
-        !found || trial.est_seconds < best_plan.est_seconds * (1 - 1e-9) ||
-        (trial.est_seconds <= best_plan.est_seconds * (1 + 1e-9) &&
-         (trial.h2d_bytes < best_plan.h2d_bytes ||
-          (trial.h2d_bytes == best_plan.h2d_bytes &&
-           trial.blocks_m * trial.blocks_n * trial.panels_k <
-               best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k)));
-    if (better) {
-      found = true;
-      best = cd.g;
-      best_plan = trial;
+  // Blocks smaller than one wave of CTAs waste SMs on every launch: they are considered
+  // only when nothing else fits the budget (second pass).
+  for (int pass = 0; pass < 2; ++pass) {
+    cands.clear();
+    for (int64_t mb : mbs)
+      for (int64_t nb : nbs)
+        for (int64_t kb : kbs)
+          for (int order = 0; order < 2; ++order) {
+            if (lim.force_order >= 0 && order != lim.force_order)
+              continue;
+            const int64_t steps = ceil_div(p.m, mb) * ceil_div(p.n, nb) * ceil_div(p.k, kb);
+            if (steps > kMaxSteps)
+              continue;
+            const bool small = launch_ctas(std::min(mb, p.m), std::min(nb, p.n)) < kSmCount &&
+                               (mb < p.m || nb < p.n);
+            if (!forced && small != (pass == 1))
+              continue;
+            const double lb = std::max({flops / lim.flops_per_s /
+                                            wave_efficiency(std::min(mb, p.m), std::min(nb, p.n)) +
+                                            steps * step_fixed_s(std::min(mb, p.m),
+                                                                 std::min(nb, p.n)),
+                                        min_h2d / lim.h2d_bytes_per_s,
+                                        min_d2h / lim.d2h_bytes_per_s});
+            cands.push_back({Geo{mb, nb, kb, order == 1}, lb});
+          }
+    std::stable_sort(cands.begin(), cands.end(),
+                     [](const Cand& x, const Cand& y) { return x.lb < y.lb; });
+
+    for (const Cand& cd : cands) {
+      if (found && (cd.lb > best_plan.est_seconds || considered >= kMaxSimulations))
+        break;
+      if (!simulate(p, lim, cd.g, false, &trial))
+        continue;
+      ++considered;
+      const bool better =
+          !found || trial.est_seconds < best_plan.est_seconds * (1 - 1e-9) ||
+          (trial.est_seconds <= best_plan.est_seconds * (1 + 1e-9) &&
+           (trial.h2d_bytes < best_plan.h2d_bytes ||
+            (trial.h2d_bytes == best_plan.h2d_bytes &&
+             trial.blocks_m * trial.blocks_n * trial.panels_k <
+                 best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k)));
+      if (better) {
+        found = true;
+        best = cd.g;
+        best_plan = trial;
+      }
     }
+    if (found || forced)
+      break;
   }
   if (!found)
     return PlanStatus::budget_too_small;

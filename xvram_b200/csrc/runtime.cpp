@@ -768,9 +768,11 @@ PlanLimits Runtime::Impl::streamed_limits(const GemmCall& call) const {
   lim.flops_per_s = call.flops_per_s > 0 ? call.flops_per_s : cfg.flops_per_s;
   lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
   lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
-  lim.transpose_a = !call.tensor_cores && s.op_a != 0;
-  lim.transpose_b = !call.tensor_cores && s.op_b == 0;
-  lim.tf32x3 = call.tensor_cores;
+  // Workspace per step is whatever the device's kernel asks for: transposes of K-major
+  // panels (FFMA) or the hi/lo split (tensor cores).
+  lim.transpose_a = !call.tensor_cores && dev->sgemm_workspace(s.op_a, 1, 128, 128, 128, false) > 0;
+  lim.transpose_b = !call.tensor_cores && dev->sgemm_workspace(0, s.op_b, 128, 128, 128, false) > 0;
+  lim.tf32x3 = call.tensor_cores && dev->sgemm_workspace(0, 1, 128, 128, 128, true) > 0;
   return lim;
 }
 

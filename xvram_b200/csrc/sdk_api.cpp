@@ -96,6 +96,7 @@ public:
 
   std::function<Error(Op&)> body;
   bool closes_session = false; // runs even on a poisoned session
+  bool read_only = false;      // diagnostics (telemetry): also run on a poisoned session
 
   bool expired() const { return has_deadline_ && Clock::now() >= deadline_; }
   Error deadline_error(const char* stage, const char* op) const {
@@ -236,12 +237,13 @@ public:
   }
 
   Error enqueue(std::function<Error(Op&)> body, uint64_t units, uint64_t deadline_ms,
-                std::shared_ptr<Op>* out) {
+                std::shared_ptr<Op>* out, bool read_only = false) {
     std::lock_guard<std::mutex> lk(qmu_);
     if (closing_)
       return make_error(XVRAM_STATUS_CLOSED, "session", "submit", "the session is closed");
     auto op = std::make_shared<Op>(next_op_++, units, deadline_ms);
     op->body = std::move(body);
+    op->read_only = read_only; // before the worker can see it
     queue_.push_back(op);
     qcv_.notify_all();
     *out = std::move(op);
@@ -251,12 +253,12 @@ public:
   // True on the session's worker thread, i.e. inside a transaction callback.
   bool on_worker() const { return worker_.get_id() == std::this_thread::get_id(); }
 
-  Error invoke_sync(std::function<Error()> fn) {
+  Error invoke_sync(std::function<Error()> fn, bool read_only = false) {
     if (on_worker()) // queued behind the running callback, it could never run
       return make_error(XVRAM_STATUS_BUSY, "session", "reentrant_call",
                         "synchronous SDK calls are not allowed from a transaction callback");
     std::shared_ptr<Op> op;
-    if (Error e = enqueue([fn = std::move(fn)](Op&) { return fn(); }, 1, 0, &op))
+    if (Error e = enqueue([fn = std::move(fn)](Op&) { return fn(); }, 1, 0, &op, read_only))
       return e;
     (void)op->wait(XVRAM_TIMEOUT_INFINITE, nullptr);
     return op->error();
@@ -330,10 +332,12 @@ public:
 
   Error telemetry(xvram_session_telemetry_v1* out) {
     if (!closed.load()) {
-      if (Error e = invoke_sync([this]() -> Error {
-            snapshot();
-            return {};
-          }))
+      if (Error e = invoke_sync(
+              [this]() -> Error {
+                snapshot();
+                return {};
+              },
+              true))
         if (e.status != XVRAM_STATUS_CLOSED)
           return e;
     }
@@ -367,7 +371,7 @@ private:
         const xvram_session_telemetry_v1 before =
             opened_ ? rt_.counters() : xvram_session_telemetry_v1{};
         Error e;
-        if (poisoned_ && !op->closes_session) {
+        if (poisoned_ && !op->closes_session && !op->read_only) {
           e = make_error(XVRAM_STATUS_POISONED, "session", "execute",
                          "an earlier failure left the device state undefined");
         } else {
