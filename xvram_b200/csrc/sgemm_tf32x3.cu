@@ -31,8 +31,10 @@
 //                 per k8 step, tcgen05.mma.cta_group::2.kind::tf32 lo*hi, hi*lo (cross-term
 //                 accumulator) and hi*hi (M=256, N=256), and commits each stage back to
 //                 both CTAs' producers;
-//     warps 2..5  epilogue per CTA: tcgen05.ld 32 lanes x 16 columns of both accumulators,
-//                 sum, alpha/beta, stores coalesced along M.
+//     warps 2..9  epilogue per CTA, two warps per TMEM lane quarter splitting the columns:
+//                 tcgen05.ld 32 lanes x 16 columns of both accumulators, sum, alpha/beta,
+//                 stores coalesced along M (the epilogue is not overlapped with MMAs --
+//                 both accumulators fill TMEM -- so its length counts directly).
 // All waits are bounded; a timeout sets a bit in the kernel error word, the CTA drains
 // what it issued, frees its TMEM and returns.
 #include "device_common.cuh"
@@ -61,7 +63,7 @@ constexpr int kPairN = 256;
 constexpr int kRows = 128;              // rows of A and of B each CTA stages
 constexpr int kBK = 32;                 // tf32 elements per stage row (128 bytes)
 constexpr int kStages = 3;
-constexpr int kThreads = 192;           // 6 warps
+constexpr int kThreads = 320;           // 10 warps: producer, MMA, 8 epilogue
 constexpr uint32_t kTile = kRows * kBK * 4;          // 16 KB: one of A_hi, A_lo, B_hi, B_lo
 constexpr uint32_t kStageBytes = 4 * kTile;          // 64 KB per CTA per stage
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
@@ -295,12 +297,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- epilogue
+    // Two epilogue warps per TMEM lane quarter (a warp may only read lanes 32 * (warp % 4)
+    // onwards), each taking half of the 256 columns.
     const int quad = warp & 3; // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
+    const int col_begin = ((warp - 2) >> 2) * (kPairN / 2);
+    const int col_end = col_begin + kPairN / 2;
     const int row = m0 + 32 * quad + lane;
     // While the MMAs run, pull this thread's row of the C tile into L2: a warp's 32 rows of
     // one column are one 128-byte line, so the epilogue's reads below hit L2.
     if (p.beta != 0.0f && row < p.m) {
-      for (int c = 0; c < kPairN; ++c) {
+      for (int c = col_begin; c < col_end; ++c) {
         const int col = pn0 + c;
         if (col < p.n)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(p.c + row + static_cast<long long>(col) * p.ldc));
@@ -315,7 +321,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // tcgen05.ld is warp-collective: decide for the whole warp at once.
     if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
       const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-      for (int c0 = 0; c0 < kPairN; c0 += 16) {
+      for (int c0 = col_begin; c0 < col_end; c0 += 16) {
         float v[16], w[16];
         tmem_ld16(t_row + c0, v);
         tmem_ld16(t_row + kSmallCol + c0, w);
