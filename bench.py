@@ -14,8 +14,9 @@ end-to-end leg reads 1/N of B per rank from the host and all-gathers it over NVL
   e2e     the same metric through the reference-facing C ABI (xvram_cuda_compat_get_api):
           per step memcpy(H2D) of A, B, C from pinned host buffers, blas_sgemm, and
           memcpy(D2H) of C -- exactly what a reference caller does.
-  roofline  achieved kernel TFLOP/s against the FP32 (FFMA) pipe peak measured in the
-          same run by xvram_b200_ffma_probe; `traffic` comes from the committed ncu
+  roofline  achieved kernel TFLOP/s against the FP32 pipe peak measured in the same run:
+          the higher of the scalar FFMA and packed FFMA2 probes (xvram_b200_ffma_probe,
+          xvram_b200_ffma2_probe); `traffic` comes from the committed ncu
           summary profiles/sgemm_ffma_c2_traffic.json when present.
   host_link  pinned H2D/D2H GB/s measured here with every rank copying at once; the e2e
           roofline is max(FLOP / P_fp32, operand bytes / BW_host).
@@ -128,37 +129,52 @@ def run_reference_arm(args) -> None:
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs.
+
+    The sampler is live before the region starts: entering waits (up to 10 s) for
+    nvidia-smi's first line, and leaving waits (up to 2 s) for one line after the region,
+    so even a region shorter than the 50 ms sampling interval is bracketed by samples.
+    `summary` uses the samples taken inside the region, or the two that bracket it when
+    the region fell between samples."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, str]] = []
+        self.t_begin = self.t_end = 0.0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
-            time.sleep(0.3)
+            deadline = time.monotonic() + 10.0
+            while not self.samples and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.t_begin = time.monotonic()
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.samples.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *exc):
+        self.t_end = time.monotonic()
         if self.proc:
-            time.sleep(0.15)
+            deadline = self.t_end + 2.0
+            while (time.monotonic() < deadline and self.proc.poll() is None and
+                   not any(t >= self.t_end for t, _ in self.samples)):
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -166,26 +182,38 @@ class ClockSampler:
                 self.proc.kill()
             self.thread.join(timeout=2)
 
-    def summary(self) -> dict:
-        sm, smax, reasons = [], 0.0, set()
+    @staticmethod
+    def _parse(line: str):
+        parts = [p.strip() for p in line.split(",")]
+        if len(parts) < 9:
+            return None
+        try:
+            sm, smax = float(parts[1]), float(parts[2])
+        except ValueError:
+            return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = max(smax, float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+        active = {n for n, v in zip(names, parts[5:9]) if v.lower().startswith("active")}
+        return sm, smax, active
+
+    def summary(self) -> dict:
+        parsed = [(t, r) for t, r in ((t, self._parse(l)) for t, l in self.samples) if r]
+        inside = [r for t, r in parsed if self.t_begin <= t <= self.t_end]
+        how = "inside the timed region"
+        if not inside:
+            before = [r for t, r in parsed if t < self.t_begin][-1:]
+            after = [r for t, r in parsed if t > self.t_end][:1]
+            inside = before + after
+            how = "bracketing the timed region (shorter than the sampling interval)"
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [r[0] for r in inside]
+        smax = max(r[1] for r in inside)
+        reasons = set().union(*(r[2] for r in inside))
         loaded = [x for x in sm if x > 0.5 * smax] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "sampled": how,
+                "region_ms": round(1e3 * (self.t_end - self.t_begin), 1),
+                "interval_ms": self.INTERVAL_MS}
 
 
 # ---------------------------------------------------------------- out-of-core workload
@@ -206,7 +234,7 @@ def run_out_of_core(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=dev)
-    peak_tflops = measure_ffma_peak(dev, stream)
+    peak_tflops, probes = measure_fp32_peak(dev, stream)
     h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
 
     api = cp.CompatApi()
@@ -250,7 +278,8 @@ def run_out_of_core(args) -> None:
         "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": len(times),
         "ms_per_step": 1e3 * sec, "dtype": "f32", "data": "synthetic",
         "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
-                     "p_fp32_tflops": peak_tflops, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs,
+                     "p_fp32_tflops": peak_tflops, "fp32_probes": probes, "h2d_gbs": h2d_gbs,
+                     "d2h_gbs": d2h_gbs,
                      "bound": "fp32" if flop / (peak_tflops * 1e12) >= alg_h2d / (h2d_gbs * 1e9)
                      else "host-link"},
         "host_link": {"h2d_bytes": h2d_b, "d2h_bytes": d2h_b,
@@ -313,7 +342,7 @@ def run_sharded_c4(args) -> None:
         return float(t.item())
 
     stream = torch.cuda.Stream(device=dev)
-    peak = measure_ffma_peak(dev, stream)
+    peak, probes = measure_fp32_peak(dev, stream)
     h2d, d2h = measure_link(dev, stream, barrier)
     h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
     # op N operands: A_local is mr x K (rows r0.. of the seeded M x K matrix), B is K x N.
@@ -373,7 +402,7 @@ def run_sharded_c4(args) -> None:
             "warmup": args.warmup, "ms_per_step": 1e3 * sec, "scaling": "strong",
             "step_ms": [round(1e3 * t, 2) for t in times],
             "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
-                         "p_fp32_tflops_per_gpu": peak, "h2d_gbs_concurrent": h2d,
+                         "p_fp32_tflops_per_gpu": peak, "fp32_probes": probes, "h2d_gbs_concurrent": h2d,
                          "d2h_gbs_concurrent": d2h,
                          "bound": "fp32" if t_compute >= max(h2d_rank / (h2d * 1e9),
                                                              d2h_rank / (d2h * 1e9)) else "host-link"},
@@ -407,7 +436,7 @@ def run_mlp(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=dev)
-    peak_tflops = measure_ffma_peak(dev, stream)
+    peak_tflops, probes = measure_fp32_peak(dev, stream)
     h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
     wbytes = F * F * 4
     abytes = F * BATCH * 4
@@ -476,7 +505,8 @@ def run_mlp(args) -> None:
         "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
                      "bound": "host-link" if alg_h2d / (h2d_gbs * 1e9) > flop / (peak_tflops * 1e12)
                      else "fp32",
-                     "p_fp32_tflops": peak_tflops, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs},
+                     "p_fp32_tflops": peak_tflops, "fp32_probes": probes, "h2d_gbs": h2d_gbs,
+                     "d2h_gbs": d2h_gbs},
         "host_link": {"h2d_bytes_per_step": h2d_moved, "algorithmic_h2d_bytes": alg_h2d,
                       "achieved_h2d_gbs": h2d_moved / sec / 1e9},
         "check": {"sampled_batch_rows": cols, "max_abs_err_vs_fp64": err,
@@ -493,8 +523,9 @@ def run_mlp(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def measure_ffma_peak(dev, stream, iters: int = 8000) -> float:
-    """FP32 pipe peak (TFLOP/s) from the FFMA probe: ~15 ms launches, best of 7."""
+def measure_ffma_peak(dev, stream, iters: int = 8000, packed: bool = False) -> float:
+    """FP32 pipe peak (TFLOP/s) from the FFMA probe (scalar FFMA, or packed FFMA2 with
+    `packed`): ~15 ms launches, best of 7."""
     import torch
     from xvram_b200 import device as xd
     sink = torch.zeros(1, device=dev)
@@ -505,12 +536,20 @@ def measure_ffma_peak(dev, stream, iters: int = 8000) -> float:
         for i in range(8):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            assert xd.ffma_probe(blocks, iters, sink, stream) == 0
+            assert xd.ffma_probe(blocks, iters, sink, stream, packed=packed) == 0
             e1.record(stream)
             e1.synchronize()
             if i:
                 best = max(best, 2.0 * blocks * 256 * iters * 512 / (e0.elapsed_time(e1) * 1e-3))
     return best / 1e12
+
+
+def measure_fp32_peak(dev, stream) -> tuple[float, dict]:
+    """The FP32 pipe peak as the higher of the scalar and packed probes (the SGEMM main
+    loop issues packed FMAs), with both figures for the record."""
+    scalar = measure_ffma_peak(dev, stream)
+    packed = measure_ffma_peak(dev, stream, packed=True)
+    return max(scalar, packed), {"ffma_probe": scalar, "ffma2_probe": packed}
 
 
 def cublas_tf32_tflops(dev) -> float:
@@ -622,7 +661,7 @@ def main_gpu(args) -> None:
     # FP32 pipe peak on this device, this run (FFMA probe), repeated after the kernel's
     # timed region so both see a warm clock; pinned host-link bandwidth.
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    peak_tflops = measure_ffma_peak(dev, stream)
+    peak_tflops, probes = measure_fp32_peak(dev, stream)
     h2d, d2h = measure_link(dev, stream, barrier)
     # the job's host link is as slow as its slowest GPU's
     h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
@@ -650,7 +689,9 @@ def main_gpu(args) -> None:
     torch.cuda.synchronize()
     barrier()
     assert xd.kernel_status(stream) == 0
-    peak_tflops = max(peak_tflops, measure_ffma_peak(dev, stream))
+    peak_again, probes_again = measure_fp32_peak(dev, stream)
+    peak_tflops = max(peak_tflops, peak_again)
+    probes = {key: max(probes[key], probes_again[key]) for key in probes}
     kernel_ms = start.elapsed_time(stop) / args.steps
     kernel_ms_max = max_over_ranks(kernel_ms)
     value = world * FLOP / (kernel_ms_max * 1e-3) / 1e12
@@ -805,7 +846,10 @@ def main_gpu(args) -> None:
                        "seeds": "A 10, B 11, C 12 (counter-based uniform[-1,1))"},
             "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak_tflops,
                          "unit": "TFLOP/s", "frac": achieved / peak_tflops, "traffic": traffic,
-                         "peak_source": "measured FFMA probe (xvram_b200_ffma_probe), this run",
+                         "peak_source": "measured FP32 pipe probes, this run: the higher of scalar "
+                                        "FFMA (xvram_b200_ffma_probe) and packed FFMA2 "
+                                        "(xvram_b200_ffma2_probe)",
+                         "probes": probes,
                          "peak_nominal_at_sampled_clock":
                              sms * 128 * 2 * (clocks.summary()["sm_mhz"] or 0) * 1e6 / 1e12},
             "host_link": {"h2d_gbs": h2d, "d2h_gbs": d2h, "concurrent_ranks": world,

@@ -161,6 +161,11 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int32_t iterations,
                                                              float* sink, uint64_t stream);
 
+/* The same probe with packed FP32 FMAs (two per lane per instruction, 8 float2 chains per
+ * thread, the same 512 FMAs per thread per iteration, so the same FLOP formula). */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma2_probe(int32_t blocks, int32_t iterations,
+                                                              float* sink, uint64_t stream);
+
 /*
  * Multi-GPU partitioned SGEMM (no reference counterpart: the reference is single-GPU,
  * src/cuda_compat/adapter.cpp:595-600).  One process or thread per GPU:

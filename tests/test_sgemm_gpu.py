@@ -182,10 +182,12 @@ def test_repeat_calls_are_deterministic(oracle):
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
 
 
-def test_ffma_probe_runs():
+@pytest.mark.parametrize("packed", [False, True])
+def test_ffma_probe_runs(packed):
     sink = torch.zeros(1, device="cuda")
-    assert device.ffma_probe(148, 8, sink) == 0
+    assert device.ffma_probe(148, 8, sink, packed=packed) == 0
     torch.cuda.synchronize()
+    assert float(sink[0]) == 0.0
 
 
 @pytest.mark.parametrize("op_a,op_b", [(1, 0), (0, 0), (1, 1)])

@@ -87,6 +87,8 @@ def _load() -> C.CDLL:
     lib.xvram_b200_validate_gemm.restype = i32
     lib.xvram_b200_ffma_probe.argtypes = [i32, i32, vp, u64]
     lib.xvram_b200_ffma_probe.restype = u32
+    lib.xvram_b200_ffma2_probe.argtypes = [i32, i32, vp, u64]
+    lib.xvram_b200_ffma2_probe.restype = u32
     lib.xvram_b200_compat_runtime_info.argtypes = [C.POINTER(RuntimeInfo)]
     lib.xvram_b200_compat_runtime_info.restype = u32
     lib.xvram_cuda_compat_get_api.argtypes = [u32, u32, vp]
@@ -122,5 +124,6 @@ EXPORTED = (
     "xvram_b200_plan_steps",
     "xvram_b200_validate_gemm",
     "xvram_b200_ffma_probe",
+    "xvram_b200_ffma2_probe",
     "xvram_b200_compat_runtime_info",
 )

@@ -54,6 +54,7 @@ cudaError_t read_and_clear_kernel_error_tc(unsigned int* out, cudaStream_t strea
 unsigned long long kernel_wait_limit_ns();
 
 // Host-side probes used by bench.py for its roofline denominators.
-cudaError_t ffma_peak_probe(int blocks, int iterations, float* sink, cudaStream_t stream);
+cudaError_t ffma_peak_probe(int blocks, int iterations, float* sink, cudaStream_t stream,
+                            bool packed = false);
 
 } // namespace xvram

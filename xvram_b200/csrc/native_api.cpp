@@ -292,6 +292,13 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int
   return from_cuda(ffma_peak_probe(blocks, iterations, sink, as_stream(stream)));
 }
 
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma2_probe(int32_t blocks, int32_t iterations,
+                                                              float* sink, uint64_t stream) {
+  if (blocks <= 0 || iterations <= 0 || !sink)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  return from_cuda(ffma_peak_probe(blocks, iterations, sink, as_stream(stream), true));
+}
+
 XVRAM_B200_API xvram_status XVRAM_CALL
 xvram_b200_compat_runtime_info(xvram_b200_runtime_info_v1* out) {
   return compat_runtime_info(out);

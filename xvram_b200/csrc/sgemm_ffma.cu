@@ -56,16 +56,29 @@ namespace {
 #ifndef XVRAM_FFMA_STAGES
 #define XVRAM_FFMA_STAGES 4
 #endif
-// Groups of 4 k unrolled per loop iteration: 2 keeps the loop body (~1,100 instructions)
-// small enough for the instruction cache; the fully unrolled 32-k stage (8) stalls on
-// instruction fetch (ncu: no_instruction 0.61 per issue) and runs ~2 % slower.
+// Groups of 4 k unrolled per loop iteration.  With one FFMA per FMA, 2 keeps the loop
+// body (~1,100 instructions) small enough for the instruction cache; the fully unrolled
+// 32-k stage (8) stalls on instruction fetch (ncu: no_instruction 0.61 per issue) and runs
+// ~2 % slower.  The packed M-/N-major loop has half the FMA instructions and runs best
+// fully unrolled (C2: 1, 2, 4, 8 groups -> 56.9, 55.5, 61.1, 61.5 TFLOP/s).
 #ifndef XVRAM_FFMA_GROUP_UNROLL
 #define XVRAM_FFMA_GROUP_UNROLL 2
+#endif
+#ifndef XVRAM_FFMA_GROUP_UNROLL_MN
+#define XVRAM_FFMA_GROUP_UNROLL_MN 8
+#endif
+// Packed FP32 FMA (FFMA2, sm_100) for N-major B tiles: one instruction updates two
+// adjacent accumulator columns, which halves the FMA issue slots per k and leaves room for
+// the shared-memory loads and address arithmetic.  Per component it is the same
+// round-to-nearest FMA as fmaf, so results are bit-identical either way.
+#ifndef XVRAM_FFMA_PACKED
+#define XVRAM_FFMA_PACKED 1
 #endif
 constexpr int kBM = 128;
 constexpr int kBK = 32;
 constexpr int kStages = XVRAM_FFMA_STAGES;
 constexpr int kGroupUnroll = XVRAM_FFMA_GROUP_UNROLL;
+constexpr int kGroupUnrollMN = XVRAM_FFMA_GROUP_UNROLL_MN;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kAStageFloats = kBM * kBK;
@@ -135,12 +148,15 @@ template <bool KMAJOR> __device__ __forceinline__ int frag_index(int t, int i) {
     return 64 * (i >> 2) + 4 * t + (i & 3);
 }
 
-// One k-group (4 consecutive k) of the B fragment, streamed: calls body(j, b[0..3]) for
-// a K-major tile (b = 4 k of column j) -- see group_ffma below for the N-major form.
-// NJ <= TN: a half-width tile computes only the thread's first NJ columns.
+// Accumulators: acc[i][j / 2] holds columns j (x) and j + 1 (y) of row i.
+__device__ __forceinline__ float& acc_at(float2& pair, int odd) { return odd ? pair.y : pair.x; }
+
+// One k-group (4 consecutive k) of a K-major B tile, streamed one column j at a time
+// (b = 4 k of column j).  NJ <= TN: a half-width tile computes only the thread's first NJ
+// columns.
 template <int TN, int NJ>
 __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const float* bs, int g,
-                                              int tn, float (&acc)[8][NJ]) {
+                                              int tn, float2 (&acc)[8][NJ / 2]) {
   const int chunk = (g ^ (tn & 7)) * 4;
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
@@ -149,33 +165,78 @@ __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const floa
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        acc[i][j] = fmaf(a[kk][i], b[kk], acc[i][j]);
+      for (int i = 0; i < 8; ++i) {
+        float& c = acc_at(acc[i][j >> 1], j & 1);
+        c = fmaf(a[kk][i], b[kk], c);
+      }
   }
 }
 
 // N-major B tile [32 k][BN]: one k row of the thread's TN columns at a time.
+// Columns j and j + 1 (j even) of a thread's fragment are adjacent in an N-major row, so
+// one float4 load gives two column pairs.
 template <int TN, int NJ>
 __device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const float* bs, int g,
-                                              int tn, float (&acc)[8][NJ]) {
+                                              int tn, float2 (&acc)[8][NJ / 2]) {
   constexpr int BN = 16 * TN;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const float* row = bs + (4 * g + kk) * BN + 4 * tn;
-    float b[NJ];
+    float2 b[NJ / 2];
 #pragma unroll
     for (int q = 0; q < NJ / 4; ++q) {
       const float4 v = *reinterpret_cast<const float4*>(row + 64 * q);
-      b[4 * q + 0] = v.x;
-      b[4 * q + 1] = v.y;
-      b[4 * q + 2] = v.z;
-      b[4 * q + 3] = v.w;
+      b[2 * q + 0] = make_float2(v.x, v.y);
+      b[2 * q + 1] = make_float2(v.z, v.w);
     }
+    // Scalar FMAs: with all four k of A held (K-major A), the packed form's duplicated A
+    // values do not fit the register budget.
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < NJ; ++j)
-        acc[i][j] = fmaf(a[kk][i], b[j], acc[i][j]);
+      for (int j2 = 0; j2 < NJ / 2; ++j2) {
+        acc[i][j2].x = fmaf(a[kk][i], b[j2].x, acc[i][j2].x);
+        acc[i][j2].y = fmaf(a[kk][i], b[j2].y, acc[i][j2].y);
+      }
+  }
+}
+
+// M-major A and N-major B (the layout the canonicalising transposes produce): one k at a
+// time, loading that k's 8 A values and NJ B values just before their FMAs, which keeps the
+// packed form's duplicated A values within the register budget.
+template <int TN, int NJ>
+__device__ __forceinline__ void ffma_group_mn(const float* as, const float* bs, int g, int tm,
+                                              int tn, float2 (&acc)[8][NJ / 2]) {
+  constexpr int BN = 16 * TN;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const float* arow = as + (4 * g + kk) * kBM + 4 * tm;
+    const float4 alo = *reinterpret_cast<const float4*>(arow);
+    const float4 ahi = *reinterpret_cast<const float4*>(arow + 64);
+    const float a[8] = {alo.x, alo.y, alo.z, alo.w, ahi.x, ahi.y, ahi.z, ahi.w};
+    const float* brow = bs + (4 * g + kk) * BN + 4 * tn;
+    float2 b[NJ / 2];
+#pragma unroll
+    for (int q = 0; q < NJ / 4; ++q) {
+      const float4 v = *reinterpret_cast<const float4*>(brow + 64 * q);
+      b[2 * q + 0] = make_float2(v.x, v.y);
+      b[2 * q + 1] = make_float2(v.z, v.w);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#if XVRAM_FFMA_PACKED
+      const float2 ai = make_float2(a[i], a[i]);
+#pragma unroll
+      for (int j2 = 0; j2 < NJ / 2; ++j2)
+        acc[i][j2] = __ffma2_rn(ai, b[j2], acc[i][j2]);
+#else
+#pragma unroll
+      for (int j2 = 0; j2 < NJ / 2; ++j2) {
+        acc[i][j2].x = fmaf(a[i], b[j2].x, acc[i][j2].x);
+        acc[i][j2].y = fmaf(a[i], b[j2].y, acc[i][j2].y);
+      }
+#endif
+    }
   }
 }
 
@@ -229,12 +290,12 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
       }
     }
   }
-  float acc[8][NJ];
+  float2 acc[8][NJ / 2];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < NJ; ++j)
-      acc[i][j] = 0.0f;
+    for (int j = 0; j < NJ / 2; ++j)
+      acc[i][j] = make_float2(0.0f, 0.0f);
 
   bool aborted = false;
   for (int kt = 0; kt < p.k_tiles; ++kt) {
@@ -247,14 +308,20 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
     }
     const float* as = smem_a + s * kAStageFloats;
     const float* bs = smem_b + s * Cfg::BStageFloats;
+    if constexpr (!A_KMAJOR && !B_KMAJOR) {
+#pragma unroll kGroupUnrollMN
+      for (int g = 0; g < kBK / 4; ++g)
+        ffma_group_mn<TN, NJ>(as, bs, g, tm, tn, acc);
+    } else {
 #pragma unroll kGroupUnroll
-    for (int g = 0; g < kBK / 4; ++g) {
-      float a[4][8];
-      load_frag<A_KMAJOR>(as, g, tm, a);
-      if constexpr (B_KMAJOR)
-        ffma_group_bk<TN, NJ>(a, bs, g, tn, acc);
-      else
-        ffma_group_bn<TN, NJ>(a, bs, g, tn, acc);
+      for (int g = 0; g < kBK / 4; ++g) {
+        float a[4][8];
+        load_frag<A_KMAJOR>(as, g, tm, a);
+        if constexpr (B_KMAJOR)
+          ffma_group_bk<TN, NJ>(a, bs, g, tn, acc);
+        else
+          ffma_group_bn<TN, NJ>(a, bs, g, tn, acc);
+      }
     }
     __syncwarp();
     if ((tid & 31) == 0)
@@ -308,7 +375,7 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
       for (int i = 0; i < 8; ++i) {
         const int row = m0 + frag_index<A_KMAJOR>(tm, i);
         if (row < p.m) {
-          const float v = alpha * acc[i][j0 + jj];
+          const float v = alpha * acc_at(acc[i][(j0 + jj) >> 1], jj & 1);
           cc[row] = (beta == 0.0f) ? v : fmaf(beta, cv[jj][i], v);
         }
       }

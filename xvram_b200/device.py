@@ -112,5 +112,6 @@ def validate(m, n, k, op_a, op_b, ids, nbytes, offsets, rows, cols, lds) -> tupl
     return err, (op.value.decode() if op.value else "")
 
 
-def ffma_probe(blocks: int, iterations: int, sink, stream=None) -> int:
-    return lib.xvram_b200_ffma_probe(blocks, iterations, sink.data_ptr(), _stream_handle(stream))
+def ffma_probe(blocks: int, iterations: int, sink, stream=None, packed: bool = False) -> int:
+    fn = lib.xvram_b200_ffma2_probe if packed else lib.xvram_b200_ffma_probe
+    return fn(blocks, iterations, sink.data_ptr(), _stream_handle(stream))
