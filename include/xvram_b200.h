@@ -155,6 +155,32 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
     const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
     const uint64_t lds[3], char* operand);
 
+/* xvram_b200_validate_gemm with element types (A, B, C; XVRAM_DATA_* numbering) and an
+ * arithmetic (0 strict FP32, 1 TF32, 2 FP64: the reference's gemm::ComputeMode,
+ * src/gemm/planner.hpp:25-36), following the whole of gemm::validate_problem
+ * (src/gemm/planner.cpp:785-859) including its type rule. */
+XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm_typed(
+    uint64_t m, uint64_t n, uint64_t k, uint32_t op_a, uint32_t op_b,
+    const uint64_t allocation_ids[3], const uint64_t allocation_bytes[3],
+    const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
+    const uint64_t lds[3], const uint32_t data_types[3], int32_t compute, char* operand);
+
+/* Device GEMM of the reference's other type combinations (the per-tile contraction the
+ * reference hands to cuBLASLt / cublasDgemm, src/platform/cublas/cublas_api.cpp:634-918):
+ * FP16 or BF16 A and B with strict FP32 arithmetic and C of the same type or FP32, FP32
+ * (strict or three-term TF32), FP64.  Column-major device pointers aligned to their
+ * element size; alpha and beta in FP64 for FP64 arithmetic, else rounded to FP32.  The
+ * workspace (256-byte aligned, xvram_b200_gemm_typed_workspace_bytes) holds widened or
+ * canonicalised operands.  INVALID_ARGUMENT for an unsupported combination. */
+XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_gemm_typed_workspace_bytes(
+    uint32_t ab_type, uint32_t c_type, int32_t compute, uint32_t op_a, uint32_t op_b, int64_t m,
+    int64_t n, int64_t k);
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_gemm_device_typed(
+    uint32_t ab_type, uint32_t c_type, int32_t compute, uint32_t op_a, uint32_t op_b, int64_t m,
+    int64_t n, int64_t k, double alpha, const void* a, int64_t lda, const void* b, int64_t ldb,
+    double beta, void* c, int64_t ldc, void* workspace, uint64_t workspace_bytes,
+    uint64_t stream);
+
 /* Launches `blocks` x 256 threads of dependent FFMA chains (`iterations` x 512 FFMA per
  * thread) on `stream`; the measured FP32 pipe peak is 2 * blocks * 256 * iterations * 512
  * FLOP over the launch time.  `sink` (device, >= 1 float) defeats dead-code elimination. */

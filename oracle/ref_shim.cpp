@@ -111,6 +111,38 @@ XR_EXPORT int xr_validate_problem(std::uint64_t m, std::uint64_t n, std::uint64_
   return static_cast<int>(v.error);
 }
 
+// gemm::validate_problem with element types (A, B, C; gemm::ElementType order) and a
+// compute mode (gemm::ComputeMode order); values outside the enumerations pass through as
+// they are (the reference's own checks classify them).
+XR_EXPORT int xr_validate_problem_typed(std::uint64_t m, std::uint64_t n, std::uint64_t k,
+                                        int op_a, int op_b, const std::uint64_t* alloc_ids,
+                                        const std::uint64_t* alloc_bytes,
+                                        const std::uint64_t* offsets, const std::uint64_t* rows,
+                                        const std::uint64_t* cols, const std::uint64_t* lds,
+                                        const std::uint32_t* types, int compute, char* operand) {
+  gm::GemmProblem p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  gm::MatrixView* views[3] = {&p.a, &p.b, &p.c};
+  for (int i = 0; i < 3; ++i) {
+    views[i]->allocation_id.value = alloc_ids[i];
+    views[i]->allocation_bytes = alloc_bytes[i];
+    views[i]->offset_bytes = offsets[i];
+    views[i]->rows = rows[i];
+    views[i]->columns = cols[i];
+    views[i]->leading_dimension = lds[i];
+    views[i]->layout = gm::MatrixLayout::column_major;
+    views[i]->element_type = static_cast<gm::ElementType>(types[i]);
+  }
+  p.a_operation = op_a == 0 ? gm::MatrixOperation::none : gm::MatrixOperation::transpose;
+  p.b_operation = op_b == 0 ? gm::MatrixOperation::none : gm::MatrixOperation::transpose;
+  p.compute_mode = static_cast<gm::ComputeMode>(compute);
+  const auto v = gm::validate_problem(p);
+  *operand = v.operand;
+  return static_cast<int>(v.error);
+}
+
 // The reference's CPU FP64 GEMM (cb::reference_result with the full k loop) over the
 // output elements [first, first + count) of an m x n column-major C, on `threads` host
 // threads.  Returns the sum of the results so the work cannot be elided.

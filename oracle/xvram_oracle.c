@@ -172,6 +172,32 @@ XO_EXPORT int xo_gemm_f64(int op_a, int op_b, int64_t m, int64_t n, int64_t k, d
   return rc;
 }
 
+/* FP64-input GEMM for the FP64 arithmetic mode (the reference hands FP64 tiles to
+ * cublasDgemm, src/platform/cublas/cublas_api.cpp:673-676, under the type rule of
+ * src/gemm/planner.cpp:836-839): out = alpha * op(A) op(B) + beta * C with every product
+ * and sum in long double (64-bit significand on x86-64), so the FP64 kernel's rounding
+ * error is measured against a reference that carries 11 more bits.  Column-major,
+ * single-threaded (test sizes).  Returns 0 on success. */
+XO_EXPORT int xo_gemm_f64_inputs(int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                                 double alpha, const double* a, int64_t lda, const double* b,
+                                 int64_t ldb, double beta, const double* c, int64_t ldc,
+                                 double* out, int64_t ldo) {
+  if (m <= 0 || n <= 0 || k < 0 || (op_a != 0 && op_a != 1) || (op_b != 0 && op_b != 1))
+    return 1;
+  for (int64_t col = 0; col < n; ++col)
+    for (int64_t i = 0; i < m; ++i) {
+      long double dot = 0.0L;
+      for (int64_t p = 0; p < k; ++p) {
+        const long double x = op_a == 0 ? a[i + p * lda] : a[p + i * lda];
+        const long double y = op_b == 0 ? b[p + col * ldb] : b[col + p * ldb];
+        dot += x * y;
+      }
+      const long double cv = c ? (long double)c[i + col * ldc] : 0.0L;
+      out[i + col * ldo] = (double)((long double)alpha * dot + (long double)beta * cv);
+    }
+  return 0;
+}
+
 typedef struct {
   int op_a, op_b;
   int64_t k;

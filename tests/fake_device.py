@@ -21,7 +21,7 @@ def build() -> C.CDLL:
     newest = max([SRC.stat().st_mtime] + [h.stat().st_mtime for h in headers])
     if not OUT.exists() or OUT.stat().st_mtime < newest:
         OUT.parent.mkdir(exist_ok=True)
-        subprocess.run(["g++", "-std=c++20", "-O2", "-fPIC", "-shared", f"-I{ROOT / 'include'}",
+        subprocess.run(["g++", "-std=c++20", "-O3", "-march=native", "-fPIC", "-shared", f"-I{ROOT / 'include'}",
                         f"-I{ROOT / 'xvram_b200' / 'csrc'}", str(SRC), "-o", str(OUT)],
                        check=True, capture_output=True)
     lib = C.CDLL(str(OUT))

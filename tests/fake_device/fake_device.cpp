@@ -11,8 +11,9 @@
 //     a physical handle is a memfd of the chunk size, map() places it at the address
 //     (MAP_FIXED | MAP_SHARED) so contents survive unmap / remap like a VMM frame's;
 //   * streams and events are immediate: every operation completes when it is issued;
-//   * sgemm is a plain FP32 loop (fmaf in k order per output), alpha / beta as the
-//     kernels apply them;
+//   * gemm is a plain loop per output in k order: FP32 fmaf for FP32 arithmetic (inputs
+//     of any type widened exactly), FP64 fma for FP64, alpha / beta as the kernels apply
+//     them; C of a narrower type is rounded to nearest even once;
 //   * mem_get_info reports a settable free-byte figure (for the live budget);
 //   * any operation can be made to fail after a number of calls (failure paths).
 #include "device.hpp"
@@ -20,6 +21,7 @@
 #include <sys/mman.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -27,6 +29,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace {
 
@@ -53,6 +56,74 @@ xvram::Error injected(const char* op) {
 }
 
 constexpr uint64_t kGranularity = 2ull << 20;
+
+// IEEE binary16 / bfloat16 <-> float, round to nearest even, written from the format
+// definitions (sign, biased exponent, fraction).
+float half_to_float(uint16_t h) {
+  const int sign = h >> 15, e = (h >> 10) & 31, f = h & 1023;
+  float v;
+  if (e == 0)
+    v = std::ldexp(static_cast<float>(f), -24);
+  else if (e == 31)
+    v = f ? NAN : INFINITY;
+  else
+    v = std::ldexp(static_cast<float>(1024 + f), e - 25);
+  return sign ? -v : v;
+}
+uint16_t float_to_half(float x) {
+  const uint16_t sign = std::signbit(x) ? 0x8000 : 0;
+  if (std::isnan(x))
+    return sign | 0x7e00;
+  const double ax = std::fabs(static_cast<double>(x));
+  if (ax >= 65520.0) // at or past the midpoint between 65504 and 2^16
+    return sign | 0x7c00;
+  if (ax < std::ldexp(1.0, -14)) { // subnormal range: units of 2^-24
+    const double q = std::nearbyint(std::ldexp(ax, 24));
+    return sign | static_cast<uint16_t>(q); // q == 1024 is the smallest normal, as bits
+  }
+  int e = 0;
+  std::frexp(ax, &e); // ax = fr * 2^e, fr in [0.5, 1)
+  e -= 1;             // ax in [2^e, 2^(e+1))
+  double q = std::nearbyint(std::ldexp(ax, 10 - e)); // [1024, 2048]
+  if (q == 2048.0) {
+    q = 1024.0;
+    ++e;
+  }
+  if (e + 15 >= 31)
+    return sign | 0x7c00;
+  return sign | static_cast<uint16_t>(((e + 15) << 10) | (static_cast<int>(q) - 1024));
+}
+float bf16_to_float(uint16_t h) {
+  const uint32_t u = static_cast<uint32_t>(h) << 16;
+  float v;
+  std::memcpy(&v, &u, 4);
+  return v;
+}
+uint16_t float_to_bf16(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  if (std::isnan(x))
+    return static_cast<uint16_t>((u >> 16) | 0x40);
+  u += 0x7fff + ((u >> 16) & 1); // round to nearest, ties to the even upper half
+  return static_cast<uint16_t>(u >> 16);
+}
+
+double load(uint32_t type, uint64_t base, int64_t i) {
+  switch (type) {
+  case xvram::kFp16: return half_to_float(reinterpret_cast<const uint16_t*>(base)[i]);
+  case xvram::kBf16: return bf16_to_float(reinterpret_cast<const uint16_t*>(base)[i]);
+  case xvram::kFp32: return reinterpret_cast<const float*>(base)[i];
+  default: return reinterpret_cast<const double*>(base)[i];
+  }
+}
+void store(uint32_t type, uint64_t base, int64_t i, double v) {
+  switch (type) {
+  case xvram::kFp16: reinterpret_cast<uint16_t*>(base)[i] = float_to_half(static_cast<float>(v)); break;
+  case xvram::kBf16: reinterpret_cast<uint16_t*>(base)[i] = float_to_bf16(static_cast<float>(v)); break;
+  case xvram::kFp32: reinterpret_cast<float*>(base)[i] = static_cast<float>(v); break;
+  default: reinterpret_cast<double*>(base)[i] = v; break;
+  }
+}
 
 class FakeDevice final : public xvram::Device {
 public:
@@ -164,30 +235,64 @@ public:
     return {};
   }
 
-  xvram::Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha,
-                     uint64_t a, int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c,
-                     int64_t ldc, uint64_t, uint64_t, bool, xvram::StreamId) override {
+  xvram::Error gemm(const xvram::GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n,
+                    int64_t k, double alpha, uint64_t a, int64_t lda, uint64_t b, int64_t ldb,
+                    double beta, uint64_t c, int64_t ldc, uint64_t, uint64_t,
+                    xvram::StreamId) override {
     if (should_fail("sgemm"))
       return injected("sgemm");
-    const float* A = reinterpret_cast<const float*>(a);
-    const float* B = reinterpret_cast<const float*>(b);
-    float* Cm = reinterpret_cast<float*>(c);
-    for (int64_t j = 0; j < n; ++j)
-      for (int64_t i = 0; i < m; ++i) {
-        float acc = 0.0f;
-        for (int64_t kk = 0; kk < k; ++kk) {
-          const float x = op_a == 0 ? A[i + kk * lda] : A[kk + i * lda];
-          const float y = op_b == 0 ? B[kk + j * ldb] : B[j + kk * ldb];
-          acc = std::fmaf(x, y, acc);
-        }
-        float& out = Cm[i + j * ldc];
-        const float v = alpha * acc;
-        out = beta == 0.0f ? v : std::fmaf(beta, out, v);
-      }
+    if (t.compute == xvram::kComputeFp64)
+      contract<double>(t, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc);
+    else // strict FP32 (the fake computes TF32 requests in strict FP32 too)
+      contract<float>(t, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc);
     ++gemms;
     return {};
   }
-  uint64_t sgemm_workspace(int, int, int64_t, int64_t, int64_t, bool) override { return 0; }
+  // Per output: one FMA chain in k order in T, then alpha * acc (+ beta * C as one FMA),
+  // stored to C's type.  Operands are widened first (exactly); loops run j, k, i so the
+  // inner loop is contiguous.
+  template <class T>
+  void contract(const xvram::GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                double alpha, uint64_t a, int64_t lda, uint64_t b, int64_t ldb, double beta,
+                uint64_t c, int64_t ldc) {
+    std::vector<T> A(static_cast<size_t>(m * k)), col(static_cast<size_t>(k)),
+        acc(static_cast<size_t>(m));
+    for (int64_t kk = 0; kk < k; ++kk)
+      for (int64_t i = 0; i < m; ++i)
+        A[static_cast<size_t>(i + kk * m)] =
+            static_cast<T>(load(t.ab, a, op_a == 0 ? i + kk * lda : kk + i * lda));
+    for (int64_t j = 0; j < n; ++j) {
+      for (int64_t kk = 0; kk < k; ++kk)
+        col[static_cast<size_t>(kk)] =
+            static_cast<T>(load(t.ab, b, op_b == 0 ? kk + j * ldb : j + kk * ldb));
+      std::fill(acc.begin(), acc.end(), T(0));
+      for (int64_t kk = 0; kk < k; ++kk) {
+        const T y = col[static_cast<size_t>(kk)];
+        const T* ak = A.data() + kk * m;
+        T* ac = acc.data();
+        for (int64_t i = 0; i < m; ++i)
+          ac[i] = std::fma(ak[i], y, ac[i]);
+      }
+      for (int64_t i = 0; i < m; ++i) {
+        const int64_t ci = i + j * ldc;
+        const T v = static_cast<T>(alpha) * acc[static_cast<size_t>(i)];
+        store(t.c, c, ci,
+              beta == 0.0 ? v
+                          : std::fma(static_cast<T>(beta), static_cast<T>(load(t.c, c, ci)), v));
+      }
+    }
+  }
+  uint64_t gemm_workspace(const xvram::GemmTypes&, int, int, int64_t, int64_t, int64_t) override {
+    return 0;
+  }
+  xvram::Error convert(uint32_t st, uint64_t src, int64_t lds, uint32_t dt, uint64_t dst,
+                       int64_t ldd, int64_t rows, int64_t cols, xvram::StreamId) override {
+    for (int64_t j = 0; j < cols; ++j)
+      for (int64_t i = 0; i < rows; ++i)
+        store(dt, dst, i + j * ldd, load(st, src, i + j * lds));
+    ++conversions;
+    return {};
+  }
   xvram::Error kernel_status(xvram::StreamId, uint32_t* word) override {
     *word = 0;
     return {};
@@ -195,7 +300,7 @@ public:
   uint64_t native_stream(xvram::StreamId) override { return 0; }
 
   uint64_t next_id = 0;
-  uint64_t maps = 0, gemms = 0;
+  uint64_t maps = 0, gemms = 0, conversions = 0;
 };
 
 } // namespace

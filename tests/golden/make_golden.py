@@ -60,6 +60,9 @@ def load():
     lib.xr_validate_problem.argtypes = [u64, u64, u64, C.c_int, C.c_int] + [C.POINTER(u64)] * 6 + [
         C.c_char_p]
     lib.xr_validate_problem.restype = C.c_int
+    lib.xr_validate_problem_typed.argtypes = [u64, u64, u64, C.c_int, C.c_int] + \
+        [C.POINTER(u64)] * 6 + [C.POINTER(C.c_uint32), C.c_int, C.c_char_p]
+    lib.xr_validate_problem_typed.restype = C.c_int
     return lib
 
 
@@ -120,6 +123,40 @@ def validation_cases():
          [0, 65536, 0], [m, k, m], [k, n, n], [m, k, m])
     case("overflow", m, n, k, 0, 0, [1, 2, 3], [big, big, big], [0, 0, 0], [m, k, m],
          [k, (1 << 62), n], [m, k, m])
+    return cases
+
+
+def typed_validation_cases():
+    """Element-type and compute-mode cases: every (A, B, C) type triple over the four types
+    under every compute mode on a valid 37 x 19 x 67 NN shape sized for 8-byte elements,
+    plus byte-exact bounds per element size and invalid enumerators."""
+    cases = []
+    m, n, k = 37, 19, 67
+    sz = lambda r, c, ld, e: e * (ld * (c - 1) + r)
+    big = [sz(m, k, m, 8), sz(k, n, k, 8), sz(m, n, m, 8)]
+    base = dict(m=m, n=n, k=k, op_a=0, op_b=0, ids=[1, 2, 3], offsets=[0, 0, 0],
+                rows=[m, k, m], cols=[k, n, n], lds=[m, k, m])
+    for ta in range(4):
+        for tb in range(4):
+            for tc in range(4):
+                for comp in range(3):
+                    cases.append(dict(base, name=f"t{ta}{tb}{tc}_c{comp}", bytes=big,
+                                      types=[ta, tb, tc], compute=comp))
+    esz = {0: 2, 1: 2, 2: 4, 3: 8}
+    for t, comp in ((0, 0), (1, 0), (2, 0), (2, 1), (3, 2)):
+        e = esz[t]
+        exact = [sz(m, k, m, e), sz(k, n, k, e), sz(m, n, m, e)]
+        cases.append(dict(base, name=f"exact_t{t}_c{comp}", bytes=exact, types=[t, t, t], compute=comp))
+        short = [exact[0], exact[1] - 1, exact[2]]
+        cases.append(dict(base, name=f"short_b_t{t}_c{comp}", bytes=short, types=[t, t, t],
+                          compute=comp))
+    cases.append(dict(base, name="half_in_f32_out", bytes=big, types=[0, 0, 2], compute=0))
+    cases.append(dict(base, name="bf16_in_f32_out", bytes=big, types=[1, 1, 2], compute=0))
+    cases.append(dict(base, name="bad_type_a", bytes=big, types=[4, 2, 2], compute=0))
+    cases.append(dict(base, name="bad_type_c", bytes=big, types=[2, 2, 7], compute=0))
+    cases.append(dict(base, name="bad_compute", bytes=big, types=[2, 2, 2], compute=3))
+    cases.append(dict(base, name="mismatch_then_types", bytes=big, types=[0, 2, 2], compute=0,
+                      rows=[m, k + 1, m], lds=[m, k + 1, m]))
     return cases
 
 
@@ -189,6 +226,19 @@ def main() -> None:
         c["operand"] = op.value.decode() if op.value else ""
         vals.append(c)
     out["validation"] = vals
+
+    tvals = []
+    for c in typed_validation_cases():
+        arr = lambda xs: (u64 * 3)(*xs)
+        op = C.create_string_buffer(1)
+        err = lib.xr_validate_problem_typed(c["m"], c["n"], c["k"], c["op_a"], c["op_b"],
+                                            arr(c["ids"]), arr(c["bytes"]), arr(c["offsets"]),
+                                            arr(c["rows"]), arr(c["cols"]), arr(c["lds"]),
+                                            (C.c_uint32 * 3)(*c["types"]), c["compute"], op)
+        c["error"] = err
+        c["operand"] = op.value.decode() if op.value else ""
+        tvals.append(c)
+    out["validation_typed"] = tvals
     out["problem_error_names"] = [
         "none", "zero_dimension", "invalid_allocation", "invalid_layout", "invalid_operation",
         "invalid_element_type", "invalid_compute_mode", "dimension_mismatch",

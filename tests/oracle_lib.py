@@ -53,6 +53,9 @@ class Oracle:
         lib.xo_pv_a.restype = f32
         lib.xo_pv_b.argtypes = [C.c_int, C.c_int]
         lib.xo_pv_b.restype = f32
+        lib.xo_gemm_f64_inputs.argtypes = [C.c_int, C.c_int, i64, i64, i64, f64, vp, i64, vp,
+                                           i64, f64, vp, i64, vp, i64]
+        lib.xo_gemm_f64_inputs.restype = C.c_int
         lib.xo_close_enough.argtypes = [f64, f64]
         lib.xo_close_enough.restype = C.c_int
 
@@ -67,6 +70,18 @@ class Oracle:
         cptr = c.ctypes.data if c is not None else None
         rc = self.lib.xo_gemm_f64(op_a, op_b, m, n, k, alpha, a.ctypes.data, lda, b.ctypes.data,
                                   ldb, beta, cptr, ldc, out.ctypes.data, m, threads)
+        assert rc == 0
+        return out
+
+    def gemm_f64_inputs(self, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc):
+        """FP64-input reference (long double accumulation), (n, m) array."""
+        out = np.empty((n, m), dtype=np.float64)
+        a = np.ascontiguousarray(a, dtype=np.float64)
+        b = np.ascontiguousarray(b, dtype=np.float64)
+        keep = c if c is None else np.ascontiguousarray(c, dtype=np.float64)
+        cptr = keep.ctypes.data if keep is not None else None
+        rc = self.lib.xo_gemm_f64_inputs(op_a, op_b, m, n, k, alpha, a.ctypes.data, lda,
+                                         b.ctypes.data, ldb, beta, cptr, ldc, out.ctypes.data, m)
         assert rc == 0
         return out
 

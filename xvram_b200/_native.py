@@ -85,6 +85,15 @@ def _load() -> C.CDLL:
     lib.xvram_b200_validate_gemm.argtypes = [u64, u64, u64, u32, u32, arr3, arr3, arr3, arr3,
                                              arr3, arr3, C.c_char_p]
     lib.xvram_b200_validate_gemm.restype = i32
+    lib.xvram_b200_validate_gemm_typed.argtypes = [u64, u64, u64, u32, u32, arr3, arr3, arr3,
+                                                   arr3, arr3, arr3, C.POINTER(u32), i32,
+                                                   C.c_char_p]
+    lib.xvram_b200_validate_gemm_typed.restype = i32
+    lib.xvram_b200_gemm_typed_workspace_bytes.argtypes = [u32, u32, i32, u32, u32, i64, i64, i64]
+    lib.xvram_b200_gemm_typed_workspace_bytes.restype = u64
+    lib.xvram_b200_gemm_device_typed.argtypes = [u32, u32, i32, u32, u32, i64, i64, i64, f64, vp,
+                                                 i64, vp, i64, f64, vp, i64, vp, u64, u64]
+    lib.xvram_b200_gemm_device_typed.restype = u32
     lib.xvram_b200_ffma_probe.argtypes = [i32, i32, vp, u64]
     lib.xvram_b200_ffma_probe.restype = u32
     lib.xvram_b200_ffma2_probe.argtypes = [i32, i32, vp, u64]
@@ -123,6 +132,9 @@ EXPORTED = (
     "xvram_b200_plan_panels",
     "xvram_b200_plan_steps",
     "xvram_b200_validate_gemm",
+    "xvram_b200_validate_gemm_typed",
+    "xvram_b200_gemm_typed_workspace_bytes",
+    "xvram_b200_gemm_device_typed",
     "xvram_b200_ffma_probe",
     "xvram_b200_ffma2_probe",
     "xvram_b200_compat_runtime_info",

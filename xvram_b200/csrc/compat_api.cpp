@@ -468,14 +468,15 @@ public:
       s.a = view(*ae, a, op_a == 0 ? s.m : s.k, op_a == 0 ? s.k : s.m, lda);
       s.b = view(*be, b, op_b == 0 ? s.k : s.n, op_b == 0 ? s.n : s.k, ldb);
       s.c = view(*ce, c, s.m, s.n, ldc);
+      // Math mode 3 (CUBLAS_TF32_TENSOR_OP_MATH) selects the three-term TF32 kernel.
+      s.compute = handle(h)->math_mode == 3 ? kTf32 : kStrictFp32;
       const Validation v = validate_gemm(s);
       if (!v)
         return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "compat_preflight", "cublasSgemm",
                           problem_error_name(v.error));
       call.alpha = alpha_v;
       call.beta = beta_v;
-      call.tensor_cores = handle(h)->math_mode == 3;
-      if (call.tensor_cores)
+      if (s.compute == kTf32)
         call.flops_per_s = 150e12; // plan for the tensor-core rate
       if (Error e = runtime_->gemm(call))
         return e;

@@ -280,41 +280,42 @@ public:
     return {};
   }
 
-  Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha, uint64_t a,
-              int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c, int64_t ldc,
-              uint64_t workspace, uint64_t workspace_bytes, bool tensor_cores,
-              StreamId s) override {
+  Error gemm(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+             double alpha, uint64_t a, int64_t lda, uint64_t b, int64_t ldb, double beta,
+             uint64_t c, int64_t ldc, uint64_t workspace, uint64_t workspace_bytes,
+             StreamId s) override {
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
-      return make_error(XVRAM_STATUS_INTERNAL, "executor", "sgemm", "tile exceeds int32");
-    if (tensor_cores && k > 0) {
-      const cudaError_t e = sgemm_tf32x3(
-          op_a, op_b, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), alpha,
-          reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(b), ldb, beta,
-          reinterpret_cast<float*>(c), ldc, reinterpret_cast<void*>(workspace), workspace_bytes,
-          stream(s));
-      if (e != cudaSuccess)
-        return rt_error("sgemm_tf32x3 launch", e);
-      return {};
-    }
-    const cudaError_t e = sgemm_ffma_ws(
-        op_a, op_b, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), alpha,
-        reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(b), ldb, beta,
-        reinterpret_cast<float*>(c), ldc, reinterpret_cast<void*>(workspace), workspace_bytes,
-        stream(s));
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "gemm", "tile exceeds int32");
+    const cudaError_t e =
+        gemm_typed(t.ab, t.c, t.compute, op_a, op_b, static_cast<int>(m), static_cast<int>(n),
+                   static_cast<int>(k), alpha, reinterpret_cast<const void*>(a), lda,
+                   reinterpret_cast<const void*>(b), ldb, beta, reinterpret_cast<void*>(c), ldc,
+                   reinterpret_cast<void*>(workspace), workspace_bytes, stream(s));
     if (e != cudaSuccess)
-      return rt_error("sgemm_ffma launch", e);
+      return rt_error(t.compute == kTf32 ? "sgemm_tf32x3 launch"
+                      : t.ab == kFp64    ? "dgemm launch"
+                                         : "sgemm_ffma launch",
+                      e);
     return {};
   }
 
-  uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k,
-                           bool tensor_cores) override {
+  uint64_t gemm_workspace(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n,
+                          int64_t k) override {
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
       return 0;
-    if (tensor_cores)
-      return sgemm_tf32x3_workspace_bytes(static_cast<int>(m), static_cast<int>(n),
-                                          static_cast<int>(k));
-    return sgemm_workspace_bytes(op_a, op_b, static_cast<int>(m), static_cast<int>(n),
-                                 static_cast<int>(k));
+    return gemm_typed_workspace_bytes(t.ab, t.c, t.compute, op_a, op_b, static_cast<int>(m),
+                                      static_cast<int>(n), static_cast<int>(k));
+  }
+
+  Error convert(uint32_t src_type, uint64_t src, int64_t lds, uint32_t dst_type, uint64_t dst,
+                int64_t ldd, int64_t rows, int64_t cols, StreamId s) override {
+    if (rows > INT32_MAX || cols > INT32_MAX)
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "convert", "block exceeds int32");
+    XV_RT("convert_matrix",
+          convert_matrix(src_type, reinterpret_cast<const void*>(src), lds, dst_type,
+                         reinterpret_cast<void*>(dst), ldd, static_cast<int>(rows),
+                         static_cast<int>(cols), stream(s)));
+    return {};
   }
 
   Error kernel_status(StreamId s, uint32_t* word) override {

@@ -9,6 +9,7 @@
 #pragma once
 
 #include "status.hpp"
+#include "validate.hpp"
 
 #include <cstdint>
 #include <memory>
@@ -30,6 +31,13 @@ using StreamId = uint64_t;
 using EventId = uint64_t;
 
 enum class CopyDir { h2d, d2h, d2d };
+
+// Element types and arithmetic of one device GEMM (validate.hpp's DataType / ComputeKind).
+struct GemmTypes {
+  uint32_t ab = kFp32; // A and B
+  uint32_t c = kFp32;
+  int compute = kStrictFp32;
+};
 
 class Device {
 public:
@@ -67,16 +75,21 @@ public:
                         uint64_t width, uint64_t height, CopyDir dir, StreamId s) = 0;
   virtual Error memset_d32(uint64_t dst, uint32_t value, uint64_t count, StreamId s) = 0;
 
-  // C = alpha * op(A) op(B) + beta * C on device addresses (column-major FP32).  With
-  // `workspace_bytes` >= sgemm_workspace_bytes K-major operands are canonicalised there.
-  // `tensor_cores` selects the three-term TF32 tcgen05 kernel instead of the FFMA kernel.
-  virtual Error sgemm(int op_a, int op_b, int64_t m, int64_t n, int64_t k, float alpha,
-                      uint64_t a, int64_t lda, uint64_t b, int64_t ldb, float beta, uint64_t c,
-                      int64_t ldc, uint64_t workspace, uint64_t workspace_bytes, bool tensor_cores,
-                      StreamId s) = 0;
-  // Workspace the chosen kernel needs for this problem (0 if none).
-  virtual uint64_t sgemm_workspace(int op_a, int op_b, int64_t m, int64_t n, int64_t k,
-                                   bool tensor_cores) = 0;
+  // C = alpha * op(A) op(B) + beta * C on device addresses (column-major), for the
+  // element types and arithmetic in `t`: strict FP32 (FFMA kernel), three-term TF32
+  // (tcgen05 kernel), FP16 / BF16 inputs (widened, FFMA kernel), FP64.  The workspace
+  // (gemm_workspace bytes) holds canonicalised or widened operands.
+  virtual Error gemm(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                     double alpha, uint64_t a, int64_t lda, uint64_t b, int64_t ldb, double beta,
+                     uint64_t c, int64_t ldc, uint64_t workspace, uint64_t workspace_bytes,
+                     StreamId s) = 0;
+  // Workspace that gemm needs for this problem (0 if none).
+  virtual uint64_t gemm_workspace(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n,
+                                  int64_t k) = 0;
+  // dst (rows x cols, column-major, ldd) = src converted between FP16 / BF16 and FP32
+  // (round to nearest even when narrowing).
+  virtual Error convert(uint32_t src_type, uint64_t src, int64_t lds, uint32_t dst_type,
+                        uint64_t dst, int64_t ldd, int64_t rows, int64_t cols, StreamId s) = 0;
   // Reads and clears the sticky error word of the library's kernels (synchronising s).
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
   // The native handle of stream s (a cudaStream_t) handed to transaction callbacks.

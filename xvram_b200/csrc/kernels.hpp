@@ -47,6 +47,23 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
                          long long ldc, void* workspace, uint64_t workspace_bytes,
                          cudaStream_t stream);
 
+// GEMM of any supported element-type combination (types and arithmetic numbered as
+// validate.hpp's DataType and ComputeKind): FP32 runs sgemm_ffma_ws or sgemm_tf32x3;
+// FP16 / BF16 inputs are widened into the workspace and run on the FFMA kernel (strict
+// FP32 arithmetic, C FP32 or rounded to the input type once at the end); FP64 runs the
+// FP64 tensor-core kernel.  Needs gemm_typed_workspace_bytes of 256-byte-aligned scratch;
+// pointers must be aligned to their element size (cudaErrorInvalidValue otherwise).
+uint64_t gemm_typed_workspace_bytes(uint32_t ab_type, uint32_t c_type, int compute, int op_a,
+                                    int op_b, int m, int n, int k);
+cudaError_t gemm_typed(uint32_t ab_type, uint32_t c_type, int compute, int op_a, int op_b, int m,
+                       int n, int k, double alpha, const void* a, long long lda, const void* b,
+                       long long ldb, double beta, void* c, long long ldc, void* workspace,
+                       uint64_t workspace_bytes, cudaStream_t stream);
+// dst (rows x cols, ldd) = src converted between FP16 / BF16 and FP32 (round to nearest
+// even when narrowing).
+cudaError_t convert_matrix(uint32_t src_type, const void* src, long long lds, uint32_t dst_type,
+                           void* dst, long long ldd, int rows, int cols, cudaStream_t stream);
+
 // Reads (synchronising `stream`) and clears the device's sticky kernel error word.
 cudaError_t read_and_clear_kernel_error(unsigned int* out, cudaStream_t stream);
 cudaError_t read_and_clear_kernel_error_tc(unsigned int* out, cudaStream_t stream);

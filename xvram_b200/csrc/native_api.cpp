@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace xvram {
@@ -283,6 +284,65 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
   if (operand)
     *operand = v.operand;
   return static_cast<int32_t>(v.error);
+}
+
+XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm_typed(
+    uint64_t m, uint64_t n, uint64_t k, uint32_t op_a, uint32_t op_b,
+    const uint64_t allocation_ids[3], const uint64_t allocation_bytes[3],
+    const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
+    const uint64_t lds[3], const uint32_t data_types[3], int32_t compute, char* operand) {
+  GemmShape s;
+  s.m = m;
+  s.n = n;
+  s.k = k;
+  s.op_a = static_cast<int>(op_a);
+  s.op_b = static_cast<int>(op_b);
+  s.compute = compute;
+  MatrixRef* mats[3] = {&s.a, &s.b, &s.c};
+  for (int i = 0; i < 3; ++i) {
+    mats[i]->allocation_id = allocation_ids[i];
+    mats[i]->allocation_bytes = allocation_bytes[i];
+    mats[i]->offset_bytes = offsets[i];
+    mats[i]->rows = rows[i];
+    mats[i]->columns = columns[i];
+    mats[i]->ld = lds[i];
+    mats[i]->dtype = data_types[i];
+  }
+  const Validation v = validate_gemm(s);
+  if (operand)
+    *operand = v.operand;
+  return static_cast<int32_t>(v.error);
+}
+
+XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_gemm_typed_workspace_bytes(
+    uint32_t ab_type, uint32_t c_type, int32_t compute, uint32_t op_a, uint32_t op_b, int64_t m,
+    int64_t n, int64_t k) {
+  if (op_a > 1 || op_b > 1 || m <= 0 || n <= 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
+      k > INT32_MAX || !supported_types(ab_type, c_type, compute))
+    return 0;
+  return gemm_typed_workspace_bytes(ab_type, c_type, compute, static_cast<int>(op_a),
+                                    static_cast<int>(op_b), static_cast<int>(m),
+                                    static_cast<int>(n), static_cast<int>(k));
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_gemm_device_typed(
+    uint32_t ab_type, uint32_t c_type, int32_t compute, uint32_t op_a, uint32_t op_b, int64_t m,
+    int64_t n, int64_t k, double alpha, const void* a, int64_t lda, const void* b, int64_t ldb,
+    double beta, void* c, int64_t ldc, void* workspace, uint64_t workspace_bytes,
+    uint64_t stream) {
+  if (op_a > 1 || op_b > 1 || m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX ||
+      k > INT32_MAX || !supported_types(ab_type, c_type, compute))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  if (m == 0 || n == 0)
+    return XVRAM_STATUS_SUCCESS;
+  const int64_t a_rows = op_a == 0 ? m : k, b_rows = op_b == 0 ? k : n;
+  if (!a || !b || !c || lda < std::max<int64_t>(1, a_rows) || ldb < std::max<int64_t>(1, b_rows) ||
+      ldc < m)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  return from_cuda(gemm_typed(ab_type, c_type, compute, static_cast<int>(op_a),
+                              static_cast<int>(op_b), static_cast<int>(m), static_cast<int>(n),
+                              static_cast<int>(k), alpha, a, lda, b, ldb, beta, c, ldc, workspace,
+                              workspace_bytes, as_stream(stream)));
 }
 
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_ffma_probe(int32_t blocks, int32_t iterations,

@@ -85,18 +85,26 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
   if (nsteps > kMaxSteps)
     return false;
   const uint64_t q = lim.quantum_bytes ? lim.quantum_bytes : 1;
-  pl.slot_bytes = round_up(static_cast<uint64_t>(std::max(g.mb, g.nb)) * g.kb * 4u, q);
-  pl.c_slot_bytes = round_up(static_cast<uint64_t>(g.mb) * g.nb * 4u, q);
+  const uint64_t cblock = static_cast<uint64_t>(g.mb) * static_cast<uint64_t>(g.nb);
+  pl.slot_bytes = round_up(static_cast<uint64_t>(std::max(g.mb, g.nb)) * g.kb * lim.ab_bytes, q);
+  if (lim.c_host_bytes < lim.c_acc_bytes) { // accumulator, then the stored-type staging copy
+    pl.c_stage_offset = round_up(cblock * lim.c_acc_bytes, 256);
+    pl.c_slot_bytes = round_up(pl.c_stage_offset + cblock * lim.c_host_bytes, q);
+  } else {
+    pl.c_slot_bytes = round_up(cblock * lim.c_acc_bytes, q);
+  }
   const int64_t blocks = pl.blocks_m * pl.blocks_n;
   pl.c_slots = blocks > 1 ? 2 : 1;
   {
     const auto up = [](uint64_t v, uint64_t m) { return (v + m - 1) / m * m; };
     uint64_t ws = 0;
-    if (lim.transpose_a)
+    if (lim.step_workspace)
+      ws = lim.step_workspace(g.mb, g.nb, g.kb);
+    else if (lim.transpose_a)
       ws += up(up(static_cast<uint64_t>(g.mb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
-    if (lim.transpose_b)
+    if (!lim.step_workspace && lim.transpose_b)
       ws += up(up(static_cast<uint64_t>(g.nb), 4) * static_cast<uint64_t>(g.kb) * 4u, 256);
-    if (lim.tf32x3)
+    if (!lim.step_workspace && lim.tf32x3)
       ws = 2 * up(static_cast<uint64_t>(g.mb) * up(static_cast<uint64_t>(g.kb), 4) * 4u, 256) +
            2 * up(static_cast<uint64_t>(g.nb) * up(static_cast<uint64_t>(g.kb), 4) * 4u, 256);
     pl.workspace_bytes = round_up(ws, q);
@@ -168,7 +176,7 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
     const int64_t kr = std::min<int64_t>(g.kb, p.k - kp * g.kb);
     const int64_t rr = operand == 0 ? std::min<int64_t>(g.mb, p.m - block * g.mb)
                                     : std::min<int64_t>(g.nb, p.n - block * g.nb);
-    return static_cast<uint64_t>(kr) * static_cast<uint64_t>(rr) * 4u;
+    return static_cast<uint64_t>(kr) * static_cast<uint64_t>(rr) * lim.ab_bytes;
   };
 
   double compute_s = 0;
@@ -236,9 +244,9 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
     const int64_t nr = std::min<int64_t>(g.nb, p.n - static_cast<int64_t>(st.bn) * g.nb);
     const int64_t kr = std::min<int64_t>(g.kb, p.k - static_cast<int64_t>(st.bk) * g.kb);
     if (st.first_k && p.beta_nonzero)
-      pl.h2d_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4u;
+      pl.h2d_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * lim.c_host_bytes;
     if (st.last_k)
-      pl.d2h_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4u;
+      pl.d2h_bytes += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * lim.c_host_bytes;
     compute_s += 2.0 * mr * nr * kr / lim.flops_per_s / wave_efficiency(mr, nr) +
                  step_fixed_s(mr, nr);
   }
@@ -248,11 +256,12 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
   // first step's operands and draining the last C block.
   const auto& s0 = steps.front();
   double head = (panel_bytes(0, s0.bm, s0.bk) + panel_bytes(1, s0.bn, s0.bk)) / lim.h2d_bytes_per_s;
-  const double cblock = static_cast<double>(std::min<int64_t>(g.mb, p.m)) *
-                        static_cast<double>(std::min<int64_t>(g.nb, p.n)) * 4.0;
+  const double cblock_bytes = static_cast<double>(std::min<int64_t>(g.mb, p.m)) *
+                              static_cast<double>(std::min<int64_t>(g.nb, p.n)) *
+                              lim.c_host_bytes;
   if (p.beta_nonzero)
-    head += cblock / lim.h2d_bytes_per_s;
-  const double tail = cblock / lim.d2h_bytes_per_s;
+    head += cblock_bytes / lim.h2d_bytes_per_s;
+  const double tail = cblock_bytes / lim.d2h_bytes_per_s;
   pl.est_seconds = std::max({compute_s, pl.h2d_bytes / lim.h2d_bytes_per_s,
                              pl.d2h_bytes / lim.d2h_bytes_per_s}) +
                    head + tail;
@@ -268,7 +277,8 @@ bool simulate(const PlanProblem& p, const PlanLimits& lim, const Geo& g, bool re
 PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* out) {
   if (p.m <= 0 || p.n <= 0 || p.k <= 0 || (p.op_a != 0 && p.op_a != 1) ||
       (p.op_b != 0 && p.op_b != 1) || lim.budget_bytes == 0 || lim.flops_per_s <= 0 ||
-      lim.h2d_bytes_per_s <= 0 || lim.d2h_bytes_per_s <= 0)
+      lim.h2d_bytes_per_s <= 0 || lim.d2h_bytes_per_s <= 0 || lim.ab_bytes == 0 ||
+      lim.c_acc_bytes == 0 || lim.c_host_bytes == 0)
     return PlanStatus::invalid;
 
   std::vector<int64_t> mbs = lim.force_mb ? std::vector<int64_t>{lim.force_mb}
@@ -298,9 +308,10 @@ PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* ou
   const double flops = 2.0 * static_cast<double>(p.m) * static_cast<double>(p.n) *
                        static_cast<double>(p.k);
   const double min_h2d =
-      4.0 * (static_cast<double>(p.m) * p.k + static_cast<double>(p.k) * p.n +
-             (p.beta_nonzero ? static_cast<double>(p.m) * p.n : 0.0));
-  const double min_d2h = 4.0 * static_cast<double>(p.m) * p.n;
+      static_cast<double>(lim.ab_bytes) *
+          (static_cast<double>(p.m) * p.k + static_cast<double>(p.k) * p.n) +
+      (p.beta_nonzero ? static_cast<double>(lim.c_host_bytes) * p.m * p.n : 0.0);
+  const double min_d2h = static_cast<double>(lim.c_host_bytes) * p.m * p.n;
   const bool forced = lim.force_mb || lim.force_nb || lim.force_kb;
   bool found = false;
   Geo best{};

@@ -20,6 +20,7 @@
 #pragma once
 
 #include <cstdint>
+#include <functional>
 #include <vector>
 
 namespace xvram {
@@ -42,6 +43,14 @@ struct PlanLimits {
   bool transpose_a = false, transpose_b = false;
   // Tensor-core steps instead: hi/lo split copies of both panels (2 x (mb + nb) x kb floats).
   bool tf32x3 = false;
+  // When set, the per-step workspace for an mb x nb x kb step (replaces the three flags
+  // above: the executor asks the device's kernel for it).
+  std::function<uint64_t(int64_t mb, int64_t nb, int64_t kb)> step_workspace;
+  // Element bytes: A / B panels and their host copies; the C block as the kernel
+  // accumulates it in its slot; C on the host.  A C stored narrower than it accumulates
+  // (FP16 / BF16 C of an FP32-arithmetic GEMM) also needs a staging copy of the block in
+  // its slot for the conversions on the way in and out.
+  uint32_t ab_bytes = 4, c_acc_bytes = 4, c_host_bytes = 4;
   int force_order = -1;                             // -1 search, 0 m-outer, 1 n-outer
 };
 
@@ -69,6 +78,7 @@ struct Plan {
   int64_t blocks_m = 0, blocks_n = 0, panels_k = 0;
   uint64_t slot_bytes = 0;   // panel slot size (multiple of quantum)
   uint64_t c_slot_bytes = 0; // C block slot size (multiple of quantum)
+  uint64_t c_stage_offset = 0; // staging copy inside a C slot (0: none, C kept as stored)
   uint64_t workspace_bytes = 0; // per-step canonicalisation workspace (multiple of quantum)
   int32_t panel_slots = 0;
   int32_t c_slots = 0;

@@ -17,6 +17,17 @@ constexpr uint64_t kArenaOwner = UINT64_MAX;
 // GEMMs.  Its chunks are never "written", so evicting them is free (no write-back).
 constexpr uint64_t kScratchId = UINT64_MAX - 1;
 
+// The device GEMM of a whole problem: the types as declared.
+GemmTypes gemm_types(const GemmShape& s) { return {s.a.dtype, s.c.dtype, s.compute}; }
+// The device GEMM of one out-of-core step: an FP16 / BF16 C accumulates across K panels in
+// FP32 in its slot and is rounded to its type once, when the block is written back.
+GemmTypes step_types(const GemmShape& s) {
+  GemmTypes t = gemm_types(s);
+  if ((s.c.dtype == kFp16 || s.c.dtype == kBf16) && s.compute == kStrictFp32)
+    t.c = kFp32;
+  return t;
+}
+
 struct Chunk {
   int32_t frame = -1;         // frame index while resident
   bool written = false;       // holds caller data (else contents are undefined)
@@ -750,9 +761,8 @@ void Runtime::Impl::gemm_chunks(const GemmCall& call, std::set<std::pair<uint64_
   }
   // The kernel's canonicalisation workspace comes out of the same frame budget.
   const GemmShape& sh = call.shape;
-  *ws = dev->sgemm_workspace(sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
-                             static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k),
-                             call.tensor_cores);
+  *ws = dev->gemm_workspace(gemm_types(sh), sh.op_a, sh.op_b, static_cast<int64_t>(sh.m),
+                            static_cast<int64_t>(sh.n), static_cast<int64_t>(sh.k));
   const uint64_t ws_chunks = (*ws + cb - 1) / cb;
   const size_t data_chunks = keep->size();
   for (uint64_t c = 0; c < ws_chunks && c < capacity; ++c)
@@ -769,10 +779,16 @@ PlanLimits Runtime::Impl::streamed_limits(const GemmCall& call) const {
   lim.h2d_bytes_per_s = cfg.h2d_bytes_per_s;
   lim.d2h_bytes_per_s = cfg.d2h_bytes_per_s;
   // Workspace per step is whatever the device's kernel asks for: transposes of K-major
-  // panels (FFMA) or the hi/lo split (tensor cores).
-  lim.transpose_a = !call.tensor_cores && dev->sgemm_workspace(s.op_a, 1, 128, 128, 128, false) > 0;
-  lim.transpose_b = !call.tensor_cores && dev->sgemm_workspace(0, s.op_b, 128, 128, 128, false) > 0;
-  lim.tf32x3 = call.tensor_cores && dev->sgemm_workspace(0, 1, 128, 128, 128, true) > 0;
+  // panels (FFMA, FP64), the hi/lo split (tensor cores), widened FP16 / BF16 panels.
+  const GemmTypes st = step_types(s);
+  Device* d = dev.get();
+  const int op_a = s.op_a, op_b = s.op_b;
+  lim.step_workspace = [d, st, op_a, op_b](int64_t mb, int64_t nb, int64_t kb) {
+    return d->gemm_workspace(st, op_a, op_b, mb, nb, kb);
+  };
+  lim.ab_bytes = static_cast<uint32_t>(element_bytes(s.a.dtype));
+  lim.c_host_bytes = static_cast<uint32_t>(element_bytes(s.c.dtype));
+  lim.c_acc_bytes = static_cast<uint32_t>(element_bytes(st.c));
   return lim;
 }
 
@@ -784,7 +800,7 @@ PlanProblem Runtime::Impl::plan_problem(const GemmCall& call) {
   pp.m = static_cast<int64_t>(s.m);
   pp.n = static_cast<int64_t>(s.n);
   pp.k = static_cast<int64_t>(s.k);
-  pp.beta_nonzero = call.beta != 0.0f;
+  pp.beta_nonzero = call.beta != 0.0;
   return pp;
 }
 
@@ -827,6 +843,14 @@ Error Runtime::refresh_budget() { return impl_->apply_budget(true); }
 Error Runtime::gemm(const GemmCall& call) {
   Impl& m = *impl_;
   const auto t0 = std::chrono::steady_clock::now();
+  // Kernels address elements with their natural alignment (allocations start on frame
+  // boundaries, so the offsets decide it).
+  for (const MatrixRef* r : {&call.shape.a, &call.shape.b, &call.shape.c}) {
+    const uint64_t es = element_bytes(r->dtype);
+    if (es == 0 || r->offset_bytes % es != 0)
+      return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "executor", "gemm",
+                        "a matrix offset is not a multiple of its element size");
+  }
   if (Error e = m.apply_budget(false))
     return e;
   Alloc& A = m.allocs.at(call.shape.a.allocation_id);
@@ -861,12 +885,12 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   const GemmShape& s = call.shape;
   ++x.tiles_submitted;
   ++x.gemm_in_place;
-  if (Error e = dev->sgemm(s.op_a, s.op_b, static_cast<int64_t>(s.m), static_cast<int64_t>(s.n),
-                           static_cast<int64_t>(s.k), call.alpha, A.va + s.a.offset_bytes,
-                           static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
-                           static_cast<int64_t>(s.b.ld), call.beta, C.va + s.c.offset_bytes,
-                           static_cast<int64_t>(s.c.ld), ws ? allocs.at(kScratchId).va : 0, ws,
-                           call.tensor_cores, s_compute))
+  if (Error e = dev->gemm(gemm_types(s), s.op_a, s.op_b, static_cast<int64_t>(s.m),
+                          static_cast<int64_t>(s.n), static_cast<int64_t>(s.k), call.alpha,
+                          A.va + s.a.offset_bytes, static_cast<int64_t>(s.a.ld),
+                          B.va + s.b.offset_bytes, static_cast<int64_t>(s.b.ld), call.beta,
+                          C.va + s.c.offset_bytes, static_cast<int64_t>(s.c.ld),
+                          ws ? allocs.at(kScratchId).va : 0, ws, s_compute))
     return e;
   for (const auto& [id, c] : keep) {
     Frame& f = frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)];
@@ -968,6 +992,11 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
                 K = static_cast<int64_t>(s.k);
   const uint64_t lda = s.a.ld, ldb = s.b.ld, ldc = s.c.ld;
   const int64_t mb = plan.mb, nb = plan.nb, kb = plan.kb;
+  // Element bytes of A / B and of C as stored; the C slot accumulates in step.c's type,
+  // with a staging copy in the stored type at c_stage_offset when that is narrower.
+  const uint64_t ea = element_bytes(s.a.dtype), ec = element_bytes(s.c.dtype);
+  const GemmTypes step = step_types(s);
+  const bool c_staged = plan.c_stage_offset != 0;
   const auto slot_va = [&](int32_t slot) {
     return arena + static_cast<uint64_t>(slot) * fps * cb;
   };
@@ -989,31 +1018,31 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
       if (ld.operand == 0) {
         const int64_t lm0 = static_cast<int64_t>(ld.block) * mb, lmr = std::min(mb, M - lm0);
         if (s.op_a == 0) { // A is m x k: kr columns of mr floats
-          src = ha + (static_cast<uint64_t>(lm0) + static_cast<uint64_t>(lk0) * lda) * 4;
-          width = static_cast<uint64_t>(lmr) * 4;
+          src = ha + (static_cast<uint64_t>(lm0) + static_cast<uint64_t>(lk0) * lda) * ea;
+          width = static_cast<uint64_t>(lmr) * ea;
           height = static_cast<uint64_t>(lkr);
-          dpitch = static_cast<uint64_t>(mb) * 4;
+          dpitch = static_cast<uint64_t>(mb) * ea;
         } else { // A is k x m: mr columns of kr floats
-          src = ha + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(lm0) * lda) * 4;
-          width = static_cast<uint64_t>(lkr) * 4;
+          src = ha + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(lm0) * lda) * ea;
+          width = static_cast<uint64_t>(lkr) * ea;
           height = static_cast<uint64_t>(lmr);
-          dpitch = static_cast<uint64_t>(kb) * 4;
+          dpitch = static_cast<uint64_t>(kb) * ea;
         }
-        spitch = lda * 4;
+        spitch = lda * ea;
       } else {
         const int64_t ln0 = static_cast<int64_t>(ld.block) * nb, lnr = std::min(nb, N - ln0);
         if (s.op_b == 0) { // B is k x n: nr columns of kr floats
-          src = hb + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(ln0) * ldb) * 4;
-          width = static_cast<uint64_t>(lkr) * 4;
+          src = hb + (static_cast<uint64_t>(lk0) + static_cast<uint64_t>(ln0) * ldb) * ea;
+          width = static_cast<uint64_t>(lkr) * ea;
           height = static_cast<uint64_t>(lnr);
-          dpitch = static_cast<uint64_t>(kb) * 4;
+          dpitch = static_cast<uint64_t>(kb) * ea;
         } else { // B is n x k: kr columns of nr floats
-          src = hb + (static_cast<uint64_t>(ln0) + static_cast<uint64_t>(lk0) * ldb) * 4;
-          width = static_cast<uint64_t>(lnr) * 4;
+          src = hb + (static_cast<uint64_t>(ln0) + static_cast<uint64_t>(lk0) * ldb) * ea;
+          width = static_cast<uint64_t>(lnr) * ea;
           height = static_cast<uint64_t>(lkr);
-          dpitch = static_cast<uint64_t>(nb) * 4;
+          dpitch = static_cast<uint64_t>(nb) * ea;
         }
-        spitch = ldb * 4;
+        spitch = ldb * ea;
       }
       if ((err = dev->copy_2d(slot_va(ld.slot), dpitch, src, spitch, width, height, CopyDir::h2d,
                               s_h2d)))
@@ -1032,20 +1061,24 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     t.cache_hits += 2 - st.load_count;
     const size_t cs = static_cast<size_t>(st.c_slot);
     const uint64_t cva = c_base + static_cast<uint64_t>(cs) * fpc * cb;
-    float beta_eff = 1.0f;
+    const uint64_t cstage = cva + plan.c_stage_offset;
+    const uint64_t c_host = hc + (static_cast<uint64_t>(m0) + static_cast<uint64_t>(n0) * ldc) * ec;
+    double beta_eff = 1.0;
     if (st.first_k) {
       beta_eff = call.beta;
-      if (call.beta != 0.0f) {
+      if (call.beta != 0.0) {
         if (wb_rec[cs] && (err = dev->stream_wait_event(s_h2d, c_wb[cs])))
           break;
-        if ((err = dev->copy_2d(cva, static_cast<uint64_t>(mb) * 4,
-                                hc + (static_cast<uint64_t>(m0) + static_cast<uint64_t>(n0) * ldc) * 4,
-                                ldc * 4, static_cast<uint64_t>(mr) * 4, static_cast<uint64_t>(nr),
-                                CopyDir::h2d, s_h2d)))
+        if ((err = dev->copy_2d(c_staged ? cstage : cva, static_cast<uint64_t>(mb) * ec, c_host,
+                                ldc * ec, static_cast<uint64_t>(mr) * ec,
+                                static_cast<uint64_t>(nr), CopyDir::h2d, s_h2d)))
           break;
-        t.bytes_h2d += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4;
+        t.bytes_h2d += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * ec;
         if ((err = dev->event_record(c_ready[cs], s_h2d)) ||
             (err = dev->stream_wait_event(s_compute, c_ready[cs])))
+          break;
+        if (c_staged && (err = dev->convert(s.c.dtype, cstage, mb, step.c, cva, mb, mr, nr,
+                                            s_compute)))
           break;
       } else if (wb_rec[cs] && (err = dev->stream_wait_event(s_compute, c_wb[cs]))) {
         break;
@@ -1056,10 +1089,9 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
       break;
     const int64_t lda_s = s.op_a == 0 ? mb : kb;
     const int64_t ldb_s = s.op_b == 0 ? kb : nb;
-    if ((err = dev->sgemm(s.op_a, s.op_b, mr, nr, kr, call.alpha, slot_va(st.slot_a), lda_s,
-                          slot_va(st.slot_b), ldb_s, beta_eff, cva, mb,
-                          plan.workspace_bytes ? ws_base : 0, plan.workspace_bytes,
-                          call.tensor_cores, s_compute)))
+    if ((err = dev->gemm(step, s.op_a, s.op_b, mr, nr, kr, call.alpha, slot_va(st.slot_a),
+                         lda_s, slot_va(st.slot_b), ldb_s, beta_eff, cva, mb,
+                         plan.workspace_bytes ? ws_base : 0, plan.workspace_bytes, s_compute)))
       break;
     ++x.tiles_submitted;
     for (int32_t sl : {st.slot_a, st.slot_b}) {
@@ -1070,16 +1102,18 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     if (err)
       break;
     if (st.last_k) {
+      if (c_staged &&
+          (err = dev->convert(step.c, cva, mb, s.c.dtype, cstage, mb, mr, nr, s_compute)))
+        break;
       if ((err = dev->event_record(c_done[cs], s_compute)) ||
           (err = dev->stream_wait_event(s_d2h, c_done[cs])) ||
-          (err = dev->copy_2d(hc + (static_cast<uint64_t>(m0) + static_cast<uint64_t>(n0) * ldc) * 4,
-                              ldc * 4, cva, static_cast<uint64_t>(mb) * 4,
-                              static_cast<uint64_t>(mr) * 4, static_cast<uint64_t>(nr),
-                              CopyDir::d2h, s_d2h)) ||
+          (err = dev->copy_2d(c_host, ldc * ec, c_staged ? cstage : cva,
+                              static_cast<uint64_t>(mb) * ec, static_cast<uint64_t>(mr) * ec,
+                              static_cast<uint64_t>(nr), CopyDir::d2h, s_d2h)) ||
           (err = dev->event_record(c_wb[cs], s_d2h)))
         break;
       wb_rec[cs] = 1;
-      t.bytes_d2h += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * 4;
+      t.bytes_d2h += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * ec;
       ++t.writebacks_completed;
     }
   }

@@ -54,11 +54,11 @@ struct RuntimeConfig {
 };
 
 struct GemmCall {
+  // Element types in shape.a/b/c.dtype, arithmetic in shape.compute: kTf32 is the
+  // three-term TF32 tensor-core kernel (FP32-accurate within 1e-6 of the normalised error
+  // bound).  alpha and beta are applied in FP32 for FP32 arithmetic, in FP64 for FP64.
   GemmShape shape;
-  float alpha = 1.0f, beta = 0.0f;
-  // Three-term TF32 on the tensor cores (FP32-accurate within 1e-6 of the normalised
-  // error bound) instead of strict FFMA.
-  bool tensor_cores = false;
+  double alpha = 1.0, beta = 0.0;
   // Rates for planning this call (0 = the runtime's configured rates).
   double flops_per_s = 0;
 };

@@ -14,10 +14,12 @@
 //   * a failure that may leave device state undefined (CUDA errors, kernel wait limits,
 //     internal errors) poisons the session: later operations fail with POISONED.
 // What differs, by design of this implementation:
-//   * GEMMs compute column-major FP32 on this library's sm_100a kernels.  Row-major
-//     matrices are handled as the transposed column-major view (the operation flips; a
-//     row-major C swaps the operands).  FP16 / BF16 / FP64 data and FP64 compute are
-//     UNSUPPORTED.  FP32_TF32 runs the three-term TF32 tensor-core kernel.
+//   * GEMMs run on this library's sm_100a kernels, for the reference's type combinations
+//     (FP32, FP16 / BF16 inputs with strict FP32 arithmetic, FP64).  Row-major matrices
+//     are handled as the transposed column-major view (the operation flips; a row-major C
+//     swaps the operands).  FP32_TF32 (and AUTO on FP32 data, as in the reference) runs
+//     the three-term TF32 tensor-core kernel, which is FP32-accurate where the
+//     reference's single-pass TF32 is not.
 //   * Tile hints are ignored: the panel planner picks the geometry from the budget.
 #include "xvram.h"
 
@@ -534,6 +536,18 @@ Error collect_ranges(const SessionPtr& s, const xvram_access_range_v1* ranges, u
   return {};
 }
 
+// Requested mode -> arithmetic, as reference src/sdk/runtime.cpp:119-142: AUTO is FP64 on
+// FP64 data, strict FP32 on FP16 / BF16 data and TF32 on FP32 data.
+int compute_kind(xvram_compute_mode mode, xvram_data_type a_type) {
+  if (mode == XVRAM_COMPUTE_AUTO)
+    return a_type == XVRAM_DATA_FP64                                ? kComputeFp64
+           : a_type == XVRAM_DATA_FP16 || a_type == XVRAM_DATA_BF16 ? kStrictFp32
+                                                                    : kTf32;
+  if (mode == XVRAM_COMPUTE_FP64)
+    return kComputeFp64;
+  return mode == XVRAM_COMPUTE_FP32_STRICT ? kStrictFp32 : kTf32;
+}
+
 // The column-major view of a matrix descriptor and the operation it then needs: a
 // row-major rows x columns matrix is the column-major columns x rows matrix, transposed.
 struct View {
@@ -554,9 +568,6 @@ Error make_view(const SessionPtr& s, const xvram_matrix_v1& m, xvram_matrix_oper
     return invalid("gemm_plan_create", "matrix descriptor has invalid enum or reserved fields");
   if (m.rows == 0 || m.columns == 0 || m.leading_dimension == 0)
     return invalid("gemm_plan_create", "matrix dimensions and leading dimension must be non-zero");
-  if (m.data_type != XVRAM_DATA_FP32)
-    return make_error(XVRAM_STATUS_UNSUPPORTED, "gemm", "create_plan",
-                      "this implementation computes FP32 GEMMs only");
   const bool row = m.layout == XVRAM_MATRIX_ROW_MAJOR;
   out->ref.allocation_id = m.allocation->id;
   out->ref.allocation_bytes = m.allocation->size;
@@ -564,6 +575,7 @@ Error make_view(const SessionPtr& s, const xvram_matrix_v1& m, xvram_matrix_oper
   out->ref.rows = row ? m.columns : m.rows;
   out->ref.columns = row ? m.rows : m.columns;
   out->ref.ld = m.leading_dimension;
+  out->ref.dtype = m.data_type;
   out->op = row ? 1 - static_cast<int>(op) : static_cast<int>(op);
   return {};
 }
@@ -586,9 +598,6 @@ Error build_plan(const SessionPtr& s, const xvram_gemm_desc_v1* d, xvram_gemm_pl
     return e;
   if (Error e = make_view(s, d->c, XVRAM_MATRIX_OP_N, &c))
     return e;
-  if (d->compute_mode == XVRAM_COMPUTE_FP64)
-    return make_error(XVRAM_STATUS_UNSUPPORTED, "gemm", "create_plan",
-                      "FP64 compute is not provided by this implementation");
   if (!std::isfinite(d->alpha) || !std::isfinite(d->beta))
     return invalid("gemm_plan_create", "alpha and beta must be finite");
   // Logical sizes from the descriptors (reference src/sdk/runtime.cpp:1303-1308).
@@ -596,10 +605,14 @@ Error build_plan(const SessionPtr& s, const xvram_gemm_desc_v1* d, xvram_gemm_pl
   const uint64_t k = d->operation_a == XVRAM_MATRIX_OP_N ? d->a.columns : d->a.rows;
   const uint64_t n = d->operation_b == XVRAM_MATRIX_OP_N ? d->b.columns : d->b.rows;
   GemmCall call;
-  call.alpha = static_cast<float>(d->alpha);
-  call.beta = static_cast<float>(d->beta);
-  call.tensor_cores = d->compute_mode == XVRAM_COMPUTE_FP32_TF32;
+  call.alpha = d->alpha;
+  call.beta = d->beta;
   GemmShape& sh = call.shape;
+  sh.compute = compute_kind(d->compute_mode, d->a.data_type);
+  if (sh.compute == kTf32)
+    call.flops_per_s = 150e12; // plan for the tensor-core rate
+  else if (sh.compute == kComputeFp64)
+    call.flops_per_s = 35e12;
   if (d->c.layout == XVRAM_MATRIX_COLUMN_MAJOR) {
     sh.m = m;
     sh.n = n;
@@ -619,6 +632,11 @@ Error build_plan(const SessionPtr& s, const xvram_gemm_desc_v1* d, xvram_gemm_pl
   }
   sh.c = c.ref;
   const Validation v = validate_gemm(sh);
+  if (v)
+    for (const MatrixRef* r : {&sh.a, &sh.b, &sh.c})
+      if (r->offset_bytes % element_bytes(r->dtype) != 0)
+        return invalid("gemm_plan_create",
+                       "a matrix offset is not a multiple of its element size");
   if (!v) {
     std::string msg = std::string(problem_error_name(v.error));
     if (v.operand)
@@ -627,7 +645,9 @@ Error build_plan(const SessionPtr& s, const xvram_gemm_desc_v1* d, xvram_gemm_pl
   }
   plan->owner = s;
   plan->call = call;
-  plan->effective = call.tensor_cores ? XVRAM_COMPUTE_FP32_TF32 : XVRAM_COMPUTE_FP32_STRICT;
+  plan->effective = sh.compute == kComputeFp64 ? XVRAM_COMPUTE_FP64
+                    : sh.compute == kTf32      ? XVRAM_COMPUTE_FP32_TF32
+                                               : XVRAM_COMPUTE_FP32_STRICT;
   plan->deadline_ms = d->deadline_ms;
   // (Operation bodies hold the session by raw pointer: the handles own it, and the last
   // owner must never be released on the worker thread itself.)

@@ -26,6 +26,9 @@ Validation check_matrix(const MatrixRef& m, char operand) {
   auto fail = [operand](ProblemError e) { return Validation{e, operand}; };
   if (m.allocation_id == 0 || m.allocation_bytes == 0)
     return fail(ProblemError::invalid_allocation);
+  const uint64_t esize = element_bytes(m.dtype);
+  if (esize == 0)
+    return fail(ProblemError::invalid_element_type);
   if (m.rows == 0 || m.columns == 0)
     return fail(ProblemError::zero_dimension);
   if (m.ld < m.rows)
@@ -36,7 +39,7 @@ Validation check_matrix(const MatrixRef& m, char operand) {
   if (!mul_ok(m.columns - 1, m.ld, &last_col) || !add_ok(last_col, m.rows - 1, &last) ||
       !add_ok(last, 1, &last))
     return fail(ProblemError::storage_overflow);
-  if (!mul_ok(last, sizeof(float), &bytes) || !add_ok(m.offset_bytes, bytes, &end))
+  if (!mul_ok(last, esize, &bytes) || !add_ok(m.offset_bytes, bytes, &end))
     return fail(ProblemError::storage_overflow);
   if (m.offset_bytes >= m.allocation_bytes || end > m.allocation_bytes)
     return fail(ProblemError::storage_out_of_bounds);
@@ -45,12 +48,27 @@ Validation check_matrix(const MatrixRef& m, char operand) {
 
 } // namespace
 
+bool supported_types(uint32_t ab, uint32_t c, int compute) {
+  switch (ab) {
+  case kFp16:
+  case kBf16:
+    return (c == ab || c == kFp32) && compute == kStrictFp32;
+  case kFp32:
+    return c == kFp32 && (compute == kStrictFp32 || compute == kTf32);
+  case kFp64:
+    return c == kFp64 && compute == kComputeFp64;
+  default:
+    return false;
+  }
+}
+
 bool matrix_byte_span(const MatrixRef& m, uint64_t* begin, uint64_t* end) {
-  if (m.rows == 0 || m.columns == 0)
+  const uint64_t esize = element_bytes(m.dtype);
+  if (m.rows == 0 || m.columns == 0 || esize == 0)
     return false;
   uint64_t last_col = 0, last = 0, bytes = 0, e = 0;
   if (!mul_ok(m.columns - 1, m.ld, &last_col) || !add_ok(last_col, m.rows, &last) ||
-      !mul_ok(last, sizeof(float), &bytes) || !add_ok(m.offset_bytes, bytes, &e))
+      !mul_ok(last, esize, &bytes) || !add_ok(m.offset_bytes, bytes, &e))
     return false;
   *begin = m.offset_bytes;
   *end = e;
@@ -78,8 +96,8 @@ const char* problem_error_name(ProblemError e) {
 }
 
 // Problem-level order (reference planner.cpp:785-859): empty problem, operations,
-// each matrix A, B, C, allocation identity consistency, operated shapes, then
-// overlap of C with an input in the same allocation.
+// compute mode, each matrix A, B, C, allocation identity consistency, operated shapes,
+// element types, then overlap of C with an input in the same allocation.
 Validation validate_gemm(const GemmShape& s) {
   if (s.m == 0 || s.n == 0 || s.k == 0)
     return {ProblemError::zero_dimension, 0};
@@ -87,6 +105,8 @@ Validation validate_gemm(const GemmShape& s) {
     return {ProblemError::invalid_operation, 'A'};
   if (s.op_b != 0 && s.op_b != 1)
     return {ProblemError::invalid_operation, 'B'};
+  if (s.compute != kStrictFp32 && s.compute != kTf32 && s.compute != kComputeFp64)
+    return {ProblemError::invalid_compute_mode, 0};
   const MatrixRef* mats[3] = {&s.a, &s.b, &s.c};
   const char names[3] = {'A', 'B', 'C'};
   for (int i = 0; i < 3; ++i)
@@ -105,6 +125,8 @@ Validation validate_gemm(const GemmShape& s) {
   if (a_rows != s.m || a_cols != s.k || b_rows != s.k || b_cols != s.n || s.c.rows != s.m ||
       s.c.columns != s.n)
     return {ProblemError::dimension_mismatch, 0};
+  if (s.a.dtype != s.b.dtype || !supported_types(s.a.dtype, s.c.dtype, s.compute))
+    return {ProblemError::unsupported_type_combination, 0};
   uint64_t ab = 0, ae = 0, bb = 0, be = 0, cb = 0, ce = 0;
   if (!matrix_byte_span(s.a, &ab, &ae) || !matrix_byte_span(s.b, &bb, &be) ||
       !matrix_byte_span(s.c, &cb, &ce))

@@ -112,6 +112,40 @@ def validate(m, n, k, op_a, op_b, ids, nbytes, offsets, rows, cols, lds) -> tupl
     return err, (op.value.decode() if op.value else "")
 
 
+def validate_typed(m, n, k, op_a, op_b, ids, nbytes, offsets, rows, cols, lds, types,
+                   compute) -> tuple[int, str]:
+    arr = lambda xs: (u64 * 3)(*xs)
+    op = C.create_string_buffer(1)
+    err = lib.xvram_b200_validate_gemm_typed(m, n, k, op_a, op_b, arr(ids), arr(nbytes),
+                                             arr(offsets), arr(rows), arr(cols), arr(lds),
+                                             (C.c_uint32 * 3)(*types), compute, op)
+    return err, (op.value.decode() if op.value else "")
+
+
+# Element types (XVRAM_DATA_*) and arithmetic (the reference's gemm::ComputeMode order).
+FP16, BF16, FP32, FP64 = range(4)
+STRICT_FP32, TF32, COMPUTE_FP64 = range(3)
+_TORCH_TYPES = {"float16": FP16, "bfloat16": BF16, "float32": FP32, "float64": FP64}
+
+
+def gemm_typed(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, Cm, ldc, compute=None,
+               stream=None) -> int:
+    """C = alpha op(A) op(B) + beta C on CUDA tensors of the reference's type combinations
+    (types read from the tensors; compute defaults to strict FP32, FP64 for FP64), with a
+    workspace allocated here."""
+    import torch
+    ab = _TORCH_TYPES[str(A.dtype).split(".")[-1]]
+    ct = _TORCH_TYPES[str(Cm.dtype).split(".")[-1]]
+    if compute is None:
+        compute = COMPUTE_FP64 if ab == FP64 else STRICT_FP32
+    need = lib.xvram_b200_gemm_typed_workspace_bytes(ab, ct, compute, op_a, op_b, m, n, k)
+    ws = torch.empty(need + 256, dtype=torch.uint8, device=A.device) if need else None
+    wp = ((ws.data_ptr() + 255) // 256 * 256) if ws is not None else 0
+    return lib.xvram_b200_gemm_device_typed(ab, ct, compute, op_a, op_b, m, n, k, alpha,
+                                            A.data_ptr(), lda, B.data_ptr(), ldb, beta,
+                                            Cm.data_ptr(), ldc, wp, need, _stream_handle(stream))
+
+
 def ffma_probe(blocks: int, iterations: int, sink, stream=None, packed: bool = False) -> int:
     fn = lib.xvram_b200_ffma2_probe if packed else lib.xvram_b200_ffma_probe
     return fn(blocks, iterations, sink.data_ptr(), _stream_handle(stream))

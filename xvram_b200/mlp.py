@@ -33,7 +33,8 @@ class StreamedMLP:
         for i in range(layers):
             src, dst = self.H[i % 2], self.H[(i + 1) % 2]
             d = session.gemm_desc(sdk.matrix(self.W[i], F, F, F), sdk.matrix(src, F, Bt, F),
-                                  sdk.matrix(dst, F, Bt, F), sdk.OP_N, sdk.OP_N)
+                                  sdk.matrix(dst, F, Bt, F), sdk.OP_N, sdk.OP_N,
+                                  mode=sdk.COMPUTE_FP32_STRICT)
             self.plans.append(session.plan(d))
         self.txns = [session.transaction_desc(
             [(self.H[(i + 1) % 2], 0, self.abytes, sdk.READ_WRITE),

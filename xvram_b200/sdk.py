@@ -279,6 +279,12 @@ class Sdk:
         self.check("gemm_plan_create", self.t.gemm_plan_create(self.session, C.byref(desc), C.byref(h)))
         return h.value
 
+    def try_plan(self, desc: GemmDesc) -> tuple[int, int]:
+        """gemm_plan_create without raising: (status, plan handle or 0)."""
+        h = vp()
+        st = self.t.gemm_plan_create(self.session, C.byref(desc), C.byref(h))
+        return st, (h.value or 0)
+
     def plan_info(self, plan: int) -> PlanInfo:
         info = PlanInfo(struct_size=C.sizeof(PlanInfo))
         self.check("gemm_plan_get_info", self.t.gemm_plan_get_info(plan, C.byref(info)))
