@@ -28,6 +28,7 @@ def build() -> C.CDLL:
     lib.fake_device_create.restype = C.c_void_p
     lib.fake_device_set_memory.argtypes = [C.c_uint64, C.c_uint64]
     lib.fake_device_fail.argtypes = [C.c_char_p, C.c_long]
+    lib.fake_device_set_workspace_fn.argtypes = [C.c_void_p]
     return lib
 
 
@@ -38,6 +39,8 @@ def installed(free_bytes: int = 8 << 30, total_bytes: int = 16 << 30):
     fake = build()
     fake.fake_device_set_memory(free_bytes, total_bytes)
     fake.fake_device_fail(b"", -1)
+    fake.fake_device_set_workspace_fn(C.cast(lib.xvram_b200_gemm_typed_workspace_bytes,
+                                             C.c_void_p))
     factory = C.cast(fake.fake_device_create, C.c_void_p)
     assert lib.xvram_b200_test_set_device_factory(factory) == 0
     try:

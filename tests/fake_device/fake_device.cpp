@@ -33,6 +33,9 @@
 
 namespace {
 
+using WorkspaceFn = uint64_t (*)(uint32_t, uint32_t, int32_t, uint32_t, uint32_t, int64_t,
+                                 int64_t, int64_t);
+std::atomic<WorkspaceFn> g_workspace_fn{nullptr};
 std::atomic<uint64_t> g_free{8ull << 30};
 std::atomic<uint64_t> g_total{16ull << 30};
 std::mutex g_fail_mu;
@@ -282,8 +285,14 @@ public:
       }
     }
   }
-  uint64_t gemm_workspace(const xvram::GemmTypes&, int, int, int64_t, int64_t, int64_t) override {
-    return 0;
+  // The workspace the real kernels would ask for (the library's own sizing function,
+  // installed by the test), so the planner budgets exactly as on a GPU; the fake's loops
+  // do not use it.
+  uint64_t gemm_workspace(const xvram::GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n,
+                          int64_t k) override {
+    return g_workspace_fn ? g_workspace_fn(t.ab, t.c, t.compute, static_cast<uint32_t>(op_a),
+                                           static_cast<uint32_t>(op_b), m, n, k)
+                          : 0;
   }
   xvram::Error convert(uint32_t st, uint64_t src, int64_t lds, uint32_t dt, uint64_t dst,
                        int64_t ldd, int64_t rows, int64_t cols, xvram::StreamId) override {
@@ -313,6 +322,11 @@ __attribute__((visibility("default"))) void fake_device_set_memory(uint64_t free
                                                                    uint64_t total_bytes) {
   g_free.store(free_bytes);
   g_total.store(total_bytes);
+}
+
+// The library's xvram_b200_gemm_typed_workspace_bytes (or null: no workspace).
+__attribute__((visibility("default"))) void fake_device_set_workspace_fn(void* fn) {
+  g_workspace_fn.store(reinterpret_cast<WorkspaceFn>(fn));
 }
 
 // The (after + 1)-th call of `op` ("copy_2d", "map", "handle_create", "sgemm") fails with

@@ -64,8 +64,11 @@ def test_allocation_round_trip_and_zero_initialize(s):
     assert z.release() == sdk.SUCCESS and a.release() == sdk.SUCCESS
 
 
+@pytest.mark.parametrize("mode", [sdk.COMPUTE_FP32_STRICT, sdk.COMPUTE_AUTO])
 @pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
-def test_column_major_gemm_matches_oracle(s, op_a, op_b):
+def test_column_major_gemm_matches_oracle(s, op_a, op_b, mode):
+    """Strict FP32, and AUTO, which on FP32 data selects TF32 as in the reference (here the
+    FP32-accurate three-term kernel)."""
     orc = load_oracle()
     m, n, k = 515, 389, 611
     a = orc.uniform(m * k, 21)
@@ -75,11 +78,12 @@ def test_column_major_gemm_matches_oracle(s, op_a, op_b):
     A, B, Cm = upload(s, a), upload(s, b), upload(s, c)
     desc = s.gemm_desc(sdk.matrix(A, m if op_a == 0 else k, k if op_a == 0 else m, lda),
                        sdk.matrix(B, k if op_b == 0 else n, n if op_b == 0 else k, ldb),
-                       sdk.matrix(Cm, m, n, m), op_a, op_b, alpha=0.75, beta=-1.25)
+                       sdk.matrix(Cm, m, n, m), op_a, op_b, alpha=0.75, beta=-1.25, mode=mode)
     plan = s.plan(desc)
     info = s.plan_info(plan)
     assert (info.m, info.n, info.k, info.tile_count) == (m, n, k, 1)
-    assert info.effective_compute_mode == sdk.COMPUTE_FP32_STRICT and info.uses_cublas_lt == 0
+    want = sdk.COMPUTE_FP32_STRICT if mode == sdk.COMPUTE_FP32_STRICT else sdk.COMPUTE_FP32_TF32
+    assert info.effective_compute_mode == want and info.uses_cublas_lt == 0
     s.check("gemm_execute", s.t.gemm_execute(plan, sdk.TIMEOUT_INFINITE))
     s.t.gemm_plan_release(plan)
     out = download(Cm, (n, m))
@@ -136,8 +140,9 @@ def test_plan_errors(s):
     out = C.c_void_p()
     for bad, status in [
         (s.gemm_desc(sdk.matrix(A, 64, 64, 64, data_type=sdk.FP16), ok, sdk.matrix(C_, 64, 64, 64)),
-         sdk.UNSUPPORTED),
-        (s.gemm_desc(ok, ok, sdk.matrix(C_, 64, 64, 64), mode=sdk.COMPUTE_FP64), sdk.UNSUPPORTED),
+         sdk.INVALID_ARGUMENT),                       # A and B types differ
+        (s.gemm_desc(ok, ok, sdk.matrix(C_, 64, 64, 64), mode=sdk.COMPUTE_FP64),
+         sdk.INVALID_ARGUMENT),                       # FP64 arithmetic on FP32 data
         (s.gemm_desc(ok, sdk.matrix(A, 32, 64, 64), sdk.matrix(C_, 64, 64, 64)),
          sdk.INVALID_ARGUMENT),                                   # k mismatch
         (s.gemm_desc(ok, ok, sdk.matrix(A, 64, 64, 64)), sdk.INVALID_ARGUMENT),  # C aliases A

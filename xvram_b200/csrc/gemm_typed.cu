@@ -316,10 +316,12 @@ cudaError_t gemm_fp64(int op_a, int op_b, int m, int n, int k, double alpha, con
       return e;
     b2 = bt;
   }
-  static const cudaError_t attr = cudaFuncSetAttribute(
-      dgemm_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize, kDSmemBytes);
-  if (attr != cudaSuccess)
-    return attr;
+  // Per call: the attribute belongs to the current device.
+  if (cudaError_t e = cudaFuncSetAttribute(dgemm_dmma,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kDSmemBytes);
+      e != cudaSuccess)
+    return e;
   const long long tiles_m = (m + kDBM - 1) / kDBM, tiles_n = (n + kDBN - 1) / kDBN;
   if (tiles_m * tiles_n > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;

@@ -140,6 +140,8 @@ def gemm_typed(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, Cm, ldc, comput
         compute = COMPUTE_FP64 if ab == FP64 else STRICT_FP32
     need = lib.xvram_b200_gemm_typed_workspace_bytes(ab, ct, compute, op_a, op_b, m, n, k)
     ws = torch.empty(need + 256, dtype=torch.uint8, device=A.device) if need else None
+    if ws is not None and isinstance(stream, torch.cuda.Stream):
+        ws.record_stream(stream)  # freed here, but not reused before the stream's work ends
     wp = ((ws.data_ptr() + 255) // 256 * 256) if ws is not None else 0
     return lib.xvram_b200_gemm_device_typed(ab, ct, compute, op_a, op_b, m, n, k, alpha,
                                             A.data_ptr(), lda, B.data_ptr(), ldb, beta,
