@@ -277,13 +277,16 @@ typedef struct xvram_operation_info_v1 {
    UINT64_C(0), UINT64_C(0), UINT64_C(0), 0.0, UINT64_C(0), UINT64_C(0), UINT64_C(0),            \
    UINT64_C(0), {0, 0}}
 
-/* Element types.  This implementation computes FP32 only; the others are UNSUPPORTED. */
+/* Element types.  Supported combinations (the reference's rule): FP32 A/B/C; FP16 or BF16
+ * A/B with C of the same type or FP32 under strict FP32 arithmetic; FP64 A/B/C under FP64
+ * arithmetic.  Others fail gemm_plan_create with INVALID_ARGUMENT. */
 typedef uint32_t xvram_data_type;
 enum { XVRAM_DATA_FP16 = 0, XVRAM_DATA_BF16 = 1, XVRAM_DATA_FP32 = 2, XVRAM_DATA_FP64 = 3 };
 
-/* AUTO and FP32_STRICT: every product and sum an FP32 FFMA.  FP32_TF32: tensor cores,
- * as the three-term TF32 kernel (FP32-accurate within max|err| / (K max|a| max|b|) <= 1e-6,
- * tighter than single-pass TF32).  FP64: UNSUPPORTED. */
+/* FP32_STRICT: every product and sum an FP32 FMA.  FP32_TF32: tensor cores, as the
+ * three-term TF32 kernel (FP32-accurate within max|err| / (K max|a| max|b|) <= 1e-6,
+ * tighter than single-pass TF32).  FP64: FP64 arithmetic (FP64 tensor-core MMA).  AUTO,
+ * as in the reference: FP64 on FP64 data, FP32_STRICT on FP16 / BF16, FP32_TF32 on FP32. */
 typedef uint32_t xvram_compute_mode;
 enum {
   XVRAM_COMPUTE_AUTO = 0,
