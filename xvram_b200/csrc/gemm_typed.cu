@@ -15,16 +15,17 @@
 // rounded to the C type once at the end (round to nearest even).
 //
 // FP64: the 5th-generation tensor cores (tcgen05) have no FP64 form, so the FP64 kernel
-// uses the FP64 MMA of the warp-level tensor path, mma.sync m8n8k4 .f64 (each
+// uses the FP64 MMA of the warp-level tensor path, mma.sync m16n8k8 .f64 (each
 // multiply-add an FP64 operation, no reduced precision), fed by a 3-stage cp.async ring:
-//   * 128 x 128 C tile per CTA, 8 warps as 2 (M) x 4 (N), each warp 64 x 32 = 8 x 4
-//     blocks of 8 x 8, accumulators in registers (64 doubles per thread);
-//   * K in stages of 16; stage tiles [16 k][128 + 8] doubles -- the 8-double pad puts
+//   * 128 x 128 C tile per CTA, 8 warps as 2 (M) x 4 (N), each warp 64 x 32 = 4 x 4
+//     blocks of 16 x 8, accumulators in registers (64 doubles per thread);
+//   * K in stages of 32; stage tiles [32 k][128 + 8] doubles -- the 8-double pad puts
 //     consecutive k rows 16 banks apart, so a fragment load (4 k rows x 8 consecutive
 //     doubles across the warp) takes the minimum two wavefronts;
 //   * operands canonicalised first, as for FP32: op(A) M-major and op(B) N-major
-//     (K-major operands are transposed into workspace); 8-byte cp.async with zero fill
-//     covers ragged edges and any leading dimension.
+//     (K-major operands are transposed into workspace); 16-byte cp.async (8-byte when a
+//     base or leading dimension is not 16-byte aligned) with zero fill covers ragged
+//     edges.
 // There are no spin-waits in these kernels (cp.async groups and block barriers only).
 #include "kernels.hpp"
 #include "validate.hpp"
@@ -119,7 +120,16 @@ cudaError_t relayout(const void* src, long long lds, void* dst, long long ldd, i
 }
 
 // ------------------------------------------------------------------ FP64 kernel
-constexpr int kDBM = 128, kDBN = 128, kDBK = 16, kDStages = 3, kDPad = 8;
+// K per stage and ring depth: C2 FP64 NT, (16, 3) 29.6, (16, 4) 29.9, (32, 2) 30.9, (32, 3)
+// 30.9 TFLOP/s -- fewer block barriers per k.
+#ifndef XVRAM_DGEMM_BK
+#define XVRAM_DGEMM_BK 32
+#endif
+#ifndef XVRAM_DGEMM_STAGES
+#define XVRAM_DGEMM_STAGES 3
+#endif
+constexpr int kDBM = 128, kDBN = 128, kDBK = XVRAM_DGEMM_BK, kDStages = XVRAM_DGEMM_STAGES;
+constexpr int kDPad = 8;
 constexpr int kDRow = kDBM + kDPad;            // doubles per k row of a stage tile
 constexpr int kDStageDoubles = kDBK * kDRow;   // one operand's stage tile
 constexpr int kDSmemBytes = kDStages * 2 * kDStageDoubles * 8;
@@ -131,6 +141,12 @@ __device__ __forceinline__ void cp_async8(double* dst, const double* src, bool v
                "r"(valid ? 8 : 0)
                : "memory");
 }
+// 16 bytes (two doubles); `bytes` (0, 8 or 16) are read, the rest of the 16 zero-filled.
+__device__ __forceinline__ void cp_async16(double* dst, const double* src, int bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -138,61 +154,99 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// d += a (8 x 4, row) * b (4 x 8, col); lane l holds a[l/4][l%4], b[l%4][l/4] and
-// d[l/4][2(l%4)], d[l/4][2(l%4)+1].
+#ifndef XVRAM_DGEMM_MMA_K
+#define XVRAM_DGEMM_MMA_K 8
+#endif
+#if XVRAM_DGEMM_MMA_K == 4
+// d (8 x 8) += a (8 x 4, row) * b (4 x 8, col); lane l (g = l/4, t = l%4) holds a[g][t],
+// b[t][g] and d[g][2t], d[g][2t+1].
 __device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
   asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
                : "+d"(d[0]), "+d"(d[1])
                : "d"(a), "d"(b));
 }
+#else
+// d (16 x 8) += a (16 x 8, row) * b (8 x 8, col); lane l (g = l/4, t = l%4) holds
+// a = {a[g][t], a[g+8][t], a[g][t+4], a[g+8][t+4]}, b = {b[t][g], b[t+4][g]} and
+// d = {d[g][2t], d[g][2t+1], d[g+8][2t], d[g+8][2t+1]}.
+__device__ __forceinline__ void dmma_16x8x8(double (&d)[4], const double (&a)[4],
+                                            const double (&b)[2]) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, "
+               "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+               : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
+}
+#endif
 
 // Stage kt of op(A) (M-major, element (i, k) at a[i + k lda]) and op(B) (N-major, element
-// (k, j) at b[j + k ldb]) into shared stage s: 2048 doubles each, 8 per thread, threads
-// consecutive along M / N so each warp reads 256 contiguous bytes of a column.
+// (k, j) at b[j + k ldb]) into shared stage s: 2048 doubles each, threads consecutive
+// along M / N so each warp reads contiguous bytes of a column.  VEC16: 16-byte copies
+// (bases 16-byte aligned, even leading dimensions), 4 per thread per operand; else
+// 8-byte copies, 8 per thread.
+template <bool VEC16>
 __device__ __forceinline__ void dgemm_load_stage(double* As, double* Bs, const double* a,
                                                  long long lda, const double* b, long long ldb,
                                                  int m, int n, int k, int m0, int n0, int kt,
                                                  int s, int tid) {
+  if constexpr (VEC16) {
 #pragma unroll
-  for (int i = 0; i < (kDBK * kDBM) / kDThreads; ++i) {
-    const int idx = tid + kDThreads * i;
-    const int kk = idx / kDBM, rr = idx % kDBM;
-    const int gk = kt * kDBK + kk;
-    const int gm = m0 + rr, gn = n0 + rr;
-    const bool va = gk < k && gm < m, vb = gk < k && gn < n;
-    cp_async8(As + s * kDStageDoubles + kk * kDRow + rr,
-              va ? a + gm + static_cast<long long>(gk) * lda : a, va);
-    cp_async8(Bs + s * kDStageDoubles + kk * kDRow + rr,
-              vb ? b + gn + static_cast<long long>(gk) * ldb : b, vb);
+    for (int i = 0; i < (kDBK * kDBM) / (2 * kDThreads); ++i) {
+      const int idx = tid + kDThreads * i;
+      const int kk = idx / (kDBM / 2), rr = (idx % (kDBM / 2)) * 2;
+      const int gk = kt * kDBK + kk;
+      const int gm = m0 + rr, gn = n0 + rr;
+      const int ba = gk < k ? (gm + 1 < m ? 16 : gm < m ? 8 : 0) : 0;
+      const int bb = gk < k ? (gn + 1 < n ? 16 : gn < n ? 8 : 0) : 0;
+      cp_async16(As + s * kDStageDoubles + kk * kDRow + rr,
+                 ba ? a + gm + static_cast<long long>(gk) * lda : a, ba);
+      cp_async16(Bs + s * kDStageDoubles + kk * kDRow + rr,
+                 bb ? b + gn + static_cast<long long>(gk) * ldb : b, bb);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < (kDBK * kDBM) / kDThreads; ++i) {
+      const int idx = tid + kDThreads * i;
+      const int kk = idx / kDBM, rr = idx % kDBM;
+      const int gk = kt * kDBK + kk;
+      const int gm = m0 + rr, gn = n0 + rr;
+      const bool va = gk < k && gm < m, vb = gk < k && gn < n;
+      cp_async8(As + s * kDStageDoubles + kk * kDRow + rr,
+                va ? a + gm + static_cast<long long>(gk) * lda : a, va);
+      cp_async8(Bs + s * kDStageDoubles + kk * kDRow + rr,
+                vb ? b + gn + static_cast<long long>(gk) * ldb : b, vb);
+    }
   }
 }
 
+template <bool VEC16>
 __global__ void __launch_bounds__(kDThreads, 1)
     dgemm_dmma(int m, int n, int k, double alpha, const double* __restrict__ a, long long lda,
                const double* __restrict__ b, long long ldb, double beta, double* __restrict__ c,
                long long ldc, int tiles_m) {
-  extern __shared__ double dsm[];
+  extern __shared__ __align__(16) double dsm[];
   double* As = dsm;
   double* Bs = dsm + kDStages * kDStageDoubles;
   const int m0 = (blockIdx.x % tiles_m) * kDBM;
   const int n0 = (blockIdx.x / tiles_m) * kDBN;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int wm = warp & 1, wn = warp >> 1;
+  const int wm = warp & 1, wn = warp >> 1; // warp tile: rows wm*64.., columns wn*32..
   const int g = lane >> 2, t = lane & 3;
 
-  double acc[8][4][2];
+#if XVRAM_DGEMM_MMA_K == 4
+  double acc[8][4][2]; // 8 x 4 blocks of 8 x 8
+#else
+  double acc[4][4][4]; // 4 x 4 blocks of 16 x 8
+#endif
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      acc[i][j][0] = acc[i][j][1] = 0.0;
+  for (int i = 0; i < int(sizeof(acc) / sizeof(double)); ++i)
+    (&acc[0][0][0])[i] = 0.0;
 
   const int k_tiles = (k + kDBK - 1) / kDBK;
 #pragma unroll
   for (int s = 0; s < kDStages - 1; ++s) {
     if (s < k_tiles)
-      dgemm_load_stage(As, Bs, a, lda, b, ldb, m, n, k, m0, n0, s, s, tid);
+      dgemm_load_stage<VEC16>(As, Bs, a, lda, b, ldb, m, n, k, m0, n0, s, s, tid);
     cp_async_commit(); // empty groups keep the group count uniform
   }
   for (int kt = 0; kt < k_tiles; ++kt) {
@@ -200,10 +254,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
     __syncthreads();               // ... everyone's; and stage kt - 1 is free
     const int nk = kt + kDStages - 1;
     if (nk < k_tiles)
-      dgemm_load_stage(As, Bs, a, lda, b, ldb, m, n, k, m0, n0, nk, nk % kDStages, tid);
+      dgemm_load_stage<VEC16>(As, Bs, a, lda, b, ldb, m, n, k, m0, n0, nk, nk % kDStages, tid);
     cp_async_commit();
     const double* as = As + (kt % kDStages) * kDStageDoubles + wm * 64 + g;
     const double* bs = Bs + (kt % kDStages) * kDStageDoubles + wn * 32 + g;
+#if XVRAM_DGEMM_MMA_K == 4
 #pragma unroll
     for (int k4 = 0; k4 < kDBK / 4; ++k4) {
       const int kr = (4 * k4 + t) * kDRow;
@@ -220,27 +275,59 @@ __global__ void __launch_bounds__(kDThreads, 1)
         for (int j = 0; j < 4; ++j)
           dmma_8x8x4(acc[i][j], af[i], bf[j]);
     }
+#else
+#pragma unroll
+    for (int k8 = 0; k8 < kDBK / 8; ++k8) {
+      const int r0 = (8 * k8 + t) * kDRow, r4 = r0 + 4 * kDRow;
+      double af[4][4], bf[4][2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        af[i][0] = as[r0 + 16 * i];
+        af[i][1] = as[r0 + 16 * i + 8];
+        af[i][2] = as[r4 + 16 * i];
+        af[i][3] = as[r4 + 16 * i + 8];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        bf[j][0] = bs[r0 + 8 * j];
+        bf[j][1] = bs[r4 + 8 * j];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          dmma_16x8x8(acc[i][j], af[i], bf[j]);
+    }
+#endif
   }
   cp_async_wait<0>();
 
   // Epilogue: alpha * acc + beta * C in FP64; C is not read when beta == 0.
+  const auto put = [&](int row, int col, double v) {
+    if (row < m && col < n) {
+      double* p = c + row + static_cast<long long>(col) * ldc;
+      const double x = alpha * v;
+      *p = beta == 0.0 ? x : fma(beta, *p, x);
+    }
+  };
+#if XVRAM_DGEMM_MMA_K == 4
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int row = m0 + wm * 64 + 8 * i + g;
-    if (row >= m)
-      continue;
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const int col = n0 + wn * 32 + 8 * j + 2 * t + v;
-        if (col < n) {
-          double* p = c + row + static_cast<long long>(col) * ldc;
-          const double x = alpha * acc[i][j][v];
-          *p = beta == 0.0 ? x : fma(beta, *p, x);
-        }
-      }
-  }
+      for (int v = 0; v < 2; ++v)
+        put(m0 + wm * 64 + 8 * i + g, n0 + wn * 32 + 8 * j + 2 * t + v, acc[i][j][v]);
+#else
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        put(m0 + wm * 64 + 16 * i + g + 8 * (v >> 1), n0 + wn * 32 + 8 * j + 2 * t + (v & 1),
+            acc[i][j][v]);
+#endif
 }
 
 uint64_t up(uint64_t v, uint64_t q) { return (v + q - 1) / q * q; }
@@ -316,16 +403,17 @@ cudaError_t gemm_fp64(int op_a, int op_b, int m, int n, int k, double alpha, con
       return e;
     b2 = bt;
   }
-  // Per call: the attribute belongs to the current device.
-  if (cudaError_t e = cudaFuncSetAttribute(dgemm_dmma,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kDSmemBytes);
-      e != cudaSuccess)
-    return e;
   const long long tiles_m = (m + kDBM - 1) / kDBM, tiles_n = (n + kDBN - 1) / kDBN;
   if (tiles_m * tiles_n > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
-  dgemm_dmma<<<static_cast<unsigned>(tiles_m * tiles_n), kDThreads, kDSmemBytes, stream>>>(
+  const bool vec16 = aligned(a2, 16) && aligned(b2, 16) && lda2 % 2 == 0 && ldb2 % 2 == 0;
+  const auto kernel = vec16 ? dgemm_dmma<true> : dgemm_dmma<false>;
+  // Per call: the attribute belongs to the current device.
+  if (cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kDSmemBytes);
+      e != cudaSuccess)
+    return e;
+  kernel<<<static_cast<unsigned>(tiles_m * tiles_n), kDThreads, kDSmemBytes, stream>>>(
       m, n, k, alpha, a2, lda2, b2, ldb2, beta, c, ldc, static_cast<int>(tiles_m));
   return cudaGetLastError();
 }
