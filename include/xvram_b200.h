@@ -155,6 +155,27 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
     const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
     const uint64_t lds[3], char* operand);
 
+/* What the library's device layer reports for one device (the GEMM bench report's device
+ * and build sections).  struct_size = sizeof before the call. */
+typedef struct xvram_b200_device_info_v1 {
+  uint32_t struct_size;
+  int32_t ordinal;
+  int32_t device_count;
+  char name[128];
+  uint64_t total_bytes;
+  uint64_t free_bytes;
+  int32_t sm_count;
+  int32_t compute_capability_major;
+  int32_t compute_capability_minor;
+  int32_t driver_version;           /* cudaDriverGetVersion */
+  uint64_t vmm_granularity;         /* recommended physical allocation granularity */
+  int32_t runtime_headers_version;  /* CUDART_VERSION the library was built with */
+  int32_t reserved0;
+} xvram_b200_device_info_v1;
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_device_query(int32_t ordinal,
+                                                               xvram_b200_device_info_v1* out);
+
 /* xvram_b200_validate_gemm with element types (A, B, C; XVRAM_DATA_* numbering) and an
  * arithmetic (0 strict FP32, 1 TF32, 2 FP64: the reference's gemm::ComputeMode,
  * src/gemm/planner.hpp:25-36), following the whole of gemm::validate_problem

@@ -138,6 +138,8 @@ public:
     info->sm_count = 148;
     info->vmm_granularity = kGranularity;
     info->driver_version = 0;
+    info->cc_major = 10;
+    info->cc_minor = 0;
     return {};
   }
   xvram::Error close() override { return {}; }

@@ -45,6 +45,18 @@ class RuntimeInfo(C.Structure):
     ]
 
 
+class DeviceInfo(C.Structure):
+    """xvram_b200_device_info_v1 (include/xvram_b200.h)."""
+
+    _fields_ = [
+        ("struct_size", u32), ("ordinal", i32), ("device_count", i32),
+        ("name", C.c_char * 128), ("total_bytes", u64), ("free_bytes", u64),
+        ("sm_count", i32), ("compute_capability_major", i32), ("compute_capability_minor", i32),
+        ("driver_version", i32), ("vmm_granularity", u64), ("runtime_headers_version", i32),
+        ("reserved0", i32),
+    ]
+
+
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
@@ -106,6 +118,8 @@ def _load() -> C.CDLL:
     lib.xvram_get_api.restype = u32
     lib.xvram_b200_bias_activation.argtypes = [u64, i64, i64, i64, u64, u32, u64]
     lib.xvram_b200_bias_activation.restype = u32
+    lib.xvram_b200_device_query.argtypes = [i32, C.POINTER(DeviceInfo)]
+    lib.xvram_b200_device_query.restype = u32
     lib.xvram_b200_test_set_device_factory.argtypes = [vp]
     lib.xvram_b200_test_set_device_factory.restype = u32
     return lib
@@ -119,6 +133,7 @@ EXPORTED = (
     "xvram_get_api",
     "xvram_b200_bias_activation",
     "xvram_b200_test_set_device_factory",
+    "xvram_b200_device_query",
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",

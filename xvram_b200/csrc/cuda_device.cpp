@@ -13,6 +13,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -115,6 +116,8 @@ public:
     info->sm_count = prop.multiProcessorCount;
     info->vmm_granularity = gran;
     info->driver_version = driver_version;
+    info->cc_major = prop.major;
+    info->cc_minor = prop.minor;
     return {};
   }
 
@@ -369,6 +372,38 @@ std::unique_ptr<Device> external_factory() {
 } // namespace
 
 } // namespace xvram
+
+extern "C" XVRAM_B200_API xvram_status XVRAM_CALL
+xvram_b200_device_query(int32_t ordinal, xvram_b200_device_info_v1* out) {
+  if (!out || out->struct_size < sizeof(xvram_b200_device_info_v1))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  std::unique_ptr<xvram::Device> dev = xvram::device_factory()();
+  if (!dev)
+    return XVRAM_STATUS_UNAVAILABLE;
+  xvram::DeviceInfo info;
+  if (xvram::Error e = dev->open(ordinal, &info)) {
+    (void)dev->close();
+    return e.status;
+  }
+  uint64_t free_bytes = 0, total_bytes = 0;
+  const xvram::Error mem = dev->mem_get_info(&free_bytes, &total_bytes);
+  (void)dev->close();
+  const uint32_t size = out->struct_size;
+  *out = xvram_b200_device_info_v1{};
+  out->struct_size = size;
+  out->ordinal = info.ordinal;
+  out->device_count = info.device_count;
+  std::snprintf(out->name, sizeof(out->name), "%s", info.name.c_str());
+  out->total_bytes = info.total_bytes;
+  out->free_bytes = mem ? 0 : free_bytes;
+  out->sm_count = info.sm_count;
+  out->compute_capability_major = info.cc_major;
+  out->compute_capability_minor = info.cc_minor;
+  out->vmm_granularity = info.vmm_granularity;
+  out->driver_version = info.driver_version;
+  out->runtime_headers_version = CUDART_VERSION;
+  return XVRAM_STATUS_SUCCESS;
+}
 
 extern "C" XVRAM_B200_API xvram_status XVRAM_CALL
 xvram_b200_test_set_device_factory(void* (*create)(void)) {

@@ -25,6 +25,7 @@ struct DeviceInfo {
   int sm_count = 0;
   uint64_t vmm_granularity = 0; // physical allocation granularity for cuMemCreate
   int driver_version = 0;
+  int cc_major = 0, cc_minor = 0;
 };
 
 using StreamId = uint64_t;

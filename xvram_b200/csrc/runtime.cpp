@@ -383,6 +383,7 @@ struct Runtime::Impl {
         capacity = target;
         ++t.budget_grows;
         t.cache_target_bytes = capacity * cb;
+        t.cache_target_maximum_bytes = std::max(t.cache_target_maximum_bytes, capacity * cb);
       }
     } else {
       growth_samples = 0;
@@ -479,8 +480,10 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
   m.max_capacity = m.capacity;
   m.last_budget_sample = std::chrono::steady_clock::now();
   m.t.cache_target_bytes = m.capacity * m.cb;
-  m.t.cache_target_minimum_bytes = m.capacity * m.cb; // lowest target seen so far
-  m.t.cache_target_maximum_bytes = usable;
+  // Lowest and highest targets seen so far (reference src/residency/runtime.cpp:321,
+  // :3415-3460).
+  m.t.cache_target_minimum_bytes = m.capacity * m.cb;
+  m.t.cache_target_maximum_bytes = m.capacity * m.cb;
   m.t.cuda_driver_version = static_cast<uint32_t>(m.info.driver_version);
   m.t.cuda_free_bytes_minimum = free_b;
   m.t.cuda_free_bytes_end = free_b;
@@ -595,6 +598,7 @@ Error Runtime::release(uint64_t id) {
     if (Error e = m.dev->host_free(a.host))
       return e;
     m.x.host_backing_bytes -= a.bytes;
+    m.t.pinned_staging_bytes = m.x.host_backing_bytes;
     a.host = nullptr;
   }
   // The address range stays reserved (tombstoned) until close so a freed pointer can
@@ -1010,8 +1014,13 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     for (uint32_t li = st.load_begin; li < st.load_begin + st.load_count && !err; ++li) {
       const PanelLoad& ld = plan.loads[li];
       const size_t sl = static_cast<size_t>(ld.slot);
-      if (used_rec[sl] && (err = dev->stream_wait_event(s_h2d, used[sl])))
-        break;
+      // A slot is reused only after the event of its last GEMM: an event boundary, as
+      // when the reference retires a mapping after its completion event.
+      if (used_rec[sl]) {
+        if ((err = dev->stream_wait_event(s_h2d, used[sl])))
+          break;
+        ++t.event_boundaries;
+      }
       const int64_t lk0 = static_cast<int64_t>(ld.kpanel) * kb;
       const int64_t lkr = std::min(kb, K - lk0);
       uint64_t src = 0, spitch = 0, width = 0, height = 0, dpitch = 0;
@@ -1138,6 +1147,7 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     if (e && !err)
       err = e;
     ++t.unmaps;
+    ++t.event_boundaries; // unmapped after the drain above
     frames[arena_frames[i]].owner = 0;
   }
   if (Error e = dev->va_free(arena, nframes * cb); e && !err)

@@ -220,6 +220,12 @@ class Allocation:
         self.sdk.check("allocation_read",
                        self.sdk.t.allocation_read(self.handle, offset, ptr, n if nbytes is None else nbytes))
 
+    def info(self) -> AllocationInfo:
+        out = AllocationInfo(struct_size=C.sizeof(AllocationInfo))
+        self.sdk.check("allocation_get_info",
+                       self.sdk.t.allocation_get_info(self.handle, C.byref(out)))
+        return out
+
     def release(self) -> int:
         st = self.sdk.t.allocation_release(self.handle)
         if st == SUCCESS:
