@@ -18,7 +18,9 @@ MiB = 1 << 20
                                                    ("fp16", "fp16", "auto"),
                                                    ("fp64", None, "auto")])
 def test_out_of_core_report(dtype, c_dtype, compute):
-    m, n, k = (2048, 1536, 1024) if dtype != "fp64" else (1536, 1024, 1024)
+    # operands above the 32 MiB budget in every case (40-48 MiB before workspace)
+    m, n, k = {"fp32": (2048, 2048, 2048), "fp16": (4096, 2048, 2048),
+               "fp64": (2048, 1024, 1024)}[dtype]
     rep = gemm_bench.run(m, n, k, 0, 1, dtype, c_dtype, compute, 1.0, 1.0, passes=2,
                          cache_target_bytes=32 * MiB, chunk_bytes=2 * MiB)
     assert rep["outcome"]["status"] == "completed", rep["outcome"]
