@@ -155,6 +155,18 @@ XVRAM_B200_API int32_t XVRAM_CALL xvram_b200_validate_gemm(
     const uint64_t offsets[3], const uint64_t rows[3], const uint64_t columns[3],
     const uint64_t lds[3], char* operand);
 
+/* The reference benches' report digests, for reports in their formats.  Hex form of a
+ * state: 16 hex digits of state[1], then 16 of state[0].
+ *   GEMM bench (src/gemm_bench/executor.cpp:42-65): bytes with their absolute offsets.
+ *   Compat bench (src/compat_bench/pattern.cpp, pattern.hpp:29-30): FP32 values. */
+#define XVRAM_B200_BENCH_DIGEST_INIT {UINT64_C(1469598103934665603), \
+                                      UINT64_C(1099511628211) ^ UINT64_C(0x9E3779B97F4A7C15)}
+#define XVRAM_B200_COMPAT_DIGEST_INIT {UINT64_C(1469598103934665603), UINT64_C(0x9e3779b97f4a7c15)}
+XVRAM_B200_API void XVRAM_CALL xvram_b200_digest_bench(const void* data, uint64_t len,
+                                                       uint64_t absolute_offset, uint64_t state[2]);
+XVRAM_B200_API void XVRAM_CALL xvram_b200_digest_compat(const float* values, uint64_t count,
+                                                        uint64_t state[2]);
+
 /* What the library's device layer reports for one device (the GEMM bench report's device
  * and build sections).  struct_size = sizeof before the call. */
 typedef struct xvram_b200_device_info_v1 {

@@ -10,7 +10,10 @@
 #include "gemm/planner.hpp"
 #include "gemm_bench/pattern.hpp"
 
+#include <cstring>
+#include <string>
 #include <cstdint>
+#include <cstdio>
 #include <thread>
 #include <vector>
 
@@ -109,6 +112,17 @@ XR_EXPORT int xr_validate_problem(std::uint64_t m, std::uint64_t n, std::uint64_
   const auto v = gm::validate_problem(p);
   *operand = v.operand;
   return static_cast<int>(v.error);
+}
+
+// The compat bench's report digest over `count` floats, as the 32 hex digits of its two
+// lanes (b, then a, as Digest::string prints them; formatted here with snprintf so no
+// iostream state crosses into the host process) plus the terminating zero in out.
+XR_EXPORT void xr_cb_digest(const float* values, std::uint64_t count, char* out) {
+  cb::Digest d;
+  for (std::uint64_t i = 0; i < count; ++i)
+    d.add(values[i]);
+  std::snprintf(out, 33, "%016llx%016llx", static_cast<unsigned long long>(d.b),
+                static_cast<unsigned long long>(d.a));
 }
 
 // gemm::validate_problem with element types (A, B, C; gemm::ElementType order) and a

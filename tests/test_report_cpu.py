@@ -90,3 +90,43 @@ def test_traced_call_sequence():
     assert [t["tiles_retired"] for t in tiles] == [1, 2]
     times = [r["monotonic_timestamp_ns"] for r in recs]
     assert times == sorted(times)
+
+
+def test_compat_digest_matches_the_reference_implementation(ref_lib):
+    """The compat bench digest against the reference's own Digest (compiled in oracle/_ref)."""
+    import ctypes as C
+
+    import numpy as np
+
+    from xvram_b200.report import compat_digest
+    if not hasattr(ref_lib, "xr_cb_digest"):
+        import pytest
+        pytest.skip("reference shim predates xr_cb_digest")
+    ref_lib.xr_cb_digest.argtypes = [C.c_void_p, C.c_uint64, C.c_char_p]
+    rng = np.random.default_rng(3)
+    for count in (0, 1, 7, 1000):
+        v = rng.uniform(-1e3, 1e3, count).astype(np.float32)
+        out = C.create_string_buffer(33)
+        ref_lib.xr_cb_digest(v.ctypes.data, count, out)
+        assert compat_digest(v) == out.value.decode()
+
+
+def test_bench_digest_follows_its_definition():
+    """The GEMM bench digest (reference src/gemm_bench/executor.cpp:42-65) against a plain
+    restatement of its two lanes, including a non-zero starting offset."""
+    import numpy as np
+
+    from xvram_b200.report import BENCH_DIGEST_INIT, bench_digest
+    mask = (1 << 64) - 1
+
+    def slow(data: bytes, offset: int) -> str:
+        low, high = BENCH_DIGEST_INIT
+        for i, v in enumerate(data):
+            idx = offset + i
+            low = ((low ^ (v + (idx & 0xFF))) * 1099511628211) & mask
+            high = ((high ^ (v + 0x9E + (idx >> 8))) * 0x100000001B3) & mask
+            high ^= high >> 29
+        return f"{high:016x}{low:016x}"
+    data = np.random.default_rng(5).integers(0, 256, 3000, dtype=np.uint8)
+    for off in (0, 1, 255, 70000):
+        assert bench_digest(data, off) == slow(data.tobytes(), off)

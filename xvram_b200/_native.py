@@ -118,6 +118,10 @@ def _load() -> C.CDLL:
     lib.xvram_get_api.restype = u32
     lib.xvram_b200_bias_activation.argtypes = [u64, i64, i64, i64, u64, u32, u64]
     lib.xvram_b200_bias_activation.restype = u32
+    lib.xvram_b200_digest_bench.argtypes = [vp, u64, u64, C.POINTER(u64)]
+    lib.xvram_b200_digest_bench.restype = None
+    lib.xvram_b200_digest_compat.argtypes = [vp, u64, C.POINTER(u64)]
+    lib.xvram_b200_digest_compat.restype = None
     lib.xvram_b200_device_query.argtypes = [i32, C.POINTER(DeviceInfo)]
     lib.xvram_b200_device_query.restype = u32
     lib.xvram_b200_test_set_device_factory.argtypes = [vp]
@@ -134,6 +138,8 @@ EXPORTED = (
     "xvram_b200_bias_activation",
     "xvram_b200_test_set_device_factory",
     "xvram_b200_device_query",
+    "xvram_b200_digest_bench",
+    "xvram_b200_digest_compat",
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",

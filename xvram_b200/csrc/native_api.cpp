@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace xvram {
@@ -201,6 +202,51 @@ XVRAM_B200_API void XVRAM_CALL xvram_b200_fill_uniform(float* dst, uint64_t coun
                                                        uint64_t first_index, int32_t threads) {
   if (dst && count)
     fill_uniform(dst, count, seed, first_index, threads);
+}
+
+// The reference GEMM bench's 128-bit digest (src/gemm_bench/executor.cpp:42-65): two 64-bit
+// lanes over the bytes, each mixed with its absolute offset.  The digest is part of the
+// report format (expected and output digests are compared across tools), so its steps are
+// the reference's.  state = {low, high}; start from XVRAM_B200_BENCH_DIGEST_INIT.
+XVRAM_B200_API void XVRAM_CALL xvram_b200_digest_bench(const void* data, uint64_t len,
+                                                       uint64_t absolute_offset,
+                                                       uint64_t state[2]) {
+  if (!data || !state)
+    return;
+  const unsigned char* p = static_cast<const unsigned char*>(data);
+  uint64_t low = state[0], high = state[1], index = absolute_offset;
+  for (uint64_t i = 0; i < len; ++i, ++index) {
+    const uint64_t v = p[i];
+    low ^= v + (index & 0xFFull);
+    low *= 1099511628211ull;
+    high ^= v + 0x9Eull + (index >> 8);
+    high *= 0x100000001B3ull;
+    high ^= high >> 29;
+  }
+  state[0] = low;
+  state[1] = high;
+}
+
+// The reference compat bench's digest (src/compat_bench/pattern.cpp Digest::add, state
+// pattern.hpp:29-30): per float, its four bytes from the least significant.
+// state = {a, b}; start from XVRAM_B200_COMPAT_DIGEST_INIT.
+XVRAM_B200_API void XVRAM_CALL xvram_b200_digest_compat(const float* values, uint64_t count,
+                                                        uint64_t state[2]) {
+  if (!values || !state)
+    return;
+  uint64_t a = state[0], b = state[1];
+  for (uint64_t i = 0; i < count; ++i) {
+    uint32_t bits;
+    std::memcpy(&bits, values + i, 4);
+    for (unsigned shift = 0; shift < 32; shift += 8) {
+      const uint64_t byte = (bits >> shift) & 255u;
+      a = (a ^ byte) * 1099511628211ull;
+      b = (b ^ (byte + 0x9eu)) * 0x100000001b3ull;
+      b ^= b >> 29;
+    }
+  }
+  state[0] = a;
+  state[1] = b;
 }
 
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_plan_panels(

@@ -22,8 +22,8 @@ The report fills every field of the schema from this run: plans and workloads fr
 gemm_plan_get_info and the operations' info, cache and telemetry from the session's
 telemetry, proof from checks made here (see `proof`).  Differences from the reference's
 writer, all stated in the report's own terms:
-  * digests are BLAKE2b-128 of C's bytes (expected and actual), not the reference's
-    digest function, so digest values are comparable within this tool only;
+  * digests are the reference bench's 128-bit digest of C's bytes (column-major, from
+    byte offset 0), expected and actual;
   * build.cuda_headers_version is the CUDA runtime version the library was built with
     (12090 here); the reference's schema asks for >= 13000 because the reference itself
     needs CUDA 13;
@@ -36,7 +36,6 @@ from __future__ import annotations
 import argparse
 import ctypes as C
 import datetime
-import hashlib
 import json
 import os
 import platform
@@ -49,6 +48,7 @@ import numpy as np
 
 from . import sdk
 from ._native import DeviceInfo, lib
+from .report import bench_digest
 
 DTYPES = {"fp16": sdk.FP16, "bf16": sdk.BF16, "fp32": sdk.FP32, "fp64": sdk.FP64}
 DTYPE_NAMES = {v: k for k, v in DTYPES.items()}
@@ -105,7 +105,8 @@ def decode(stored: np.ndarray, dtype: int) -> np.ndarray:
 
 
 def digest128(arr: np.ndarray) -> str:
-    return hashlib.blake2b(np.ascontiguousarray(arr).tobytes(), digest_size=16).hexdigest()
+    """The reference bench's digest of C's bytes (column-major, from offset 0)."""
+    return bench_digest(np.ascontiguousarray(arr).view(np.uint8))
 
 
 def stored_operand(which: str, op: int, m: int, n: int, k: int, dtype: int) -> np.ndarray:

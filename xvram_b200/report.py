@@ -20,6 +20,41 @@ from typing import IO, Optional
 
 TRANSITIONS = ("call", "return", "retired_tile", "final")
 
+BENCH_DIGEST_INIT = (1469598103934665603, 1099511628211 ^ 0x9E3779B97F4A7C15)
+COMPAT_DIGEST_INIT = (1469598103934665603, 0x9E3779B97F4A7C15)
+
+
+def _hex(state) -> str:
+    return f"{state[1]:016x}{state[0]:016x}"
+
+
+def bench_digest(data, absolute_offset: int = 0) -> str:
+    """The reference GEMM bench's 128-bit digest of a byte buffer (numpy array or bytes)
+    whose first byte sits at `absolute_offset` (xvram_b200_digest_bench)."""
+    import ctypes as C
+
+    import numpy as np
+
+    from ._native import lib
+    buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8) if isinstance(data, bytes)
+                               else data)
+    state = (C.c_uint64 * 2)(*BENCH_DIGEST_INIT)
+    lib.xvram_b200_digest_bench(buf.ctypes.data, buf.nbytes, absolute_offset, state)
+    return _hex(state)
+
+
+def compat_digest(values) -> str:
+    """The reference compat bench's digest of FP32 values (xvram_b200_digest_compat)."""
+    import ctypes as C
+
+    import numpy as np
+
+    from ._native import lib
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    state = (C.c_uint64 * 2)(*COMPAT_DIGEST_INIT)
+    lib.xvram_b200_digest_compat(v.ctypes.data, v.size, state)
+    return _hex(state)
+
 
 def trace_record(sequence: int, timestamp_ns: int, transition: str, operation_id: int,
                  allocation_id: Optional[int], nbytes: int, tiles_retired: int,
