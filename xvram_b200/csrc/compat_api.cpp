@@ -188,6 +188,10 @@ public:
         tel_.live_allocations = 0;
         tel_.live_handles = 0;
         tel_.logical_bytes = 0;
+        // The worker had no call in flight (calls are serialised) and the runtime's close
+        // synchronised its streams and destroyed every event.
+        tel_.cleanup_operations_drained = 1;
+        tel_.cleanup_events_drained = 1;
         tel_.cleanup_completed = 1;
       }
     }
@@ -552,6 +556,8 @@ private:
     tel_.host_backing_peak_bytes = x.host_backing_peak_bytes;
     tel_.retired_va_reservations = x.retired_va_reservations;
     tel_.retired_va_bytes = x.retired_va_bytes;
+    tel_.retired_va_reservations_freed = x.retired_va_reservations_freed;
+    tel_.retired_va_bytes_freed = x.retired_va_bytes_freed;
     ++tel_.progress_sequence;
     info_.struct_size = sizeof(info_);
     info_.frame_bytes = runtime_->chunk_bytes();

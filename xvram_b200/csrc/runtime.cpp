@@ -539,6 +539,10 @@ Error Runtime::close() {
       a.host = nullptr;
     }
     keep(m.dev->va_free(a.va, a.reserved));
+    if (!a.live) { // a tombstoned range of a released allocation
+      ++m.x.retired_va_reservations_freed;
+      m.x.retired_va_bytes_freed += a.reserved;
+    }
   }
   m.allocs.clear();
   for (auto& f : m.frames) {

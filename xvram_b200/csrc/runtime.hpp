@@ -105,6 +105,9 @@ struct RuntimeExtra {
   uint64_t host_backing_peak_bytes = 0;
   uint64_t retired_va_reservations = 0;
   uint64_t retired_va_bytes = 0;
+  // Tombstoned ranges released at close.
+  uint64_t retired_va_reservations_freed = 0;
+  uint64_t retired_va_bytes_freed = 0;
   // Last streamed plan.
   int64_t last_mb = 0, last_nb = 0, last_kb = 0;
   int64_t last_steps = 0;

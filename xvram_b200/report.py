@@ -72,7 +72,10 @@ def trace_record(sequence: int, timestamp_ns: int, transition: str, operation_id
 
 class TracedCompat:
     """Wraps a CompatApi: every malloc / free / memcpy / sgemm writes call and return
-    records (and the tiles retired in between) to `sink`, one JSON object per line."""
+    records (and the tiles retired in between) to `sink`, one JSON object per line.
+    Allocations are identified by sequence numbers given at malloc (as the reference's
+    bench does), never by their addresses; a call on an interior pointer names the
+    allocation that contains it."""
 
     def __init__(self, api, sink: IO[str]):
         self.api, self.sink = api, sink
@@ -81,6 +84,14 @@ class TracedCompat:
         self.operation = 0
         self.tiles = int(api.telemetry().tiles_retired)
         self.records = 0
+        self.next_allocation = 0
+        self.allocations: dict[int, tuple[int, int]] = {}  # base -> (id, bytes)
+
+    def _allocation(self, ptr: int):
+        for base, (ident, size) in self.allocations.items():
+            if base <= ptr < base + max(size, 1):
+                return ident
+        return None
 
     def _emit(self, transition, allocation, nbytes, reason):
         self.sequence += 1
@@ -110,19 +121,28 @@ class TracedCompat:
         return out
 
     def malloc(self, nbytes):
-        return self._traced("malloc_device", None, nbytes, lambda: self.api.malloc(nbytes))
+        self.next_allocation += 1
+        ident = self.next_allocation
+        ptr = self._traced("malloc_device", ident, nbytes, lambda: self.api.malloc(nbytes))
+        self.allocations[ptr] = (ident, nbytes)
+        return ptr
 
     def free(self, ptr):
-        return self._traced("free_device", ptr, 0, lambda: self.api.free(ptr))
+        ident = self._allocation(ptr)
+        out = self._traced("free_device", ident, 0, lambda: self.api.free(ptr))
+        self.allocations.pop(ptr, None)
+        return out
 
     def h2d(self, dst, src_ptr, nbytes):
-        return self._traced("memcpy_h2d", dst, nbytes, lambda: self.api.h2d(dst, src_ptr, nbytes))
+        return self._traced("memcpy_h2d", self._allocation(dst), nbytes,
+                            lambda: self.api.h2d(dst, src_ptr, nbytes))
 
     def d2h(self, dst_ptr, src, nbytes):
-        return self._traced("memcpy_d2h", src, nbytes, lambda: self.api.d2h(dst_ptr, src, nbytes))
+        return self._traced("memcpy_d2h", self._allocation(src), nbytes,
+                            lambda: self.api.d2h(dst_ptr, src, nbytes))
 
     def sgemm(self, h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc):
-        return self._traced("blas_sgemm", c, 0, lambda: self.api.sgemm(
+        return self._traced("blas_sgemm", self._allocation(c), 0, lambda: self.api.sgemm(
             h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc))
 
     def close(self, ok: bool = True) -> None:
