@@ -240,6 +240,17 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void*
                                                                    uint64_t* out_group);
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_destroy(uint64_t group);
 
+/* All-gather of row blocks, collectively on every rank of the group, enqueued on `stream`
+ * (a cudaStream_t of the group's device): rank q's block (rows x cols, column-major,
+ * ld_block) becomes rows [q rows, (q + 1) rows) of every rank's dst (world rows x cols,
+ * ld_dst).  `staging` is device scratch of world x rows x cols floats.  This is the
+ * activation exchange of a Linear layer split by output features (each rank computes its
+ * rows of Y = W X; the next layer needs all of them).  One ncclAllGather over NVLink plus
+ * device copies; POISONED after the group was aborted. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_allgather_rows(
+    uint64_t group, const float* block, int64_t rows, int64_t cols, int64_t ld_block, float* dst,
+    int64_t ld_dst, void* staging, uint64_t staging_bytes, uint64_t stream);
+
 /*
  * C_local = alpha * op(A_local) * op(B) + beta * C_local for this rank's m_local rows of C,
  * all operands in (preferably page-locked) host memory, column-major.  A_local holds this

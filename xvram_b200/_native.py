@@ -80,6 +80,8 @@ def _load() -> C.CDLL:
     lib.xvram_b200_shard_group_create.restype = u32
     lib.xvram_b200_shard_group_destroy.argtypes = [u64]
     lib.xvram_b200_shard_group_destroy.restype = u32
+    lib.xvram_b200_shard_allgather_rows.argtypes = [u64, vp, i64, i64, i64, vp, i64, vp, u64, u64]
+    lib.xvram_b200_shard_allgather_rows.restype = u32
     lib.xvram_b200_sgemm_sharded.argtypes = [u64, u32, u32, i64, i64, i64, f32, vp, i64, vp, i64,
                                              f32, vp, i64, i64]
     lib.xvram_b200_sgemm_sharded.restype = u32
@@ -148,6 +150,7 @@ EXPORTED = (
     "xvram_b200_shard_unique_id",
     "xvram_b200_shard_group_create",
     "xvram_b200_shard_group_destroy",
+    "xvram_b200_shard_allgather_rows",
     "xvram_b200_sgemm_sharded",
     "xvram_b200_fill_uniform",
     "xvram_b200_plan_panels",

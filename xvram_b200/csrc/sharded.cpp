@@ -376,6 +376,46 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void*
   return XVRAM_STATUS_SUCCESS;
 }
 
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_allgather_rows(
+    uint64_t group, const float* block, int64_t rows, int64_t cols, int64_t ld_block, float* dst,
+    int64_t ld_dst, void* staging, uint64_t staging_bytes, uint64_t stream) {
+  auto* g = reinterpret_cast<ShardGroup*>(group);
+  if (!g || !block || !dst || !staging || rows <= 0 || cols <= 0 || ld_block < rows ||
+      ld_dst < rows * g->world)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  const uint64_t per_rank = static_cast<uint64_t>(rows) * static_cast<uint64_t>(cols);
+  if (staging_bytes < per_rank * 4 * static_cast<uint64_t>(g->world))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  if (g->aborted)
+    return XVRAM_STATUS_POISONED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* stage = static_cast<float*>(staging);
+  float* mine = stage + per_rank * static_cast<uint64_t>(g->rank);
+  // 1. this rank's block, packed (ld = rows) into its slot of the staging buffer
+  cudaError_t e = cudaMemcpy2DAsync(mine, static_cast<size_t>(rows) * 4, block,
+                                    static_cast<size_t>(ld_block) * 4,
+                                    static_cast<size_t>(rows) * 4, static_cast<size_t>(cols),
+                                    cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess)
+    return XVRAM_STATUS_CUDA_ERROR;
+  // 2. every rank's block into every rank's staging buffer (in place)
+  if (g->world > 1)
+    if (xvram_status st = nccl_issued(*g, nccl().all_gather(mine, stage, per_rank, ncclFloat,
+                                                            g->comm, s));
+        st != XVRAM_STATUS_SUCCESS)
+      return st;
+  // 3. block q becomes rows [q rows, (q + 1) rows) of dst
+  for (int q = 0; q < g->world; ++q) {
+    e = cudaMemcpy2DAsync(dst + static_cast<uint64_t>(q) * static_cast<uint64_t>(rows),
+                          static_cast<size_t>(ld_dst) * 4, stage + per_rank * q,
+                          static_cast<size_t>(rows) * 4, static_cast<size_t>(rows) * 4,
+                          static_cast<size_t>(cols), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess)
+      return XVRAM_STATUS_CUDA_ERROR;
+  }
+  return XVRAM_STATUS_SUCCESS;
+}
+
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_destroy(uint64_t group) {
   destroy_group(reinterpret_cast<ShardGroup*>(group));
   return XVRAM_STATUS_SUCCESS;

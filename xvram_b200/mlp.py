@@ -90,3 +90,98 @@ class StreamedMLP:
         for p in self.plans:
             self.s.t.gemm_plan_release(p)
         self.plans = []
+
+
+class ShardedMLP:
+    """The same MLP over the ranks of a ShardGroup (one process per GPU), each layer split
+    by output features: rank r holds rows [r F/P, (r + 1) F/P) of every weight (and its
+    bias slice) in host memory and streams only those through its own session, computes
+    its rows of Y = W X, applies bias + ReLU, and the row blocks are all-gathered over
+    NVLink into every rank's next activation (xvram_b200_shard_allgather_rows).  Host
+    traffic per rank per forward is 1/P of the weights; the exchange is F x B floats per
+    layer.  Collective: every rank calls forward with the same input."""
+
+    def __init__(self, session: "sdk.Sdk", group, features: int, batch: int, layers: int):
+        P, r = group.world, group.rank
+        if features % P:
+            raise ValueError("features must divide evenly over the ranks")
+        self.s, self.g, self.F, self.B, self.L = session, group, features, batch, layers
+        self.Fr = features // P
+        self.wbytes = self.Fr * features * 4
+        self.abytes = features * batch * 4
+        self.ybytes = self.Fr * batch * 4
+        self.W = [session.alloc(self.wbytes) for _ in range(layers)]
+        self.bias = session.alloc(layers * self.Fr * 4)
+        self.H = [session.alloc(self.abytes), session.alloc(self.abytes)]
+        self.Y = session.alloc(self.ybytes)
+        self.statuses: list[int] = []
+        F, Fr, Bt = features, self.Fr, batch
+        self.plans = []
+        for i in range(layers):
+            d = session.gemm_desc(sdk.matrix(self.W[i], Fr, F, Fr),
+                                  sdk.matrix(self.H[i % 2], F, Bt, F),
+                                  sdk.matrix(self.Y, Fr, Bt, Fr), sdk.OP_N, sdk.OP_N,
+                                  mode=sdk.COMPUTE_FP32_STRICT)
+            self.plans.append(session.plan(d))
+        self.txns = [session.transaction_desc(
+            [(self.Y, 0, self.ybytes, sdk.READ_WRITE),
+             (self.bias, i * Fr * 4, Fr * 4, sdk.READ),
+             (self.H[(i + 1) % 2], 0, self.abytes, sdk.WRITE_ONLY)],
+            self._body(), workspace_bytes=self.abytes) for i in range(layers)]
+        self.prefetches = [session.prefetch_desc([(w, 0, self.wbytes, sdk.READ)]) for w in self.W]
+
+    def _body(self):
+        F, Fr, Bt, g = self.F, self.Fr, self.B, self.g
+
+        def body(ctx):
+            y, b, h = ctx.ranges[0], ctx.ranges[1], ctx.ranges[2]
+            st = sdk.bias_activation(y.device_address, Fr, Fr, Bt, b.device_address, True,
+                                     ctx.native_stream)
+            if st == sdk.SUCCESS:
+                st = g.allgather_rows(y.device_address, Fr, Bt, Fr, h.device_address, F,
+                                      ctx.workspace_device_address, ctx.workspace_bytes,
+                                      ctx.native_stream)
+            self.statuses.append(st)
+            return st
+        return body
+
+    def load_weight(self, i: int, host_rows) -> None:
+        """This rank's rows of weight i: an (F / P) x F column-major FP32 block (out x in)."""
+        self.W[i].write(host_rows)
+
+    def load_biases(self, host) -> None:
+        """This rank's bias slices, layer after layer (layers x F / P floats)."""
+        self.bias.write(host)
+
+    def forward(self, x_host, out_host) -> None:
+        """x_host, out_host: batch x F row-major FP32 host buffers (the whole activation on
+        every rank)."""
+        s = self.s
+        self.H[0].write(x_host)
+        ops = []
+
+        def submit(fn, *args):
+            op = C.c_void_p()
+            s.check(fn, getattr(s.t, fn)(*args, C.byref(op)))
+            ops.append(op.value)
+        submit("prefetch_submit", s.session, C.byref(self.prefetches[0]))
+        for i in range(self.L):
+            if i + 1 < self.L:
+                submit("prefetch_submit", s.session, C.byref(self.prefetches[i + 1]))
+            submit("gemm_submit", self.plans[i])
+            submit("transaction_submit", s.session, C.byref(self.txns[i]))
+        failure = None
+        for op in ops:
+            info = s.wait(op)
+            if info.result != sdk.SUCCESS and failure is None:
+                failure = sdk.SdkError("sharded MLP layer operation", info.result,
+                                       s.op_error(op))
+            s.t.operation_release(op)
+        if failure is not None:
+            raise failure
+        self.H[self.L % 2].read(out_host)
+
+    def close(self) -> None:
+        for p in self.plans:
+            self.s.t.gemm_plan_release(p)
+        self.plans = []

@@ -53,6 +53,12 @@ class ShardGroup:
         return lib.xvram_b200_sgemm_sharded(self.handle, op_a, op_b, m_local, n, k, alpha, _ptr(a),
                                             lda, _ptr(b), ldb, beta, _ptr(c), ldc, panel_k)
 
+    def allgather_rows(self, block: int, rows: int, cols: int, ld_block: int, dst: int,
+                       ld_dst: int, staging: int, staging_bytes: int, stream: int) -> int:
+        """xvram_b200_shard_allgather_rows on raw device addresses and a native stream."""
+        return lib.xvram_b200_shard_allgather_rows(self.handle, block, rows, cols, ld_block, dst,
+                                                   ld_dst, staging, staging_bytes, stream)
+
     def close(self) -> None:
         if self.handle:
             lib.xvram_b200_shard_group_destroy(self.handle)
