@@ -418,27 +418,59 @@ def run_sharded_c4(args) -> None:
 def run_mlp(args) -> None:
     """BASELINE config 5 through the SDK (include/xvram.h): 24 x Linear(16384 -> 16384,
     bias) + ReLU, batch 512, weights N(0, 1/16384), input uniform[-1,1], device budget
-    8 GiB.  The 24 GiB of weights live in the session's pinned host backing; every forward
+    8 GiB per GPU.  The weights live in the session's pinned host backing; every forward
     streams each layer's weight through the frame cache.  Per layer the host submits, in
     order: prefetch of the next layer's weight, the GEMM (strict FP32), and a transaction
     whose callback runs bias + ReLU on the resident output, then waits only at the end.
     Activations are column-major features x batch (= row-major batch x features); weights
     are stored column-major out x in, so op(A) = N.  A step is one forward pass including
-    the input upload and the output download."""
+    the input upload and the output download.
+
+    Under torchrun (N > 1) each layer is split by output features (xvram_b200.mlp.
+    ShardedMLP): rank r streams rows [r F/N, (r + 1) F/N) of every weight from its host
+    memory, and the activation row blocks are all-gathered over NVLink between layers;
+    strong scaling (the same 24-layer forward on N GPUs), time = max over ranks."""
+    import datetime
+
     import numpy as np
     import torch
+    import torch.distributed as dist
 
     from xvram_b200 import sdk
-    from xvram_b200.mlp import StreamedMLP
+    from xvram_b200 import shard
+    from xvram_b200.mlp import ShardedMLP, StreamedMLP
 
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=datetime.timedelta(seconds=300))
     F, BATCH, LAYERS = args.mlp_features, args.mlp_batch, args.mlp_layers
+    if F % world:
+        raise SystemExit("features must divide evenly over the GPUs")
+    Fr = F // world
+    rows = slice(rank * Fr, (rank + 1) * Fr)
     budget = int(args.mlp_budget_gib * (1 << 30))
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     stream = torch.cuda.Stream(device=dev)
     peak_tflops, probes = measure_fp32_peak(dev, stream)
-    h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
-    wbytes = F * F * 4
+    h2d_gbs, d2h_gbs = measure_link(dev, stream, barrier)
+    h2d_gbs, d2h_gbs = -max_over_ranks(-h2d_gbs), -max_over_ranks(-d2h_gbs)
+    wbytes = Fr * F * 4
     abytes = F * BATCH * 4
 
     def weight(i):  # column-major out x in, N(0, 1/F), regenerated on demand for the check
@@ -451,14 +483,22 @@ def run_mlp(args) -> None:
     bias_all = ((torch.rand((LAYERS, F), generator=g, device=dev) * 2 - 1) / np.sqrt(F))
     x = (torch.rand((BATCH, F), generator=g, device=dev) * 2 - 1)
 
-    s = sdk.Sdk(sdk.session_config(cache_target_bytes=budget))
-    net = StreamedMLP(s, F, BATCH, LAYERS)
-    stage = torch.empty(F * F, dtype=torch.float32).pin_memory()
+    # the sharded layers' exchange uses an F x B staging workspace in each transaction
+    s = sdk.Sdk(sdk.session_config(device_ordinal=local, cache_target_bytes=budget,
+                                   workspace_cap_bytes=max(4 << 20, abytes)))
+    group = None
+    if world > 1:
+        group = shard.ShardGroup(shard.exchange_unique_id(rank), rank, world)
+        net = ShardedMLP(s, group, F, BATCH, LAYERS)
+    else:
+        net = StreamedMLP(s, F, BATCH, LAYERS)
+    stage = torch.empty(Fr * F, dtype=torch.float32).pin_memory()
     for i in range(LAYERS):
-        stage.copy_(weight(i).reshape(-1))
+        # weight(i) is [in][out]: this rank's out-rows are its columns -> [in][Fr] block
+        stage.copy_(weight(i)[:, rows].contiguous().reshape(-1))
         net.load_weight(i, stage)
     del stage
-    net.load_biases(bias_all.cpu().contiguous().pin_memory())
+    net.load_biases(bias_all[:, rows].cpu().contiguous().pin_memory())
     x_h = x.cpu().contiguous().pin_memory()
     out_h = torch.empty_like(x_h).pin_memory()
 
@@ -467,13 +507,15 @@ def run_mlp(args) -> None:
 
     for _ in range(args.warmup):
         forward()
+    barrier()
     times = []
     t0 = s.telemetry()
-    with ClockSampler(0) as clocks:
+    with ClockSampler(local) as clocks:
         for _ in range(args.steps):
+            barrier()
             start = time.perf_counter()
             forward()
-            times.append(time.perf_counter() - start)
+            times.append(max_over_ranks(time.perf_counter() - start))
     t1 = s.telemetry()
     assert net.statuses and all(st == 0 for st in net.statuses)
 
@@ -483,32 +525,47 @@ def run_mlp(args) -> None:
     for i in range(LAYERS):
         ref = torch.relu(ref @ weight(i).double() + bias_all[i].double())
     got = out_h[cols].to(dev).double()
-    err = float((got - ref).abs().max())
+    err = max_over_ranks(float((got - ref).abs().max()))
     scale = float(ref.abs().max())
 
     sec = statistics.median(times)
     flop = LAYERS * 2.0 * F * F * BATCH
     h2d_moved = (t1.bytes_h2d - t0.bytes_h2d) / args.steps
-    alg_h2d = LAYERS * wbytes + abytes + LAYERS * F * 4   # weights, input, biases, once each
+    # per rank: its weight rows, input, bias slices, once each
+    alg_h2d = LAYERS * wbytes + abytes + LAYERS * Fr * 4
     alg_d2h = abytes
-    t_roof = max(flop / (peak_tflops * 1e12), alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
+    t_roof = max(flop / world / (peak_tflops * 1e12), alg_h2d / (h2d_gbs * 1e9),
+                 alg_d2h / (d2h_gbs * 1e9))
     net.close()
     tel = s.telemetry()
     s.close()
+    if group is not None:
+        group.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     line = {
         "metric": METRIC,
         "workload": f"C5: {LAYERS} x Linear({F}->{F}, bias) + ReLU, batch {BATCH}, "
-                    f"device budget {args.mlp_budget_gib} GiB, through the SDK (xvram_get_api)",
-        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+                    f"device budget {args.mlp_budget_gib} GiB per GPU, through the SDK "
+                    f"(xvram_get_api)" + (f"; layers split by output features over {world} "
+                                          "GPUs, activations all-gathered over NVLink"
+                                          if world > 1 else ""),
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * sec, "higher_is_better": True,
-        "dtype": "f32", "data": "synthetic (seeded torch generators on the GPU)",
+        "scaling": "strong", "dtype": "f32",
+        "data": "synthetic (seeded torch generators on the GPU)",
         "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
-                     "bound": "host-link" if alg_h2d / (h2d_gbs * 1e9) > flop / (peak_tflops * 1e12)
-                     else "fp32",
+                     "bound": "host-link" if alg_h2d / (h2d_gbs * 1e9) >
+                     flop / world / (peak_tflops * 1e12) else "fp32",
                      "p_fp32_tflops": peak_tflops, "fp32_probes": probes, "h2d_gbs": h2d_gbs,
-                     "d2h_gbs": d2h_gbs},
-        "host_link": {"h2d_bytes_per_step": h2d_moved, "algorithmic_h2d_bytes": alg_h2d,
-                      "achieved_h2d_gbs": h2d_moved / sec / 1e9},
+                     "d2h_gbs": d2h_gbs, "per": "rank"},
+        "host_link": {"h2d_bytes_per_step_rank0": h2d_moved,
+                      "algorithmic_h2d_bytes_per_rank": alg_h2d,
+                      "achieved_h2d_gbs_rank0": h2d_moved / sec / 1e9,
+                      "concurrent_ranks": world},
         "check": {"sampled_batch_rows": cols, "max_abs_err_vs_fp64": err,
                   "max_abs_ref": scale},
         "residency": {"cache_target_bytes": int(tel.cache_target_bytes),
