@@ -128,22 +128,26 @@ def run_reference_arm(args) -> None:
 
 
 # ----------------------------------------------------------------------------- clocks
+INTERVAL_MS = 50
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons while the timed region runs.
 
-    The sampler is live before the region starts: entering waits (up to 10 s) for
-    nvidia-smi's first line, and leaving waits (up to 2 s) for one line after the region,
-    so even a region shorter than the 50 ms sampling interval is bracketed by samples.
-    `summary` uses the samples taken inside the region, or the two that bracket it when
-    the region fell between samples."""
+    The sampler is live and settled before the region starts: entering waits (up to 10 s)
+    for nvidia-smi's second line (its start-up, which takes driver locks, is over by
+    then), and leaving waits (up to 2 s) for one line after the region, so even a region
+    shorter than the sampling interval is bracketed by samples.  `summary` uses the
+    samples taken inside the region, or the two that bracket it when the region fell
+    between samples.  Long workloads that map and unmap device memory throughout (the
+    out-of-core and MLP runs) sample every 200 ms rather than every 50 ms."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    INTERVAL_MS = 50
-
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_ms: int = INTERVAL_MS):
         self.gpu = gpu_index
+        self.interval_ms = interval_ms
         self.proc = None
         self.samples: list[tuple[float, str]] = []
         self.t_begin = self.t_end = 0.0
@@ -152,12 +156,13 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
             deadline = time.monotonic() + 10.0
-            while not self.samples and time.monotonic() < deadline and self.proc.poll() is None:
+            while (len(self.samples) < 2 and time.monotonic() < deadline and
+                   self.proc.poll() is None):
                 time.sleep(0.01)
         except OSError:
             self.proc = None
@@ -213,7 +218,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm), "sampled": how,
                 "region_ms": round(1e3 * (self.t_end - self.t_begin), 1),
-                "interval_ms": self.INTERVAL_MS}
+                "interval_ms": self.interval_ms}
 
 
 # ---------------------------------------------------------------- out-of-core workload
@@ -254,7 +259,7 @@ def run_out_of_core(args) -> None:
     h = api.blas_create()
     flop = 2.0 * n ** 3
     times, moved = [], []
-    with ClockSampler(0) as clocks:
+    with ClockSampler(0, 200) as clocks:
         for _ in range(max(args.steps, 1)):
             t0 = api.telemetry().runtime
             b0 = (t0.bytes_h2d, t0.bytes_d2h)
@@ -365,7 +370,7 @@ def run_sharded_c4(args) -> None:
     for _ in range(args.warmup):
         step()
     times = []
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, 200) as clocks:
         for _ in range(args.steps):
             barrier()
             t0 = time.perf_counter()
@@ -510,7 +515,7 @@ def run_mlp(args) -> None:
     barrier()
     times = []
     t0 = s.telemetry()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, 200) as clocks:
         for _ in range(args.steps):
             barrier()
             start = time.perf_counter()
