@@ -62,6 +62,13 @@ def test_explicit_workspace_and_beta_zero(oracle):
     assert run(oracle, 0, 1, 700, 600, 900, -1.25, 0.0, seed=11, explicit_ws=True) <= TOLERANCE
 
 
+@pytest.mark.parametrize("op_a,op_b", [(1, 0), (0, 1)])
+def test_three_k_chunks(oracle, op_a, op_b):
+    """K = 5000 is three chunks of the tensor-core accumulation (three launches, each
+    updating C in FP32 after the previous one)."""
+    assert run(oracle, op_a, op_b, 1000, 777, 5000, 0.5, 1.5, seed=19) <= TOLERANCE
+
+
 def test_long_k_accuracy(oracle):
     """K = 8192: the dropped lo*lo term and TF32 rounding of lo stay far below tolerance."""
     err = run(oracle, 1, 0, 256, 256, 8192, 1.0, 0.0, seed=13)
