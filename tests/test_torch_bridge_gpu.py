@@ -84,3 +84,82 @@ def test_host_tensors_run_out_of_core():
         assert tel.handle_reuses > 0
     finally:
         tb.set_host_budget(0)
+
+
+HALF_ROUND = {torch.float16: 2.0 ** -11, torch.bfloat16: 2.0 ** -8}
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(257, 130, 99), (64, 64, 64), (3, 500, 7)])
+def test_mm_cuda_half_types(dtype, shape):
+    """FP16 / BF16 matrices: strict FP32 arithmetic on the exactly widened values, the
+    result rounded to the type once -- bit-identical to the FP32 kernel on the widened
+    operands followed by one rounding, in every layout."""
+    m, k, n = shape
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = (torch.rand((m, k), generator=g, device="cuda") * 2 - 1).to(dtype)
+    B = (torch.rand((k, n), generator=g, device="cuda") * 2 - 1).to(dtype)
+    want = tb.mm(A.float(), B.float()).to(dtype)
+    ref = A.double().cpu() @ B.double().cpu()
+    bound = TOL * k * float(A.abs().max()) * float(B.abs().max())
+    for a in views(A):
+        for b in views(B):
+            got = tb.mm(a, b)
+            assert got.dtype == dtype and got.shape == (m, n) and got.is_contiguous()
+            assert torch.equal(got, want)
+            d = (got.double().cpu() - ref).abs()
+            assert bool((d <= bound + HALF_ROUND[dtype] * ref.abs()).all())
+
+
+@pytest.mark.parametrize("shape", [(257, 130, 99), (200, 64, 300), (3, 500, 7)])
+def test_mm_cuda_float64(shape):
+    m, k, n = shape
+    g = torch.Generator(device="cuda").manual_seed(8)
+    A = torch.rand((m, k), generator=g, device="cuda", dtype=torch.float64) * 2 - 1
+    B = torch.rand((k, n), generator=g, device="cuda", dtype=torch.float64) * 2 - 1
+    ref = (A.cpu() @ B.cpu())
+    for a in views(A):
+        for b in views(B):
+            got = tb.mm(a, b)
+            assert got.dtype == torch.float64
+            assert err(got, A, B, ref) <= 1e-13
+
+
+def test_typed_options_refused():
+    x = torch.ones((8, 8), device="cuda", dtype=torch.float16)
+    with pytest.raises(TypeError):
+        tb.mm(x, x, tensor_cores=True)
+    with pytest.raises(TypeError):
+        tb.linear(x, x, torch.ones(8, device="cuda", dtype=torch.float16))
+    with pytest.raises(TypeError):
+        tb.mm(x, x.float())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float64])
+def test_host_tensors_out_of_core_typed(dtype):
+    """FP16 and FP64 host operands stream through a 16 MiB budget (several panels)."""
+    tb.set_host_budget(16 << 20)
+    try:
+        g = torch.Generator().manual_seed(9)
+        A = (torch.rand((1500, 1300), generator=g, dtype=torch.float64) * 2 - 1).to(dtype)
+        B = (torch.rand((1300, 1100), generator=g, dtype=torch.float64) * 2 - 1).to(dtype)
+        got = tb.mm(A, B)
+        assert got.device.type == "cpu" and got.dtype == dtype
+        ref = A.double() @ B.double()
+        k = A.shape[1]
+        if dtype == torch.float64:
+            assert err(got, A, B, ref) <= 1e-13
+        else:  # panels of K accumulate in an FP32 slot; one rounding to FP16 at the end
+            bound = TOL * k * float(A.abs().max()) * float(B.abs().max())
+            assert bool(((got.double() - ref).abs() <= bound + 2.0 ** -11 * ref.abs()).all())
+        w = (torch.randn((700, 1300), generator=g, dtype=torch.float64) / 40).to(dtype)
+        y = tb.linear(A, w)
+        assert y.dtype == dtype
+        ref = A.double() @ w.double().t()
+        bound = TOL * k * float(A.abs().max()) * float(w.abs().max())
+        if dtype == torch.float64:
+            assert float((y.double() - ref).abs().max()) <= 1e-7 * bound
+        else:
+            assert bool(((y.double() - ref).abs() <= bound + 2.0 ** -11 * ref.abs()).all())
+    finally:
+        tb.set_host_budget(0)

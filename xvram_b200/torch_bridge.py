@@ -1,11 +1,12 @@
-"""PyTorch tiled-GEMM bridge: `mm` and `linear` on this library's FP32 kernels.
+"""PyTorch tiled-GEMM bridge: `mm` and `linear` on this library's kernels.
 
 The reference routes bias-free `mm` / `linear` of torch graphs whose working set exceeds
 the device budget through its native tiled GEMM (reference
 python/xvram/torch_native.py:1876-1935, `_submit_tiled_gemm` / `_make_gemm_problem`).
 This bridge serves the same two operations, B200-side:
 
-* CUDA tensors run in HBM through `xvram_b200_sgemm_device` on torch's current stream.
+* CUDA tensors run in HBM through `xvram_b200_sgemm_device` (float32) or
+  `xvram_b200_gemm_device_typed` (the other types) on torch's current stream.
   Row-major (C-contiguous) and column-major (transposed) views are passed as the matching
   column-major operand and operation, so no copy is made for either.
 * Host tensors run out of core through an SDK session (`xvram_get_api`): the operands
@@ -15,9 +16,13 @@ This bridge serves the same two operations, B200-side:
   torch_native.py:1913-1921); on the GPU they are one pass of `xvram_b200_bias_activation`
   over the output.
 
-`tensor_cores=True` selects the three-term TF32 kernel (FP32-accurate within
-max|err| / (K max|a| max|b|) <= 1e-6); the default is strict FP32 FFMA.  FP32 only; there
-is no CPU fallback: without a GPU every call raises.
+Element types are the reference route's (python/xvram/torch_native.py:95-100): float32,
+and float16 / bfloat16 / float64 matrices of one type, with the result in that type --
+FP16 / BF16 under strict FP32 arithmetic (the products are exact in FP32, the result is
+rounded to the type once), FP64 in FP64.  `tensor_cores=True` selects the three-term TF32
+kernel for float32 (FP32-accurate within max|err| / (K max|a| max|b|) <= 1e-6); the
+default is strict FP32 FFMA.  Bias and ReLU are float32 only (the reference route takes
+neither).  There is no CPU fallback: without a GPU every call raises.
 """
 from __future__ import annotations
 
@@ -30,6 +35,15 @@ from . import device as xd
 from . import sdk
 
 _TF32X3 = 3
+_TYPES = {torch.float16: sdk.FP16, torch.bfloat16: sdk.BF16, torch.float32: sdk.FP32,
+          torch.float64: sdk.FP64}
+
+
+def _dtype_of(a: torch.Tensor, b: torch.Tensor) -> torch.dtype:
+    if a.dtype != b.dtype or a.dtype not in _TYPES:
+        raise TypeError("mm supports float16, bfloat16, float32 and float64 matrices of one "
+                        f"type (got {a.dtype} and {b.dtype})")
+    return a.dtype
 
 
 def _colmajor(x: torch.Tensor):
@@ -54,9 +68,11 @@ def _check(st: int, what: str) -> None:
 
 def mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
        tensor_cores: bool = False) -> torch.Tensor:
-    """a @ b for FP32 matrices (m x k) @ (k x n), on the device the tensors are on."""
-    if a.dtype != torch.float32 or b.dtype != torch.float32:
-        raise TypeError("mm supports float32 only")
+    """a @ b for (m x k) @ (k x n) matrices of one floating type, on the device the
+    tensors are on; the result has that type."""
+    dtype = _dtype_of(a, b)
+    if tensor_cores and dtype != torch.float32:
+        raise TypeError("tensor_cores applies to float32 matrices")
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
         raise ValueError(f"shapes {tuple(a.shape)} and {tuple(b.shape)} do not multiply")
     if a.device != b.device:
@@ -66,9 +82,9 @@ def mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
     m, k = a.shape
     n = b.shape[1]
     if out is None:
-        out = torch.empty((m, n), dtype=torch.float32, device=a.device)
-    elif out.shape != (m, n) or not out.is_contiguous() or out.dtype != torch.float32:
-        raise ValueError("out must be a contiguous float32 (m, n) tensor")
+        out = torch.empty((m, n), dtype=dtype, device=a.device)
+    elif out.shape != (m, n) or not out.is_contiguous() or out.dtype != dtype:
+        raise ValueError(f"out must be a contiguous {dtype} (m, n) tensor")
     if m == 0 or n == 0:
         return out
     if k == 0:
@@ -77,15 +93,21 @@ def mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
     bs, ldb, ob = _colmajor(b)       # b as op_b(S_b): b = S_b^T when ob == 1
     as_, lda, oa = _colmajor(a)
     # C^T = b^T a^T: the first operand is b^T = op(S_b) with the operation flipped, etc.
-    st = xd.sgemm(1 - ob, 1 - oa, n, m, k, 1.0, bs, ldb, as_, lda, 0.0, out, n,
-                  path=_TF32X3 if tensor_cores else 0)
-    _check(st, "xvram_b200_sgemm_device")
+    if dtype == torch.float32:
+        st = xd.sgemm(1 - ob, 1 - oa, n, m, k, 1.0, bs, ldb, as_, lda, 0.0, out, n,
+                      path=_TF32X3 if tensor_cores else 0)
+        _check(st, "xvram_b200_sgemm_device")
+    else:
+        st = xd.gemm_typed(1 - ob, 1 - oa, n, m, k, 1.0, bs, ldb, as_, lda, 0.0, out, n)
+        _check(st, "xvram_b200_gemm_device_typed")
     return out
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            relu: bool = False, tensor_cores: bool = False) -> torch.Tensor:
     """x @ weight^T (+ bias) (then ReLU), x: (batch, in), weight: (out, in)."""
+    if (bias is not None or relu) and x.dtype != torch.float32:
+        raise TypeError("bias and ReLU apply to float32 matrices")
     if x.device.type != "cuda":
         return _host_session().linear(x, weight, bias, relu, tensor_cores)
     y = mm(x, weight.t(), tensor_cores=tensor_cores)
@@ -121,7 +143,7 @@ class HostGemm:
 
     def _upload(self, t: torch.Tensor):
         t = t.contiguous()
-        alloc = self.s.alloc(max(t.numel() * 4, 4))
+        alloc = self.s.alloc(max(t.numel() * t.element_size(), 4))
         if t.numel():
             alloc.write(t)
         return alloc
@@ -129,31 +151,35 @@ class HostGemm:
     def mm(self, a, b, out=None, tensor_cores=False, b_transposed=False, bias=None,
            relu=False):
         """Row-major a (m x k) @ b (k x n), or a @ b^T for b (n x k) when b_transposed."""
-        if a.dtype != torch.float32 or b.dtype != torch.float32:
-            raise TypeError("mm supports float32 only")
+        dtype = _dtype_of(a, b)
+        if (tensor_cores or bias is not None or relu) and dtype != torch.float32:
+            raise TypeError("tensor_cores, bias and ReLU apply to float32 matrices")
+        dt = _TYPES[dtype]
         m, k = a.shape
         n = b.shape[0] if b_transposed else b.shape[1]
         if (b.shape[1] if b_transposed else b.shape[0]) != k:
             raise ValueError(f"shapes {tuple(a.shape)} and {tuple(b.shape)} do not multiply")
         if out is None:
-            out = torch.empty((m, n), dtype=torch.float32)
+            out = torch.empty((m, n), dtype=dtype)
         if m == 0 or n == 0:
             return out
         if k == 0:
             raise ValueError("the out-of-core path needs k > 0 (no host-side arithmetic)")
         with self.lock:
             A, B = self._upload(a), self._upload(b)
-            C = self.s.alloc(max(m * n * 4, 4))
+            C = self.s.alloc(max(m * n * a.element_size(), 4))
             allocs = [A, B, C]
             try:
-                mode = sdk.COMPUTE_FP32_TF32 if tensor_cores else sdk.COMPUTE_FP32_STRICT
+                mode = (sdk.COMPUTE_FP64 if dt == sdk.FP64 else
+                        sdk.COMPUTE_FP32_TF32 if tensor_cores else sdk.COMPUTE_FP32_STRICT)
                 if b_transposed:  # b is (n x k) row-major; op(B) = T
-                    bdesc = sdk.matrix(B, n, k, k, sdk.ROW_MAJOR)
+                    bdesc = sdk.matrix(B, n, k, k, sdk.ROW_MAJOR, data_type=dt)
                 else:
-                    bdesc = sdk.matrix(B, k, n, n, sdk.ROW_MAJOR)
-                desc = self.s.gemm_desc(sdk.matrix(A, m, k, k, sdk.ROW_MAJOR), bdesc,
-                                        sdk.matrix(C, m, n, n, sdk.ROW_MAJOR), sdk.OP_N,
-                                        sdk.OP_T if b_transposed else sdk.OP_N, mode=mode)
+                    bdesc = sdk.matrix(B, k, n, n, sdk.ROW_MAJOR, data_type=dt)
+                desc = self.s.gemm_desc(sdk.matrix(A, m, k, k, sdk.ROW_MAJOR, data_type=dt),
+                                        bdesc, sdk.matrix(C, m, n, n, sdk.ROW_MAJOR, data_type=dt),
+                                        sdk.OP_N, sdk.OP_T if b_transposed else sdk.OP_N,
+                                        mode=mode)
                 plan = self.s.plan(desc)
                 try:
                     self.s.check("gemm_execute", self.s.t.gemm_execute(plan, sdk.TIMEOUT_INFINITE))
