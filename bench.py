@@ -823,24 +823,39 @@ def main_gpu(args) -> None:
     h = api.blas_create()
     da, db, dc = api.malloc(a_h.nbytes), api.malloc(b_h.nbytes), api.malloc(c_h.nbytes)
 
+    call_ms = {key: [] for key in ("h2d_a", "h2d_b", "h2d_c", "sgemm", "d2h_c")}
+
     def e2e_step():
+        t = [time.perf_counter()]
         api.h2d(da, a_h.data_ptr(), a_h.nbytes)
+        t.append(time.perf_counter())
         api.h2d(db, b_h.data_ptr(), b_h.nbytes)
+        t.append(time.perf_counter())
         api.h2d(dc, c_h.data_ptr(), c_h.nbytes)
+        t.append(time.perf_counter())
         api.check("sgemm", api.sgemm(h, OP_A, OP_B, M, N, K, ALPHA, da, K, db, K, BETA, dc, M))
+        t.append(time.perf_counter())
         api.d2h(c_out.data_ptr(), dc, c_out.nbytes)
+        t.append(time.perf_counter())
+        for i, key in enumerate(call_ms):
+            call_ms[key].append(1e3 * (t[i + 1] - t[i]))
 
     for _ in range(args.warmup):
         e2e_step()
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    e2e_marks = [t0]
     for _ in range(args.steps):
         e2e_step()
+        e2e_marks.append(time.perf_counter())
     torch.cuda.synchronize()
     e2e_s = (time.perf_counter() - t0) / args.steps
     barrier()
     e2e_s_max = max_over_ranks(e2e_s)
+    e2e_step_ms = sorted(1e3 * (b - a) for a, b in zip(e2e_marks[:-1], e2e_marks[1:]))
+    # per-call medians over the timed steps (the warm-up steps come first in each list)
+    e2e_call_ms = {key: statistics.median(v[-args.steps:]) for key, v in call_ms.items()}
     trace_records = None
     if args.trace and rank == 0:
         # one more step, outside the timed region, in the reference's trace format
@@ -868,8 +883,13 @@ def main_gpu(args) -> None:
     torch.cuda.synchronize()
     e2e_tc_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
     api.check("math", api.t.blas_set_math_mode(h, 0))
-    # one SGEMM kernel plus the two canonicalising transposes per in-place GEMM
-    launches_e2e = int(info.gemm_in_place) * (1 + int(OP_A == 1) + int(OP_B == 0))
+    tc_call_ms = {key: statistics.median(v[-args.steps:]) for key, v in call_ms.items()}
+    tc_step_ms = sorted(sum(v[-args.steps:][i] for v in call_ms.values())
+                        for i in range(args.steps))
+    # the canonicalising transposes per in-place GEMM, plus its kernel, or one kernel per C
+    # column block when the call returned before its kernels finished (the default)
+    launches_e2e = (int(info.gemm_in_place) * (int(OP_A == 1) + int(OP_B == 0)) +
+                    (int(info.gemm_column_blocks) or int(info.gemm_in_place)))
     for d in (da, db, dc):
         api.free(d)
     api.blas_destroy(h)
@@ -884,6 +904,9 @@ def main_gpu(args) -> None:
     t_roof = max(t_compute, h2d_bytes / (h2d * 1e9) + d2h_bytes / (d2h * 1e9))
     t_roof_overlap = max(t_compute, (h2d_bytes + d2h_bytes) / (h2d * 1e9))
     t_roof_sharded = max(t_compute, (sh_h2d + sh_d2h) / (h2d * 1e9))
+    # The floor the call sequence allows: cudaMemcpy returns only once its copy is done, so
+    # the three H2D copies precede the GEMM in series; C's D2H can overlap the kernel.
+    t_floor_api = h2d_bytes / (h2d * 1e9) + max(kernel_ms * 1e-3, d2h_bytes / (d2h * 1e9))
 
     traffic = None
     tfile = ROOT / "profiles" / "sgemm_ffma_c2_traffic.json"
@@ -920,6 +943,8 @@ def main_gpu(args) -> None:
                           "compat_e2e_roofline_ms_serial": 1e3 * t_roof,
                           "compat_e2e_roofline_ms": 1e3 * t_roof_overlap,
                           "compat_e2e_frac_of_roofline": t_roof_overlap / e2e_s_max,
+                          "compat_e2e_floor_ms_call_order": 1e3 * t_floor_api,
+                          "compat_e2e_frac_of_call_order_floor": t_floor_api / e2e_s_max,
                           "sharded_e2e_link_gbs": (sh_h2d + sh_d2h) / sharded_s / 1e9,
                           "sharded_e2e_roofline_ms": 1e3 * t_roof_sharded,
                           "sharded_e2e_frac_of_roofline": t_roof_sharded / sharded_s},
@@ -929,6 +954,12 @@ def main_gpu(args) -> None:
                  "ms_per_step": 1e3 * e2e_s_max,
                  "path": "xvram_cuda_compat_get_api: memcpy H2D x3, blas_sgemm, memcpy D2H",
                  "gemm_in_place": int(info.gemm_in_place),
+                 "step_ms": {"min": e2e_step_ms[0],
+                             "median": e2e_step_ms[len(e2e_step_ms) // 2],
+                             "max": e2e_step_ms[-1]},
+                 "call_ms_median": e2e_call_ms,
+                 "gemm_deferred": int(info.gemm_deferred),
+                 "gemm_column_blocks": int(info.gemm_column_blocks),
                  "gemm_streamed": int(info.gemm_streamed),
                  "runtime_h2d_bytes": int(tel.runtime.bytes_h2d)}
                 if world == 1 else
@@ -962,6 +993,10 @@ def main_gpu(args) -> None:
                                                        / tf32_cublas},
                 "e2e": {"value": FLOP / e2e_tc_s / 1e12, "unit": "TFLOP/s",
                         "ms_per_step": 1e3 * e2e_tc_s,
+                        "step_ms": {"min": tc_step_ms[0],
+                                    "median": tc_step_ms[len(tc_step_ms) // 2],
+                                    "max": tc_step_ms[-1]},
+                        "call_ms_median": tc_call_ms,
                         "path": "compat ABI, blas_set_math_mode(3)"},
                 "clocks": tc_clocks.summary(),
             },

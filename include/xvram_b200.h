@@ -309,6 +309,11 @@ typedef struct xvram_b200_runtime_info_v1 {
   uint64_t last_steps;
   uint64_t last_panel_slots;
   double last_gemm_ms;
+  /* blas_sgemm calls that returned before their kernels finished (the default; the
+     environment variable XVRAM_B200_SYNC_GEMM=1 waits for them), and the C column blocks
+     those kernels ran as. */
+  uint64_t gemm_deferred;
+  uint64_t gemm_column_blocks;
 } xvram_b200_runtime_info_v1;
 
 XVRAM_B200_API xvram_status XVRAM_CALL

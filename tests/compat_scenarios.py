@@ -256,6 +256,54 @@ def scenario_tensor_cores(oracle):
     return res
 
 
+def scenario_deferred(oracle):
+    """blas_sgemm returning before its kernels finish (the default): C split into column
+    blocks, each copied home after its own kernel.  Every operation with ldc > m, C read
+    whole and in pieces that cut through blocks; digests of C for comparison with a run
+    under XVRAM_B200_SYNC_GEMM=1, and sampled FP64 errors."""
+    import hashlib
+    api = cp.CompatApi()
+    init(api)
+    h = api.blas_create()
+    m, n, k = 8192, 4096, 256
+    ldc = m + 8
+    res = {"digests": {}, "errors": {}}
+    rng = np.random.default_rng(5)
+    rows, cols = rng.integers(0, m, 8192), rng.integers(0, n, 8192)
+    for op_a, op_b, math in [(x, y, z) for z in (0, 3) for x in (0, 1) for y in (0, 1)]:
+        api.check("math", api.t.blas_set_math_mode(h, math))
+        lda = m if op_a == 0 else k
+        ldb = k if op_b == 0 else n
+        a = oracle.uniform(lda * (k if op_a == 0 else m), 70 + op_a)
+        b = oracle.uniform(ldb * (n if op_b == 0 else k), 72 + op_b)
+        c = oracle.uniform(ldc * n, 74)
+        da, db, dc = upload(api, a), upload(api, b), upload(api, c)
+        api.check("sgemm", api.sgemm(h, op_a, op_b, m, n, k, 0.5, da, lda, db, ldb, 1.5, dc,
+                                     ldc))
+        out = np.empty_like(c)
+        if op_a == 1 and op_b == 0:
+            cuts = [0, 4 * (ldc * 333 + 5), 4 * (ldc * 2000 + 1), 4 * ldc * 3072, out.nbytes]
+            for lo, hi in zip(cuts[:-1], cuts[1:]):
+                api.d2h(ptr(out) + lo, dc + lo, hi - lo)
+        else:
+            api.d2h(ptr(out), dc, out.nbytes)
+        key = f"{op_a}{op_b}m{math}"
+        res["digests"][key] = hashlib.sha256(out.tobytes()).hexdigest()
+        ref = oracle.gemm_sampled(op_a, op_b, k, 0.5, a, lda, b, ldb, 1.5, c, ldc, rows, cols,
+                                  threads=16)
+        o = out.reshape(n, ldc)
+        res["errors"][key] = float(np.max(np.abs(o[cols, rows] - ref))) / k
+        res["pad_kept"] = res.get("pad_kept", True) and bool(
+            np.array_equal(o[:, m:], c.reshape(n, ldc)[:, m:]))
+        for d in (da, db, dc):
+            api.free(d)
+    info = cp.runtime_info()
+    res.update(deferred=info.gemm_deferred, blocks=info.gemm_column_blocks,
+               in_place=info.gemm_in_place)
+    res["shutdown"] = api.shutdown()
+    return res
+
+
 SCENARIOS = {name[len("scenario_"):]: fn for name, fn in globals().items()
              if name.startswith("scenario_")}
 

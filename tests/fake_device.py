@@ -29,6 +29,10 @@ def build() -> C.CDLL:
     lib.fake_device_set_memory.argtypes = [C.c_uint64, C.c_uint64]
     lib.fake_device_fail.argtypes = [C.c_char_p, C.c_long]
     lib.fake_device_set_workspace_fn.argtypes = [C.c_void_p]
+    lib.fake_device_set_sm_count.argtypes = [C.c_int]
+    lib.fake_device_set_kernel_word.argtypes = [C.c_uint32]
+    lib.fake_device_gemm_calls.restype = C.c_uint64
+    lib.fake_device_prepares.restype = C.c_uint64
     return lib
 
 
@@ -39,6 +43,8 @@ def installed(free_bytes: int = 8 << 30, total_bytes: int = 16 << 30):
     fake = build()
     fake.fake_device_set_memory(free_bytes, total_bytes)
     fake.fake_device_fail(b"", -1)
+    fake.fake_device_set_sm_count(148)
+    fake.fake_device_set_kernel_word(0)
     fake.fake_device_set_workspace_fn(C.cast(lib.xvram_b200_gemm_typed_workspace_bytes,
                                              C.c_void_p))
     factory = C.cast(fake.fake_device_create, C.c_void_p)

@@ -37,6 +37,9 @@ using WorkspaceFn = uint64_t (*)(uint32_t, uint32_t, int32_t, uint32_t, uint32_t
                                  int64_t, int64_t);
 std::atomic<WorkspaceFn> g_workspace_fn{nullptr};
 std::atomic<uint64_t> g_free{8ull << 30};
+std::atomic<int> g_sm_count{148};
+std::atomic<uint32_t> g_kernel_word{0};
+std::atomic<uint64_t> g_gemm_calls{0}, g_prepares{0};
 std::atomic<uint64_t> g_total{16ull << 30};
 std::mutex g_fail_mu;
 std::string g_fail_op;
@@ -135,7 +138,7 @@ public:
     info->device_count = 1;
     info->name = "fake host-memory device";
     info->total_bytes = g_total.load();
-    info->sm_count = 148;
+    info->sm_count = g_sm_count.load();
     info->vmm_granularity = kGranularity;
     info->driver_version = 0;
     info->cc_major = 10;
@@ -251,6 +254,7 @@ public:
     else // strict FP32 (the fake computes TF32 requests in strict FP32 too)
       contract<float>(t, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc);
     ++gemms;
+    ++g_gemm_calls;
     return {};
   }
   // Per output: one FMA chain in k order in T, then alpha * acc (+ beta * C as one FMA),
@@ -304,8 +308,41 @@ public:
     ++conversions;
     return {};
   }
+  // The fake keeps the operands where they are: preparing records them, and a block is the
+  // plain loop over C's columns [n0, n0 + nj) (op(B)'s columns n0.. are B's columns for
+  // op N, its rows for op T).
+  xvram::Error gemm_prepare(const xvram::GemmTypes& t, int op_a, int op_b, int64_t, int64_t,
+                            int64_t, uint64_t a, int64_t lda, uint64_t b, int64_t ldb, uint64_t,
+                            uint64_t, xvram::StreamId, xvram::PreparedGemm* out) override {
+    if (should_fail("sgemm"))
+      return injected("sgemm");
+    *out = xvram::PreparedGemm{};
+    out->compute = t.compute;
+    out->op_a = op_a;
+    out->op_b = op_b;
+    out->a = a;
+    out->b = b;
+    out->lda = lda;
+    out->ldb = ldb;
+    ++g_prepares;
+    return {};
+  }
+  xvram::Error gemm_block(const xvram::PreparedGemm& p, int64_t m, int64_t n0, int64_t nj,
+                          int64_t k, double alpha, double beta, uint64_t c, int64_t ldc,
+                          xvram::StreamId) override {
+    if (should_fail("sgemm"))
+      return injected("sgemm");
+    const xvram::GemmTypes t{xvram::kFp32, xvram::kFp32, p.compute};
+    const uint64_t b = p.b + static_cast<uint64_t>(p.op_b == 0 ? n0 * p.ldb : n0) * 4;
+    contract<float>(t, p.op_a, p.op_b, m, nj, k, alpha, p.a, p.lda, b, p.ldb, beta, c, ldc);
+    ++gemms;
+    ++g_gemm_calls;
+    return {};
+  }
+  // The kernels' sticky error word: a test may set it to stand for a kernel whose bounded
+  // wait ran out; reading clears it, as on the device.
   xvram::Error kernel_status(xvram::StreamId, uint32_t* word) override {
-    *word = 0;
+    *word = g_kernel_word.exchange(0);
     return {};
   }
   uint64_t native_stream(xvram::StreamId) override { return 0; }
@@ -330,6 +367,18 @@ __attribute__((visibility("default"))) void fake_device_set_memory(uint64_t free
 __attribute__((visibility("default"))) void fake_device_set_workspace_fn(void* fn) {
   g_workspace_fn.store(reinterpret_cast<WorkspaceFn>(fn));
 }
+
+// SM count reported by open() (the runtime sizes GEMM column blocks by it).
+__attribute__((visibility("default"))) void fake_device_set_sm_count(int n) { g_sm_count.store(n); }
+
+// The error word the next kernel_status returns.
+__attribute__((visibility("default"))) void fake_device_set_kernel_word(uint32_t w) {
+  g_kernel_word.store(w);
+}
+
+// GEMM launches (whole GEMMs and column blocks) and column-block preparations since load.
+__attribute__((visibility("default"))) uint64_t fake_device_gemm_calls() { return g_gemm_calls.load(); }
+__attribute__((visibility("default"))) uint64_t fake_device_prepares() { return g_prepares.load(); }
 
 // The (after + 1)-th call of `op` ("copy_2d", "map", "handle_create", "sgemm") fails with
 // an injected CUDA error; after < 0 clears the injection.

@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -13,9 +14,9 @@ HERE = Path(__file__).resolve().parent
 S = {"SUCCESS": 0, "INVALID_ARGUMENT": 1, "UNSUPPORTED": 3, "NOT_READY": 9, "CLOSED": 17}
 
 
-def run(name: str, timeout: int = 600) -> dict:
+def run(name: str, timeout: int = 600, env: dict | None = None) -> dict:
     p = subprocess.run([sys.executable, str(HERE / "compat_scenarios.py"), name],
-                       capture_output=True, text=True, timeout=timeout)
+                       capture_output=True, text=True, timeout=timeout, env=env)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-4000:]
     return json.loads(p.stdout.strip().splitlines()[-1])
 
@@ -74,3 +75,20 @@ def test_tensor_core_math_mode_in_place_and_streamed():
     assert r["ok"], r
     assert r["in_place_calls"] == 1 and r["streamed_calls"] == 1
     assert r["shutdown"] == 0
+
+
+def test_deferred_column_blocks_bit_identical_to_synchronous():
+    """The default blas_sgemm returns before its kernels finish and runs C as column
+    blocks; its results equal the reference's synchronous completion
+    (XVRAM_B200_SYNC_GEMM=1) bit for bit, for every operation in strict FP32 and in TF32
+    tensor-op math, with ldc > m and reads of C that cut through blocks."""
+    env = {k: v for k, v in os.environ.items() if k != "XVRAM_B200_SYNC_GEMM"}
+    d = run("deferred", env=env)
+    s = run("deferred", env=dict(env, XVRAM_B200_SYNC_GEMM="1"))
+    # strict: 64 x 16 tiles of 128 x 256 on 148 SMs; TF32: 32 x 16 tiles of 256 x 256 on
+    # 74 SM pairs; 6 blocks of 768 columns (the last 256) either way
+    assert d["in_place"] == 8 and d["deferred"] == 8 and d["blocks"] == 8 * 6
+    assert s["deferred"] == 0 and s["blocks"] == 0
+    assert d["digests"] == s["digests"]
+    assert max(d["errors"].values()) <= 1e-6 and d["pad_kept"]
+    assert d["shutdown"] == 0 and s["shutdown"] == 0

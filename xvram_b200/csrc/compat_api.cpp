@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -123,6 +124,10 @@ public:
                                "only one initialization attempt is permitted"));
     attempted_ = true;
     config_ = *config;
+    {
+      const char* v = std::getenv("XVRAM_B200_SYNC_GEMM");
+      sync_gemm_ = v && v[0] == '1';
+    }
     set_state(XVRAM_CUDA_COMPAT_INITIALIZING);
     count_submitted();
     RuntimeConfig rc;
@@ -482,6 +487,10 @@ public:
       call.beta = beta_v;
       if (s.compute == kTf32)
         call.flops_per_s = 150e12; // plan for the tensor-core rate
+      // cuBLAS semantics: the call returns once the kernels are queued and the next
+      // cudaMemcpy of C (or cudaDeviceSynchronize) waits for them and reports a failed
+      // kernel.  XVRAM_B200_SYNC_GEMM=1 keeps the reference's synchronous completion.
+      call.defer_completion = !sync_gemm_;
       if (Error e = runtime_->gemm(call))
         return e;
       std::lock_guard lock(snap_mu_);
@@ -570,6 +579,8 @@ private:
     info_.last_steps = static_cast<uint64_t>(x.last_steps);
     info_.last_panel_slots = static_cast<uint64_t>(x.last_panel_slots);
     info_.last_gemm_ms = x.last_gemm_ms;
+    info_.gemm_deferred = x.gemm_deferred;
+    info_.gemm_column_blocks = x.gemm_column_blocks;
   }
 
   template <class F> xvram_status run(const char* op, F&& fn) {
@@ -652,6 +663,7 @@ private:
   Error error_;
   xvram_cuda_compat_config_v1 config_{};
   bool attempted_ = false;
+  bool sync_gemm_ = false; // blas_sgemm waits for its kernels (XVRAM_B200_SYNC_GEMM=1)
   std::unique_ptr<Runtime> runtime_;
   std::map<uint64_t, Entry> allocs_;
   std::vector<std::unique_ptr<Handle>> handles_;

@@ -321,6 +321,67 @@ public:
     return {};
   }
 
+  Error gemm_prepare(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n, int64_t k,
+                     uint64_t a, int64_t lda, uint64_t b, int64_t ldb, uint64_t workspace,
+                     uint64_t workspace_bytes, StreamId s, PreparedGemm* out) override {
+    if (t.ab != kFp32 || t.c != kFp32 || (t.compute != kStrictFp32 && t.compute != kTf32))
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "gemm_prepare", "FP32 GEMMs only");
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "gemm_prepare", "tile exceeds int32");
+    SgemmPrepared p;
+    XV_RT("sgemm_prepare",
+          sgemm_prepare(t.compute == kTf32, op_a, op_b, static_cast<int>(m), static_cast<int>(n),
+                        static_cast<int>(k), reinterpret_cast<const float*>(a), lda,
+                        reinterpret_cast<const float*>(b), ldb, reinterpret_cast<void*>(workspace),
+                        workspace_bytes, stream(s), &p));
+    *out = PreparedGemm{};
+    out->compute = t.compute;
+    if (p.tf32) {
+      out->a = reinterpret_cast<uint64_t>(p.a_hi);
+      out->a2 = reinterpret_cast<uint64_t>(p.a_lo);
+      out->b = reinterpret_cast<uint64_t>(p.b_hi);
+      out->b2 = reinterpret_cast<uint64_t>(p.b_lo);
+      out->lda = out->ldb = p.kp;
+    } else {
+      out->a = reinterpret_cast<uint64_t>(p.a);
+      out->b = reinterpret_cast<uint64_t>(p.b);
+      out->lda = p.lda;
+      out->ldb = p.ldb;
+      out->op_a = p.op_a;
+      out->op_b = p.op_b;
+    }
+    return {};
+  }
+
+  Error gemm_block(const PreparedGemm& q, int64_t m, int64_t n0, int64_t nj, int64_t k,
+                   double alpha, double beta, uint64_t c, int64_t ldc, StreamId s) override {
+    if (m > INT32_MAX || n0 + nj > INT32_MAX || k > INT32_MAX)
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "gemm_block", "tile exceeds int32");
+    SgemmPrepared p;
+    p.tf32 = q.compute == kTf32;
+    if (p.tf32) {
+      p.a_hi = reinterpret_cast<const float*>(q.a);
+      p.a_lo = reinterpret_cast<const float*>(q.a2);
+      p.b_hi = reinterpret_cast<const float*>(q.b);
+      p.b_lo = reinterpret_cast<const float*>(q.b2);
+      p.kp = q.lda;
+    } else {
+      p.a = reinterpret_cast<const float*>(q.a);
+      p.b = reinterpret_cast<const float*>(q.b);
+      p.lda = q.lda;
+      p.ldb = q.ldb;
+      p.op_a = q.op_a;
+      p.op_b = q.op_b;
+    }
+    const cudaError_t e = sgemm_block(p, static_cast<int>(m), static_cast<int>(n0),
+                                      static_cast<int>(nj), static_cast<int>(k),
+                                      static_cast<float>(alpha), static_cast<float>(beta),
+                                      reinterpret_cast<float*>(c), ldc, stream(s));
+    if (e != cudaSuccess)
+      return rt_error(p.tf32 ? "sgemm_tf32x3 launch" : "sgemm_ffma launch", e);
+    return {};
+  }
+
   Error kernel_status(StreamId s, uint32_t* word) override {
     unsigned int w = 0, wt = 0;
     XV_RT("read_kernel_error", read_and_clear_kernel_error(&w, stream(s)));

@@ -33,6 +33,16 @@ using EventId = uint64_t;
 
 enum class CopyDir { h2d, d2h, d2d };
 
+// The operands of one GEMM after gemm_prepare: addresses, leading dimensions and
+// operations as the device's kernel reads them (a2 / b2: second terms, e.g. the low parts
+// of a split).  Device-defined; the runtime only passes it back to gemm_block.
+struct PreparedGemm {
+  uint32_t compute = 0;
+  int op_a = 0, op_b = 0;
+  uint64_t a = 0, b = 0, a2 = 0, b2 = 0;
+  int64_t lda = 0, ldb = 0;
+};
+
 // Element types and arithmetic of one device GEMM (validate.hpp's DataType / ComputeKind).
 struct GemmTypes {
   uint32_t ab = kFp32; // A and B
@@ -91,6 +101,17 @@ public:
   // (round to nearest even when narrowing).
   virtual Error convert(uint32_t src_type, uint64_t src, int64_t lds, uint32_t dst_type,
                         uint64_t dst, int64_t ldd, int64_t rows, int64_t cols, StreamId s) = 0;
+  // An FP32 GEMM (strict or three-term TF32) in two parts, for launching C's column blocks
+  // separately: gemm_prepare brings op(A) and op(B) into the workspace in the form the
+  // kernel reads; gemm_block computes C's columns [n0, n0 + nj) (c = the address of column
+  // n0) from them.  For n0 on a multiple of 256, every output equals that of one gemm call
+  // over all of C.  The workspace must stay untouched until the last block has run.
+  virtual Error gemm_prepare(const GemmTypes& t, int op_a, int op_b, int64_t m, int64_t n,
+                             int64_t k, uint64_t a, int64_t lda, uint64_t b, int64_t ldb,
+                             uint64_t workspace, uint64_t workspace_bytes, StreamId s,
+                             PreparedGemm* out) = 0;
+  virtual Error gemm_block(const PreparedGemm& p, int64_t m, int64_t n0, int64_t nj, int64_t k,
+                           double alpha, double beta, uint64_t c, int64_t ldc, StreamId s) = 0;
   // Reads and clears the sticky error word of the library's kernels (synchronising s).
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
   // The native handle of stream s (a cudaStream_t) handed to transaction callbacks.

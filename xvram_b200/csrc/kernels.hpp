@@ -32,6 +32,33 @@ cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, 
 bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
                         long long ldb);
 
+// One FP32 GEMM in two parts, so C's column blocks can be launched separately (and on
+// different streams) after a single preparation of the operands:
+//   sgemm_prepare  brings op(A) and op(B) into the form the kernel reads (the FFMA path's
+//                  transposes into the workspace, the TF32 path's hi/lo splits);
+//   sgemm_block    computes C's columns [n0, n0 + nj) from the prepared operands; c points
+//                  at column n0.
+// Each output is computed exactly as by one sgemm_ffma_ws / sgemm_tf32x3 call over all of
+// C, provided n0 is a multiple of 256 (whole tile columns): block results are
+// bit-identical to the unsplit call.  The prepared operands live in the workspace, so it
+// must not be reused until every block has run.
+struct SgemmPrepared {
+  bool tf32 = false;
+  // FFMA: the operands as the kernel reads them (canonical op N / op T when transposed)
+  const float* a = nullptr;
+  const float* b = nullptr;
+  long long lda = 0, ldb = 0;
+  int op_a = 0, op_b = 0;
+  // TF32: K-major hi/lo parts, leading dimension kp
+  const float *a_hi = nullptr, *a_lo = nullptr, *b_hi = nullptr, *b_lo = nullptr;
+  long long kp = 0;
+};
+cudaError_t sgemm_prepare(bool tf32, int op_a, int op_b, int m, int n, int k, const float* a,
+                          long long lda, const float* b, long long ldb, void* workspace,
+                          uint64_t workspace_bytes, cudaStream_t stream, SgemmPrepared* out);
+cudaError_t sgemm_block(const SgemmPrepared& p, int m, int n0, int nj, int k, float alpha,
+                        float beta, float* c, long long ldc, cudaStream_t stream);
+
 // dst (cols x rows, column-major, ldd) = src^T (src: rows x cols, column-major, lds), on
 // `stream`.  Moves values only; used to bring K-major operands into the M/N-major form
 // the kernel reads fastest.
@@ -46,6 +73,14 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
                          long long lda, const float* b, long long ldb, float beta, float* c,
                          long long ldc, void* workspace, uint64_t workspace_bytes,
                          cudaStream_t stream);
+// The TF32 halves of sgemm_prepare / sgemm_block: the hi/lo splits into the workspace, and
+// the kernel's K chunks over C's columns [n0, n0 + nj).
+cudaError_t sgemm_tf32x3_prepare(int op_a, int op_b, int m, int n, int k, const float* a,
+                                 long long lda, const float* b, long long ldb, void* workspace,
+                                 uint64_t workspace_bytes, cudaStream_t stream,
+                                 SgemmPrepared* out);
+cudaError_t sgemm_tf32x3_block(const SgemmPrepared& p, int m, int n0, int nj, int k, float alpha,
+                               float beta, float* c, long long ldc, cudaStream_t stream);
 
 // GEMM of any supported element-type combination (types and arithmetic numbered as
 // validate.hpp's DataType and ComputeKind): FP32 runs sgemm_ffma_ws or sgemm_tf32x3;

@@ -77,9 +77,41 @@ struct Runtime::Impl {
   uint64_t next_id = 1;
   uint64_t clock = 0;
   StreamId s_h2d = 0, s_d2h = 0, s_compute = 0;
+  StreamId s_compute2 = 0; // column blocks of a deferred GEMM alternate between the two
   EventId e_a = 0, e_b = 0;
   std::vector<EventId> event_pool;
   bool opened = false;
+
+  // The C column blocks of the last deferred GEMM: byte ranges of one allocation and the
+  // event after which each holds its final values.  Valid until the next operation that
+  // launches device work or touches that allocation.
+  struct BlockRange {
+    uint64_t begin = 0, end = 0;
+    EventId done = 0;
+  };
+  uint64_t staged_alloc = 0;
+  std::vector<BlockRange> staged;
+  bool status_unchecked = false; // a deferred GEMM's error word has not been read yet
+
+  void clear_staged() {
+    for (const BlockRange& r : staged)
+      put_event(r.done);
+    staged.clear();
+    staged_alloc = 0;
+  }
+  // Reads the kernels' error word once a deferred GEMM's kernels have been waited for.
+  Error check_deferred() {
+    if (!status_unchecked)
+      return {};
+    status_unchecked = false;
+    uint32_t word = 0;
+    if (Error e = dev->kernel_status(s_compute, &word))
+      return e;
+    if (word)
+      return make_error(XVRAM_STATUS_TIMEOUT, "executor", "sgemm",
+                        "a kernel pipeline wait exceeded its limit");
+    return {};
+  }
 
   uint64_t chunk_len(const Alloc& a, uint64_t c) const {
     return std::min<uint64_t>(cb, a.bytes - c * cb);
@@ -394,6 +426,9 @@ struct Runtime::Impl {
   Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
                       const std::set<std::pair<uint64_t, uint32_t>>& keep, uint64_t ws);
   Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
+  int64_t column_block_width(const GemmCall& call) const;
+  Error gemm_column_blocks(const GemmCall& call, const Alloc& A, const Alloc& B, const Alloc& C,
+                           uint64_t ws_va, uint64_t ws, int64_t width);
   void gemm_chunks(const GemmCall& call, std::set<std::pair<uint64_t, uint32_t>>* keep,
                    uint64_t* ws, bool* in_place);
   PlanLimits streamed_limits(const GemmCall& call) const;
@@ -495,6 +530,8 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
     return e;
   if (Error e = m.dev->stream_create(&m.s_compute))
     return e;
+  if (Error e = m.dev->stream_create(&m.s_compute2))
+    return e;
   if (Error e = m.dev->event_create(&m.e_a))
     return e;
   if (Error e = m.dev->event_create(&m.e_b))
@@ -523,8 +560,11 @@ Error Runtime::close() {
       first = e;
   };
   keep(m.dev->stream_sync(m.s_h2d));
+  keep(m.dev->stream_sync(m.s_compute2));
   keep(m.dev->stream_sync(m.s_compute));
   keep(m.dev->stream_sync(m.s_d2h));
+  keep(m.check_deferred());
+  m.clear_staged();
   for (auto& [id, a] : m.allocs) {
     for (size_t c = 0; c < a.chunks.size(); ++c) {
       if (a.chunks[c].frame >= 0) {
@@ -585,6 +625,8 @@ Error Runtime::release(uint64_t id) {
   if (it == m.allocs.end() || !it->second.live)
     return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "runtime", "release", "unknown allocation");
   Alloc& a = it->second;
+  if (m.staged_alloc == id)
+    m.clear_staged();
   for (size_t c = 0; c < a.chunks.size(); ++c) {
     Chunk& ch = a.chunks[c];
     if (ch.frame < 0)
@@ -621,6 +663,8 @@ Error Runtime::write(uint64_t id, uint64_t offset, const void* src, uint64_t byt
   Alloc& a = m.allocs.at(id);
   if (bytes == 0)
     return {};
+  if (m.staged_alloc == id)
+    m.clear_staged();
   const uint32_t c0 = static_cast<uint32_t>(offset / m.cb);
   const uint32_t c1 = static_cast<uint32_t>((offset + bytes - 1) / m.cb);
   bool all_resident = true;
@@ -690,10 +734,16 @@ Error Runtime::read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes) {
     return {};
   const uint64_t end = offset + bytes;
   bool any_dma = false;
+  // e_a follows all device work so far (a deferred GEMM's blocks are joined into s_compute).
+  // A read of the C of the last deferred GEMM waits for each column block's own kernel
+  // instead, so the first blocks come home while the last ones compute.
   if (Error e = m.dev->event_record(m.e_a, m.s_compute))
     return e;
-  if (Error e = m.dev->stream_wait_event(m.s_d2h, m.e_a))
-    return e;
+  const bool by_block = m.staged_alloc == id && !m.staged.empty();
+  if (!by_block)
+    if (Error e = m.dev->stream_wait_event(m.s_d2h, m.e_a))
+      return e;
+  EventId waited = by_block ? 0 : m.e_a;
   // Chunks still being uploaded (a prefetch) are read after their upload.
   for (uint64_t c = offset / m.cb; c <= (end - 1) / m.cb; ++c) {
     const int32_t fi = a.chunks[static_cast<size_t>(c)].frame;
@@ -716,9 +766,28 @@ Error Runtime::read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes) {
         break;
       run_end = std::min(end, (run_end / m.cb + 1) * m.cb);
     }
+    EventId need = m.e_a;
+    if (by_block) { // the piece ends at the edge of its column block
+      for (const Impl::BlockRange& r : m.staged) {
+        if (pos >= r.end)
+          continue;
+        if (pos >= r.begin) {
+          run_end = std::min(run_end, r.end);
+          need = r.done;
+        } else {
+          run_end = std::min(run_end, r.begin);
+        }
+        break;
+      }
+    }
     char* out = static_cast<char*>(dst) + (pos - offset);
     const uint64_t len = run_end - pos;
     if (from_dev) {
+      if (waited != m.e_a && need != waited) {
+        if (Error e = m.dev->stream_wait_event(m.s_d2h, need))
+          return e;
+        waited = need;
+      }
       if (Error e = m.dev->copy_2d(reinterpret_cast<uint64_t>(out), len, a.va + pos, len, len, 1,
                                    CopyDir::d2h, m.s_d2h))
         return e;
@@ -734,16 +803,20 @@ Error Runtime::read(uint64_t id, uint64_t offset, void* dst, uint64_t bytes) {
   if (any_dma)
     if (Error e = m.dev->stream_sync(m.s_d2h))
       return e;
-  return {};
+  return m.check_deferred();
 }
 
 Error Runtime::synchronize() {
   Impl& m = *impl_;
   if (Error e = m.dev->stream_sync(m.s_h2d))
     return e;
+  if (Error e = m.dev->stream_sync(m.s_compute2))
+    return e;
   if (Error e = m.dev->stream_sync(m.s_compute))
     return e;
-  return m.dev->stream_sync(m.s_d2h);
+  if (Error e = m.dev->stream_sync(m.s_d2h))
+    return e;
+  return m.check_deferred();
 }
 
 Error Runtime::mem_get_info(uint64_t* free_bytes, uint64_t* total_bytes) {
@@ -859,6 +932,7 @@ Error Runtime::gemm(const GemmCall& call) {
       return make_error(XVRAM_STATUS_INVALID_ARGUMENT, "executor", "gemm",
                         "a matrix offset is not a multiple of its element size");
   }
+  m.clear_staged();
   if (Error e = m.apply_budget(false))
     return e;
   Alloc& A = m.allocs.at(call.shape.a.allocation_id);
@@ -893,18 +967,40 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   const GemmShape& s = call.shape;
   ++x.tiles_submitted;
   ++x.gemm_in_place;
-  if (Error e = dev->gemm(gemm_types(s), s.op_a, s.op_b, static_cast<int64_t>(s.m),
-                          static_cast<int64_t>(s.n), static_cast<int64_t>(s.k), call.alpha,
-                          A.va + s.a.offset_bytes, static_cast<int64_t>(s.a.ld),
-                          B.va + s.b.offset_bytes, static_cast<int64_t>(s.b.ld), call.beta,
-                          C.va + s.c.offset_bytes, static_cast<int64_t>(s.c.ld),
-                          ws ? allocs.at(kScratchId).va : 0, ws, s_compute))
+  const uint64_t ws_va = ws ? allocs.at(kScratchId).va : 0;
+  const int64_t width = call.defer_completion ? column_block_width(call) : 0;
+  if (width > 0) {
+    if (Error e = gemm_column_blocks(call, A, B, C, ws_va, ws, width))
+      return e;
+  } else if (Error e = dev->gemm(gemm_types(s), s.op_a, s.op_b, static_cast<int64_t>(s.m),
+                                 static_cast<int64_t>(s.n), static_cast<int64_t>(s.k),
+                                 call.alpha, A.va + s.a.offset_bytes,
+                                 static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
+                                 static_cast<int64_t>(s.b.ld), call.beta,
+                                 C.va + s.c.offset_bytes, static_cast<int64_t>(s.c.ld), ws_va, ws,
+                                 s_compute)) {
     return e;
+  }
   for (const auto& [id, c] : keep) {
     Frame& f = frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)];
     if (Error e = dev->event_record(f.last_use, s_compute))
       return e;
     f.pending = true;
+  }
+  if (call.defer_completion) {
+    // The frames stay pending (evicting or releasing them waits for last_use); C's
+    // chunks hold the result from here on in stream order.
+    for (const auto& [id, c] : keep)
+      if (id == C.id) {
+        Chunk& ch = C.chunks[c];
+        ch.written = true;
+        ch.dev_valid = true;
+        ch.backing_valid = false;
+      }
+    status_unchecked = true;
+    ++x.gemm_deferred;
+    ++x.tiles_retired;
+    return {};
   }
   uint32_t word = 0;
   if (Error e = dev->kernel_status(s_compute, &word))
@@ -924,6 +1020,78 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   for (const auto& [id, c] : keep)
     frames[static_cast<size_t>(allocs.at(id).chunks[c].frame)].pending = false;
   ++x.tiles_retired;
+  return {};
+}
+
+// Column blocks for a deferred in-place GEMM: whole 256-column tile columns, about one wave
+// of tiles per block (128 x 256 tiles, one per SM, for FFMA; 256 x 256 tiles, one per SM
+// pair, for TF32) and at most 8 blocks, so a block's D2H copy takes less time than the
+// next block's kernels.  0 = launch it whole: FP16 / BF16 / FP64, or fewer than two
+// waves of tiles.
+int64_t Runtime::Impl::column_block_width(const GemmCall& call) const {
+  const GemmShape& s = call.shape;
+  const GemmTypes t = gemm_types(s);
+  if (t.ab != kFp32 || t.c != kFp32 || (t.compute != kStrictFp32 && t.compute != kTf32) ||
+      s.k == 0)
+    return 0;
+  const uint64_t tile_m = t.compute == kTf32 ? 256 : 128;
+  const uint64_t tiles_m = (s.m + tile_m - 1) / tile_m, tiles_n = (s.n + 255) / 256;
+  const uint64_t sms = static_cast<uint64_t>(std::max(1, info.sm_count));
+  const uint64_t wave = t.compute == kTf32 ? std::max<uint64_t>(1, sms / 2) : sms;
+  const uint64_t blocks = std::min<uint64_t>({8, tiles_n, tiles_m * tiles_n / wave});
+  if (blocks < 2)
+    return 0;
+  return static_cast<int64_t>((tiles_n + blocks - 1) / blocks * 256);
+}
+
+// The deferred in-place GEMM as column blocks: the operands are prepared once in the
+// workspace (the FFMA path's transposes, the TF32 path's hi/lo splits), then block j
+// computes C's columns [j w, (j + 1) w) on one of two streams, so a block's last wave
+// overlaps the next block's first.  Every output is computed as in the unsplit launch, so
+// the results are bit-identical.
+Error Runtime::Impl::gemm_column_blocks(const GemmCall& call, const Alloc& A, const Alloc& B,
+                                        const Alloc& C, uint64_t ws_va, uint64_t ws,
+                                        int64_t width) {
+  const GemmShape& s = call.shape;
+  const int64_t m = static_cast<int64_t>(s.m), n = static_cast<int64_t>(s.n),
+                k = static_cast<int64_t>(s.k), ldc = static_cast<int64_t>(s.c.ld);
+  PreparedGemm prep;
+  if (Error e = dev->gemm_prepare(gemm_types(s), s.op_a, s.op_b, m, n, k, A.va + s.a.offset_bytes,
+                                  static_cast<int64_t>(s.a.ld), B.va + s.b.offset_bytes,
+                                  static_cast<int64_t>(s.b.ld), ws_va, ws, s_compute, &prep))
+    return e;
+  // The second stream starts after the uploads and the preparation.
+  if (Error e = dev->event_record(e_b, s_compute))
+    return e;
+  if (Error e = dev->stream_wait_event(s_compute2, e_b))
+    return e;
+  clear_staged();
+  staged_alloc = C.id;
+  EventId last2 = 0;
+  int64_t j = 0;
+  for (int64_t j0 = 0; j0 < n; j0 += width, ++j) {
+    const int64_t nj = std::min(width, n - j0);
+    const StreamId st = (j & 1) ? s_compute2 : s_compute;
+    const uint64_t col = s.c.offset_bytes + static_cast<uint64_t>(j0 * ldc) * 4;
+    if (Error e = dev->gemm_block(prep, m, j0, nj, k, call.alpha, call.beta, C.va + col, ldc, st))
+      return e;
+    EventId done = 0;
+    if (Error e = get_event(&done))
+      return e;
+    // Block ranges tile C's span without gaps: the rows below m of a block's last column
+    // (ldc > m) belong to it, so a read of the whole span never waits for all blocks.
+    const int64_t end_elem = j0 + nj < n ? (j0 + nj) * ldc : (n - 1) * ldc + m;
+    staged.push_back({col, s.c.offset_bytes + static_cast<uint64_t>(end_elem) * 4, done});
+    if (Error e = dev->event_record(done, st))
+      return e;
+    if (st == s_compute2)
+      last2 = done;
+  }
+  // Later work on s_compute (and events recorded there) follows every block.
+  if (last2)
+    if (Error e = dev->stream_wait_event(s_compute, last2))
+      return e;
+  x.gemm_column_blocks += static_cast<uint64_t>(j);
   return {};
 }
 
@@ -1216,6 +1384,7 @@ Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t work
   const auto t0 = std::chrono::steady_clock::now();
   if (Error e = m.check_ranges(ranges, "transaction"))
     return e;
+  m.clear_staged();
   if (Error e = m.apply_budget(false))
     return e;
   std::set<std::pair<uint64_t, uint32_t>> keep;

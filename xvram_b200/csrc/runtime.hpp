@@ -61,6 +61,13 @@ struct GemmCall {
   double alpha = 1.0, beta = 0.0;
   // Rates for planning this call (0 = the runtime's configured rates).
   double flops_per_s = 0;
+  // Return once the kernels are queued, as cublasSgemm does, instead of after they finish.
+  // An in-place FP32 GEMM (strict or TF32) is then launched as column blocks of C on two
+  // streams,
+  // and a later read of C copies each block home as soon as its own kernel is done, while
+  // the next blocks compute.  The kernels' error word is read at the next read, synchronize
+  // or close, which report a failed kernel.
+  bool defer_completion = false;
 };
 
 // A byte range of an allocation that an operation touches (reference
@@ -113,6 +120,10 @@ struct RuntimeExtra {
   int64_t last_steps = 0;
   int32_t last_panel_slots = 0;
   double last_gemm_ms = 0;
+  // In-place GEMMs that returned before their kernels finished, and the C column blocks
+  // they were launched as.
+  uint64_t gemm_deferred = 0;
+  uint64_t gemm_column_blocks = 0;
 };
 
 class Runtime {

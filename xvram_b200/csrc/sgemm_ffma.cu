@@ -658,41 +658,93 @@ uint64_t sgemm_workspace_bytes(int op_a, int op_b, int m, int n, int k) {
   return bytes;
 }
 
+namespace {
+
+// The FFMA half of sgemm_prepare; `tma` says whether the canonical operands go to the TMA
+// kernel (they always qualify) or the operands stay as given.
+cudaError_t ffma_prepare(int op_a, int op_b, int m, int n, int k, const float* a, long long lda,
+                         const float* b, long long ldb, void* workspace, uint64_t workspace_bytes,
+                         SgemmPath path, cudaStream_t stream, SgemmPrepared* out, bool* tma) {
+  *out = SgemmPrepared{};
+  out->a = a;
+  out->b = b;
+  out->lda = lda;
+  out->ldb = ldb;
+  out->op_a = op_a;
+  out->op_b = op_b;
+  *tma = false;
+  const uint64_t need = sgemm_workspace_bytes(op_a, op_b, m, n, k);
+  if (need == 0 || !workspace || workspace_bytes < need || path == SgemmPath::generic ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
+      !sgemm_tma_eligible(op_a, op_b, a, lda, b, ldb))
+    return cudaSuccess;
+  // Canonicalise K-major operands into the workspace for the M/N-major kernel.
+  const auto up4 = [](long long v) { return (v + 3) / 4 * 4; };
+  char* ws = static_cast<char*>(workspace);
+  if (op_a != 0) {
+    float* at = reinterpret_cast<float*>(ws);
+    out->lda = up4(m);
+    if (cudaError_t e = launch_transpose(a, lda, at, out->lda, k, m, stream); e != cudaSuccess)
+      return e;
+    out->a = at;
+    out->op_a = 0;
+    ws += (static_cast<uint64_t>(out->lda) * k * 4 + 255) / 256 * 256;
+  }
+  if (op_b == 0) {
+    float* bt = reinterpret_cast<float*>(ws);
+    out->ldb = up4(n);
+    if (cudaError_t e = launch_transpose(b, ldb, bt, out->ldb, k, n, stream); e != cudaSuccess)
+      return e;
+    out->b = bt;
+    out->op_b = 1;
+  }
+  *tma = true;
+  return cudaSuccess;
+}
+
+// C's columns [n0, n0 + nj): op(B)'s columns n0.. are B's columns (op N) or rows (op T).
+cudaError_t ffma_block(const SgemmPrepared& p, int m, int n0, int nj, int k, float alpha,
+                       float beta, float* c, long long ldc, cudaStream_t stream, SgemmPath path) {
+  const float* b = p.op_b == 0 ? p.b + static_cast<long long>(n0) * p.ldb : p.b + n0;
+  return sgemm_ffma(p.op_a, p.op_b, m, nj, k, alpha, p.a, p.lda, b, p.ldb, beta, c, ldc, stream,
+                    path);
+}
+
+} // namespace
+
 cudaError_t sgemm_ffma_ws(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,
                           long long lda, const float* b, long long ldb, float beta, float* c,
                           long long ldc, void* workspace, uint64_t workspace_bytes,
                           cudaStream_t stream, SgemmPath path) {
   if (m <= 0 || n <= 0)
     return cudaSuccess;
-  const uint64_t need = sgemm_workspace_bytes(op_a, op_b, m, n, k);
-  if (need > 0 && workspace && workspace_bytes >= need && path != SgemmPath::generic &&
-      (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
-      sgemm_tma_eligible(op_a, op_b, a, lda, b, ldb)) {
-    // Canonicalise K-major operands into the workspace, then run the M/N-major kernel.
-    const auto up4 = [](long long v) { return (v + 3) / 4 * 4; };
-    char* ws = static_cast<char*>(workspace);
-    const float* a2 = a;
-    const float* b2 = b;
-    long long lda2 = lda, ldb2 = ldb;
-    if (op_a != 0) {
-      float* at = reinterpret_cast<float*>(ws);
-      lda2 = up4(m);
-      if (cudaError_t e = launch_transpose(a, lda, at, lda2, k, m, stream); e != cudaSuccess)
-        return e;
-      a2 = at;
-      ws += (static_cast<uint64_t>(lda2) * k * 4 + 255) / 256 * 256;
-    }
-    if (op_b == 0) {
-      float* bt = reinterpret_cast<float*>(ws);
-      ldb2 = up4(n);
-      if (cudaError_t e = launch_transpose(b, ldb, bt, ldb2, k, n, stream); e != cudaSuccess)
-        return e;
-      b2 = bt;
-    }
-    return sgemm_ffma(0, 1, m, n, k, alpha, a2, lda2, b2, ldb2, beta, c, ldc, stream,
-                      SgemmPath::tma);
-  }
-  return sgemm_ffma(op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, stream, path);
+  SgemmPrepared p;
+  bool tma = false;
+  if (cudaError_t e = ffma_prepare(op_a, op_b, m, n, k, a, lda, b, ldb, workspace,
+                                   workspace_bytes, path, stream, &p, &tma);
+      e != cudaSuccess)
+    return e;
+  return ffma_block(p, m, 0, n, k, alpha, beta, c, ldc, stream, tma ? SgemmPath::tma : path);
+}
+
+cudaError_t sgemm_prepare(bool tf32, int op_a, int op_b, int m, int n, int k, const float* a,
+                          long long lda, const float* b, long long ldb, void* workspace,
+                          uint64_t workspace_bytes, cudaStream_t stream, SgemmPrepared* out) {
+  if (tf32)
+    return sgemm_tf32x3_prepare(op_a, op_b, m, n, k, a, lda, b, ldb, workspace,
+                                workspace_bytes, stream, out);
+  bool tma = false;
+  return ffma_prepare(op_a, op_b, m, n, k, a, lda, b, ldb, workspace, workspace_bytes,
+                      SgemmPath::automatic, stream, out, &tma);
+}
+
+cudaError_t sgemm_block(const SgemmPrepared& p, int m, int n0, int nj, int k, float alpha,
+                        float beta, float* c, long long ldc, cudaStream_t stream) {
+  if (m <= 0 || nj <= 0)
+    return cudaSuccess;
+  if (p.tf32)
+    return sgemm_tf32x3_block(p, m, n0, nj, k, alpha, beta, c, ldc, stream);
+  return ffma_block(p, m, n0, nj, k, alpha, beta, c, ldc, stream, SgemmPath::automatic);
 }
 
 cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, const float* a,

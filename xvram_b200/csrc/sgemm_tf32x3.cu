@@ -474,7 +474,20 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
                          cudaStream_t stream) {
   if (m <= 0 || n <= 0)
     return cudaSuccess;
-  if (k <= 0 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) ||
+  SgemmPrepared p;
+  if (cudaError_t e = sgemm_tf32x3_prepare(op_a, op_b, m, n, k, a, lda, b, ldb, workspace,
+                                           workspace_bytes, stream, &p);
+      e != cudaSuccess)
+    return e;
+  return sgemm_tf32x3_block(p, m, 0, n, k, alpha, beta, c, ldc, stream);
+}
+
+cudaError_t sgemm_tf32x3_prepare(int op_a, int op_b, int m, int n, int k, const float* a,
+                                 long long lda, const float* b, long long ldb, void* workspace,
+                                 uint64_t workspace_bytes, cudaStream_t stream,
+                                 SgemmPrepared* out) {
+  if (m <= 0 || n <= 0 || k <= 0 || !workspace ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) ||
       workspace_bytes < sgemm_tf32x3_workspace_bytes(m, n, k))
     return cudaErrorInvalidValue;
   const uint64_t kp = up(static_cast<uint64_t>(k), 4);
@@ -514,10 +527,30 @@ cudaError_t sgemm_tf32x3(int op_a, int op_b, int m, int n, int k, float alpha, c
     return e;
   if (cudaError_t e = split(b, ldb, op_b == 0, n, b_hi, b_lo); e != cudaSuccess)
     return e;
+  *out = SgemmPrepared{};
+  out->tf32 = true;
+  out->a_hi = a_hi;
+  out->a_lo = a_lo;
+  out->b_hi = b_hi;
+  out->b_lo = b_lo;
+  out->kp = static_cast<long long>(kp);
+  return cudaSuccess;
+}
 
+cudaError_t sgemm_tf32x3_block(const SgemmPrepared& o, int m, int n0, int nj, int k, float alpha,
+                               float beta, float* c, long long ldc, cudaStream_t stream) {
+  if (m <= 0 || nj <= 0)
+    return cudaSuccess;
+  if (k <= 0 || !o.tf32 || n0 < 0)
+    return cudaErrorInvalidValue;
+  const uint64_t kp = static_cast<uint64_t>(o.kp);
+  const int n = nj;
+  // op(B)'s columns n0.. are rows n0.. of the K-major splits.
+  const float* b_hi = o.b_hi + static_cast<uint64_t>(n0) * kp;
+  const float* b_lo = o.b_lo + static_cast<uint64_t>(n0) * kp;
   CUtensorMap t_ahi, t_alo, t_bhi, t_blo;
-  if (!encode_kmajor(&t_ahi, a_hi, k, m, kp, kRows) ||
-      !encode_kmajor(&t_alo, a_lo, k, m, kp, kRows) ||
+  if (!encode_kmajor(&t_ahi, o.a_hi, k, m, kp, kRows) ||
+      !encode_kmajor(&t_alo, o.a_lo, k, m, kp, kRows) ||
       !encode_kmajor(&t_bhi, b_hi, k, n, kp, kRows) ||
       !encode_kmajor(&t_blo, b_lo, k, n, kp, kRows))
     return cudaErrorInvalidValue;
