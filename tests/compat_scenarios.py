@@ -304,6 +304,47 @@ def scenario_deferred(oracle):
     return res
 
 
+def scenario_deferred_evict(oracle):
+    """Under a 512 MiB budget: a deferred GEMM whose C (128 MiB) is not read, then an
+    8192 x 8192 x 4096 GEMM that streams and writes that C back to the host to free its
+    frames, then C read (from the host copy) and updated in place by a second deferred
+    GEMM, read in two pieces."""
+    api = cp.CompatApi()
+    init(api, cache_target=512 * MiB, chunk=64 * MiB)
+    h = api.blas_create()
+    m, n, k = 8192, 4096, 256
+    a = oracle.uniform(m * k, 80).reshape(k, m)
+    b = oracle.uniform(k * n, 81).reshape(n, k)
+    c = oracle.uniform(m * n, 82).reshape(n, m)
+    da, db, dc = upload(api, a), upload(api, b), upload(api, c)
+    api.check("sgemm", api.sgemm(h, 0, 0, m, n, k, 0.5, da, m, db, k, 1.5, dc, m))
+    bm, bn, bk = 8192, 8192, 4096
+    x1 = oracle.uniform(bm * bk, 83)
+    x2 = oracle.uniform(bk * bn, 84)
+    d1, d2 = upload(api, x1), upload(api, x2)
+    d3 = api.malloc(bm * bn * 4)
+    api.check("sgemm", api.sgemm(h, 0, 0, bm, bn, bk, 1.0, d1, bm, d2, bk, 0.0, d3, bm))
+    first = np.empty_like(c)
+    api.d2h(ptr(first), dc, first.nbytes)
+    rng = np.random.default_rng(6)
+    rows, cols = rng.integers(0, m, 8192), rng.integers(0, n, 8192)
+    ref = oracle.gemm_sampled(0, 0, k, 0.5, a, m, b, k, 1.5, c, m, rows, cols, threads=16)
+    res = {"evicted_err": float(np.max(np.abs(first[cols, rows] - ref))) / k}
+    api.check("sgemm", api.sgemm(h, 0, 0, m, n, k, 1.0, da, m, db, k, 1.0, dc, m))
+    second = np.empty_like(c)
+    half = 4 * (m * 1500 + 3)
+    api.d2h(ptr(second), dc, half)
+    api.d2h(ptr(second) + half, dc + half, second.nbytes - half)
+    dot = oracle.gemm_sampled(0, 0, k, 1.0, a, m, b, k, 0.0, None, m, rows, cols, threads=16)
+    res["second_err"] = float(np.max(np.abs(second[cols, rows] - (dot + first[cols, rows])))) / k
+    t = api.telemetry()
+    info = cp.runtime_info()
+    res.update(dirty_evictions=t.runtime.dirty_evictions, streamed=info.gemm_streamed,
+               deferred=info.gemm_deferred, blocks=info.gemm_column_blocks)
+    res["shutdown"] = api.shutdown()
+    return res
+
+
 SCENARIOS = {name[len("scenario_"):]: fn for name, fn in globals().items()
              if name.startswith("scenario_")}
 

@@ -92,3 +92,13 @@ def test_deferred_column_blocks_bit_identical_to_synchronous():
     assert d["digests"] == s["digests"]
     assert max(d["errors"].values()) <= 1e-6 and d["pad_kept"]
     assert d["shutdown"] == 0 and s["shutdown"] == 0
+
+
+def test_deferred_result_survives_eviction():
+    """A deferred GEMM's unread C is written back to the host when a streamed GEMM needs
+    its frames; the values read afterwards, and after a second deferred update, are right."""
+    r = run("deferred_evict")
+    assert r["streamed"] == 1 and r["dirty_evictions"] > 0
+    assert r["deferred"] == 2 and r["blocks"] == 2 * 6
+    assert r["evicted_err"] <= 1e-6 and r["second_err"] <= 1e-6
+    assert r["shutdown"] == 0

@@ -74,6 +74,37 @@ with installed() as fake:
                 for p in (pa, pb, pc):
                     api.free(p)
         out["prepares"] = int(fake.fake_device_prepares() - p0)
+    elif mode == "evict":
+        # a deferred GEMM whose C is not read, then a GEMM too large for the 64 MiB budget
+        # (streamed: it writes the first C back to the host to free its frames), then C
+        # written again by a third, in-place GEMM whose result is read in pieces
+        a, b, c = orc.uniform(m * k, 1), orc.uniform(k * n, 2), orc.uniform(ldc * n, 3)
+        pa, pb, pc = (api.malloc(x.nbytes) for x in (a, b, c))
+        for p, x in zip((pa, pb, pc), (a, b, c)):
+            api.h2d(p, x.ctypes.data, x.nbytes)
+        api.check("sgemm", api.sgemm(h, 0, 0, m, n, k, 0.5, pa, m, pb, k, 1.5, pc, ldc))
+        big = 2816
+        x1, x2 = orc.uniform(big * big, 4), orc.uniform(big * big, 5)
+        p1, p2, p3 = (api.malloc(big * big * 4) for _ in range(3))
+        api.h2d(p1, x1.ctypes.data, x1.nbytes)
+        api.h2d(p2, x2.ctypes.data, x2.nbytes)
+        api.check("sgemm", api.sgemm(h, 0, 0, big, big, big, 1.0, p1, big, p2, big, 0.0, p3, big))
+        got = np.empty(ldc * n, np.float32)
+        api.d2h(got.ctypes.data, pc, got.nbytes)
+        ref = orc.gemm(0, 0, m, n, k, 0.5, a, m, b, k, 1.5, c, ldc)
+        out["evicted_err"] = float(normalized_error(got.reshape(n, ldc)[:, :m], ref, k, 1.0, 1.0))
+        # C holds the first result; a second deferred GEMM updates it in place again
+        api.check("sgemm", api.sgemm(h, 0, 0, m, n, k, 1.0, pa, m, pb, k, 1.0, pc, ldc))
+        got2 = np.empty_like(got)
+        half = 4 * (ldc * 901 + 11)
+        api.d2h(got2.ctypes.data, pc, half)
+        api.d2h(got2.ctypes.data + half, pc + half, got2.nbytes - half)
+        dot = orc.gemm(0, 0, m, n, k, 1.0, a, m, b, k, 0.0, None, m)
+        out["second_err"] = float(normalized_error(got2.reshape(n, ldc)[:, :m],
+                                                   dot + got.reshape(n, ldc)[:, :m], k, 1.0, 1.0))
+        tel = api.telemetry()
+        out["dirty_evictions"] = int(tel.runtime.dirty_evictions)
+        out["streamed"] = int(cp.runtime_info().gemm_streamed)
     elif mode == "error":
         a, b, c = orc.uniform(m * k, 1), orc.uniform(k * n, 2), orc.uniform(ldc * n, 3)
         pa, pb, pc = (api.malloc(x.nbytes) for x in (a, b, c))
@@ -148,3 +179,13 @@ def test_kernel_error_surfaces_at_the_next_copy():
     assert e["after"] == 15          # XVRAM_STATUS_POISONED
     assert r["state"] == 3           # XVRAM_CUDA_COMPAT_POISONED
     assert r["deferred"] == 2
+
+
+def test_deferred_result_survives_eviction_by_a_streamed_gemm():
+    """A deferred GEMM's C, never read, is written back to the host when a larger,
+    streamed GEMM needs its frames; reading it afterwards (from the host copy) and updating
+    it with another deferred GEMM both give the right values."""
+    r = run("evict")
+    assert r["streamed"] == 1 and r["dirty_evictions"] > 0
+    assert r["evicted_err"] <= TOLERANCE and r["second_err"] <= TOLERANCE
+    assert r["deferred"] == 2 and r["shutdown"] == 0
