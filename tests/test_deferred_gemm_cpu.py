@@ -40,14 +40,18 @@ with installed() as fake:
     orc = load_oracle()
     h = api.blas_create()
     m, n, k = 500, 1800, 96
+    if mode == "narrow":
+        n = 2800  # 11 tile columns in 8 blocks: one-column first and last blocks
     ldc = m + 6
     out = {"results": {}, "errors": {}}
-    if mode in ("ops", "tf32"):
+    if mode in ("ops", "tf32", "narrow"):
         if mode == "tf32":  # math mode 3; the fake computes it in strict FP32
             api.check("math", api.t.blas_set_math_mode(h, 3))
         p0 = fake.fake_device_prepares()
         for op_a in (0, 1):
             for op_b in (0, 1):
+                if mode == "narrow" and (op_a, op_b) != (1, 0):
+                    continue
                 lda = m if op_a == 0 else k
                 ldb = k if op_b == 0 else n
                 a = orc.uniform(lda * (k if op_a == 0 else m), 10 + op_a)
@@ -189,3 +193,14 @@ def test_deferred_result_survives_eviction_by_a_streamed_gemm():
     assert r["streamed"] == 1 and r["dirty_evictions"] > 0
     assert r["evicted_err"] <= TOLERANCE and r["second_err"] <= TOLERANCE
     assert r["deferred"] == 2 and r["shutdown"] == 0
+
+
+def test_narrow_first_and_last_blocks():
+    """11 tile columns in 8 blocks: the first and last are one tile column wide, the six
+    between share the other nine; the result is still bit-identical."""
+    d = run("narrow")
+    s = run("narrow", sync=True)
+    assert d["deferred"] == 1 and d["blocks"] == 8
+    r = d["results"]["10"]
+    assert r["err"] <= TOLERANCE and r["pad_kept"]
+    assert r["digest"] == s["results"]["10"]["digest"]

@@ -426,9 +426,9 @@ struct Runtime::Impl {
   Error gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C,
                       const std::set<std::pair<uint64_t, uint32_t>>& keep, uint64_t ws);
   Error gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, Alloc& C);
-  int64_t column_block_width(const GemmCall& call) const;
+  std::vector<int64_t> column_block_edges(const GemmCall& call) const;
   Error gemm_column_blocks(const GemmCall& call, const Alloc& A, const Alloc& B, const Alloc& C,
-                           uint64_t ws_va, uint64_t ws, int64_t width);
+                           uint64_t ws_va, uint64_t ws, const std::vector<int64_t>& edges);
   void gemm_chunks(const GemmCall& call, std::set<std::pair<uint64_t, uint32_t>>* keep,
                    uint64_t* ws, bool* in_place);
   PlanLimits streamed_limits(const GemmCall& call) const;
@@ -968,9 +968,10 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   ++x.tiles_submitted;
   ++x.gemm_in_place;
   const uint64_t ws_va = ws ? allocs.at(kScratchId).va : 0;
-  const int64_t width = call.defer_completion ? column_block_width(call) : 0;
-  if (width > 0) {
-    if (Error e = gemm_column_blocks(call, A, B, C, ws_va, ws, width))
+  const std::vector<int64_t> edges =
+      call.defer_completion ? column_block_edges(call) : std::vector<int64_t>{};
+  if (!edges.empty()) {
+    if (Error e = gemm_column_blocks(call, A, B, C, ws_va, ws, edges))
       return e;
   } else if (Error e = dev->gemm(gemm_types(s), s.op_a, s.op_b, static_cast<int64_t>(s.m),
                                  static_cast<int64_t>(s.n), static_cast<int64_t>(s.k),
@@ -1023,35 +1024,52 @@ Error Runtime::Impl::gemm_in_place(const GemmCall& call, Alloc& A, Alloc& B, All
   return {};
 }
 
-// Column blocks for a deferred in-place GEMM: whole 256-column tile columns, about one wave
-// of tiles per block (128 x 256 tiles, one per SM, for FFMA; 256 x 256 tiles, one per SM
-// pair, for TF32) and at most 8 blocks, so a block's D2H copy takes less time than the
-// next block's kernels.  0 = launch it whole: FP16 / BF16 / FP64, or fewer than two
-// waves of tiles.
-int64_t Runtime::Impl::column_block_width(const GemmCall& call) const {
+// Column blocks for a deferred in-place GEMM, as the column edges [0, e1, ..., n]: whole
+// 256-column tile columns, about one wave of tiles per block (128 x 256 tiles, one per SM,
+// for FFMA; 256 x 256 tiles, one per SM pair, for TF32) and at most 8 blocks, so a block's
+// D2H copy takes less time than the next block's kernels.  With 4 or more blocks the first
+// and last are one tile column wide: the copies start sooner (the TF32 path, whose D2H
+// outlasts its kernels) and the copy left after the last kernel is short (the FFMA path).
+// Empty = launch it whole: FP16 / BF16 / FP64, or fewer than two waves of tiles.
+std::vector<int64_t> Runtime::Impl::column_block_edges(const GemmCall& call) const {
   const GemmShape& s = call.shape;
   const GemmTypes t = gemm_types(s);
   if (t.ab != kFp32 || t.c != kFp32 || (t.compute != kStrictFp32 && t.compute != kTf32) ||
       s.k == 0)
-    return 0;
+    return {};
   const uint64_t tile_m = t.compute == kTf32 ? 256 : 128;
   const uint64_t tiles_m = (s.m + tile_m - 1) / tile_m, tiles_n = (s.n + 255) / 256;
   const uint64_t sms = static_cast<uint64_t>(std::max(1, info.sm_count));
   const uint64_t wave = t.compute == kTf32 ? std::max<uint64_t>(1, sms / 2) : sms;
   const uint64_t blocks = std::min<uint64_t>({8, tiles_n, tiles_m * tiles_n / wave});
   if (blocks < 2)
-    return 0;
-  return static_cast<int64_t>((tiles_n + blocks - 1) / blocks * 256);
+    return {};
+  // Tile columns per block.
+  std::vector<uint64_t> widths;
+  const bool narrow_ends = blocks >= 4 && tiles_n >= blocks + 2;
+  const uint64_t inner = narrow_ends ? blocks - 2 : blocks;
+  const uint64_t inner_tiles = narrow_ends ? tiles_n - 2 : tiles_n;
+  if (narrow_ends)
+    widths.push_back(1);
+  for (uint64_t i = 0; i < inner; ++i) // near-equal, wider ones first
+    widths.push_back(inner_tiles / inner + (i < inner_tiles % inner ? 1 : 0));
+  if (narrow_ends)
+    widths.push_back(1);
+  std::vector<int64_t> edges{0};
+  for (uint64_t w : widths)
+    edges.push_back(std::min<int64_t>(static_cast<int64_t>(s.n), edges.back() +
+                                                                   static_cast<int64_t>(w * 256)));
+  return edges;
 }
 
 // The deferred in-place GEMM as column blocks: the operands are prepared once in the
 // workspace (the FFMA path's transposes, the TF32 path's hi/lo splits), then block j
-// computes C's columns [j w, (j + 1) w) on one of two streams, so a block's last wave
-// overlaps the next block's first.  Every output is computed as in the unsplit launch, so
+// computes C's columns [edges[j], edges[j + 1]) on one of two streams, so a block's last
+// wave overlaps the next block's first.  Every output is computed as in the unsplit launch, so
 // the results are bit-identical.
 Error Runtime::Impl::gemm_column_blocks(const GemmCall& call, const Alloc& A, const Alloc& B,
                                         const Alloc& C, uint64_t ws_va, uint64_t ws,
-                                        int64_t width) {
+                                        const std::vector<int64_t>& edges) {
   const GemmShape& s = call.shape;
   const int64_t m = static_cast<int64_t>(s.m), n = static_cast<int64_t>(s.n),
                 k = static_cast<int64_t>(s.k), ldc = static_cast<int64_t>(s.c.ld);
@@ -1069,8 +1087,9 @@ Error Runtime::Impl::gemm_column_blocks(const GemmCall& call, const Alloc& A, co
   staged_alloc = C.id;
   EventId last2 = 0;
   int64_t j = 0;
-  for (int64_t j0 = 0; j0 < n; j0 += width, ++j) {
-    const int64_t nj = std::min(width, n - j0);
+  for (; j + 1 < static_cast<int64_t>(edges.size()); ++j) {
+    const int64_t j0 = edges[static_cast<size_t>(j)];
+    const int64_t nj = edges[static_cast<size_t>(j) + 1] - j0;
     const StreamId st = (j & 1) ? s_compute2 : s_compute;
     const uint64_t col = s.c.offset_bytes + static_cast<uint64_t>(j0 * ldc) * 4;
     if (Error e = dev->gemm_block(prep, m, j0, nj, k, call.alpha, call.beta, C.va + col, ldc, st))
