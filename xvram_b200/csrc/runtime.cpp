@@ -71,6 +71,8 @@ struct Runtime::Impl {
   uint64_t capacity = 0; // frames the budget allows now
   uint64_t max_capacity = 0; // frames of the budget at open (the scratch range is this big)
   std::chrono::steady_clock::time_point last_budget_sample{};
+  bool queued_sample = false; // queued_free was sampled after the last operation's submit
+  uint64_t queued_free = 0;
   uint32_t growth_samples = 0;
   std::vector<Frame> frames;
   std::map<uint64_t, Alloc> allocs;
@@ -353,18 +355,26 @@ struct Runtime::Impl {
   // budget it opened with.  A lower figure releases frames at once (free ones first, then
   // least recently used ones, written back when dirty); a higher one is taken only after
   // three consecutive samples agree.
+  //
+  // cudaMemGetInfo usually returns in tens of microseconds but now and then takes
+  // milliseconds (up to tens), so an operation samples at its start only when no sample
+  // is younger than budget_poll_ms.  Otherwise it applies the sample taken after the
+  // previous operation had queued its device work (sample_after_submit), where that
+  // latency overlaps the kernels instead of delaying them.
   Error apply_budget(bool force) {
     const auto now = std::chrono::steady_clock::now();
-    if (!force && cfg.budget_poll_ms > 0 &&
-        now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms))
-      return {};
-    last_budget_sample = now;
     uint64_t free_b = 0, total_b = 0;
-    if (Error e = dev->mem_get_info(&free_b, &total_b))
-      return e;
-    ++t.budget_sample_count;
-    t.cuda_free_bytes_end = free_b;
-    t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, free_b);
+    if (!force && cfg.budget_poll_ms > 0 &&
+        now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms)) {
+      if (!queued_sample)
+        return {};
+      queued_sample = false;
+      free_b = queued_free;
+    } else {
+      queued_sample = false;
+      if (Error e = take_sample(now, &free_b, &total_b))
+        return e;
+    }
     const uint64_t reclaimable = free_b + static_cast<uint64_t>(frames.size()) * cb;
     const uint64_t after = reclaimable > cfg.headroom_bytes ? reclaimable - cfg.headroom_bytes : 0;
     const uint64_t target = std::max<uint64_t>(2, std::min(after / cb, max_capacity));
@@ -420,6 +430,32 @@ struct Runtime::Impl {
     } else {
       growth_samples = 0;
     }
+    return {};
+  }
+
+  Error take_sample(std::chrono::steady_clock::time_point now, uint64_t* free_b,
+                    uint64_t* total_b) {
+    last_budget_sample = now;
+    if (Error e = dev->mem_get_info(free_b, total_b))
+      return e;
+    ++t.budget_sample_count;
+    t.cuda_free_bytes_end = *free_b;
+    t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, *free_b);
+    return {};
+  }
+
+  // After an operation has queued its device work: sample free memory for the next
+  // operation's apply_budget once the last sample is half a poll interval old.
+  Error sample_after_submit() {
+    if (cfg.budget_poll_ms == 0)
+      return {}; // every operation samples at its start
+    const auto now = std::chrono::steady_clock::now();
+    if (now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms) / 2)
+      return {};
+    uint64_t total_b = 0;
+    if (Error e = take_sample(now, &queued_free, &total_b))
+      return e;
+    queued_sample = true;
     return {};
   }
 
@@ -943,6 +979,8 @@ Error Runtime::gemm(const GemmCall& call) {
   bool in_place = false;
   m.gemm_chunks(call, &keep, &ws, &in_place);
   Error err = in_place ? m.gemm_in_place(call, A, B, C, keep, ws) : m.gemm_streamed(call, A, B, C);
+  if (!err && in_place && call.defer_completion)
+    err = m.sample_after_submit(); // overlaps the kernels just queued
   m.x.last_gemm_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   m.t.last_transaction_ms = m.x.last_gemm_ms;
@@ -1394,7 +1432,7 @@ Error Runtime::prefetch(const std::vector<AccessRange>& ranges) {
       return e;
     m.frames[static_cast<size_t>(a.chunks[c].frame)].prefetched = true;
   }
-  return {};
+  return m.sample_after_submit(); // overlaps the uploads just queued
 }
 
 Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t workspace_bytes,

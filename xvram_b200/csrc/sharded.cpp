@@ -125,6 +125,12 @@ struct ShardGroup {
   uint64_t* plan_host = nullptr; // 2 x u64, page-locked
   bool aborted = false;
   std::mutex mu;
+  // Device memory this group may use (free + its own buffers), as sampled for the last
+  // call, with that call's shape: a repeat of the same shape within a second reuses it
+  // instead of calling cudaMemGetInfo, whose latency now and then reaches milliseconds.
+  uint64_t avail_sampled = 0;
+  uint64_t shape_sampled[6] = {};
+  std::chrono::steady_clock::time_point when_sampled{};
 
   static constexpr int kBuffers = 3 + 3 * kSlots + 1;
   Buffer* buffers[kBuffers] = {&a_canon,    &a_raw[0],   &a_raw[1],   &b_raw[0], &b_raw[1],
@@ -446,10 +452,19 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
                  K = static_cast<uint64_t>(k);
 
   // ---- 1. agree on the plan: max rows over ranks, min device memory available.
-  uint64_t free_b = 0, total_b = 0;
-  if (cudaError_t e = cudaMemGetInfo(&free_b, &total_b); e != cudaSuccess)
-    return cuda_status(e);
-  uint64_t avail = free_b + g->held_bytes() - g->plan_dev.bytes;
+  const uint64_t shape[6] = {M, N, K, op_a, op_b, static_cast<uint64_t>(panel_k)};
+  const auto now = std::chrono::steady_clock::now();
+  uint64_t avail = g->avail_sampled;
+  if (std::memcmp(shape, g->shape_sampled, sizeof shape) != 0 ||
+      now - g->when_sampled > std::chrono::seconds(1) || avail == 0) {
+    uint64_t free_b = 0, total_b = 0;
+    if (cudaError_t e = cudaMemGetInfo(&free_b, &total_b); e != cudaSuccess)
+      return cuda_status(e);
+    avail = free_b + g->held_bytes() - g->plan_dev.bytes;
+    g->avail_sampled = avail;
+    std::memcpy(g->shape_sampled, shape, sizeof shape);
+    g->when_sampled = now;
+  }
   avail = avail > kHeadroomBytes ? avail - kHeadroomBytes : 0;
   avail = std::min(avail, env_u64("XVRAM_B200_SHARD_BUDGET_BYTES", UINT64_MAX));
   g->plan_host[0] = M;
