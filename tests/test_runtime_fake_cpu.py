@@ -164,6 +164,42 @@ def test_live_budget_on_the_fake():
         assert s.telemetry().budget_grows >= 1
 
 
+def test_budget_sample_taken_after_submit_is_applied_by_the_next_operation():
+    """With a 400 ms poll: an operation whose last sample is over half a poll old samples
+    after queuing its work (not at its start); the next operation applies that sample,
+    even though free memory has changed since; only once no sample is younger than the
+    poll does an operation sample at its start and see the change."""
+    import time
+    with installed(free_bytes=64 * MiB) as fake, session(poll=400, headroom=0) as s:
+        blocks = [s.alloc(2 * MiB) for _ in range(12)]
+        for i, a in enumerate(blocks):
+            a.write(np.full(512 * 1024, float(i), dtype=np.float32))
+
+        def touch():
+            d = s.prefetch_desc([(blocks[-1], 0, 4096, sdk.READ)])
+            op = C.c_void_p()
+            s.check("prefetch", s.t.prefetch_submit(s.session, C.byref(d), C.byref(op)))
+            s.wait(op.value)
+            s.t.operation_release(op.value)
+
+        time.sleep(0.45)                    # half a poll since the sample at open
+        n0 = s.telemetry().budget_sample_count
+        touch()                             # samples after submitting (64 MiB free)
+        t1 = s.telemetry()
+        assert t1.budget_sample_count == n0 + 1
+        fake.fake_device_set_memory(0, 16 << 30)
+        touch()                             # applies the earlier sample: no shrink
+        t2 = s.telemetry()
+        assert t2.budget_sample_count == t1.budget_sample_count
+        assert t2.budget_shrinks == t1.budget_shrinks
+        time.sleep(0.45)                    # no sample younger than the poll now
+        touch()                             # samples at its start: shrinks
+        t3 = s.telemetry()
+        assert t3.budget_shrinks == t2.budget_shrinks + 1
+        for i, a in enumerate(blocks):
+            assert np.all(download(a, 512 * 1024)[::8192] == i)
+
+
 def test_injected_copy_failure_poisons_the_session():
     with installed() as fake, session() as s:
         a = s.alloc(4 * MiB)
