@@ -4,9 +4,12 @@
 
 #include <algorithm>
 #include <chrono>
+#include <condition_variable>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <set>
+#include <thread>
 #include <utility>
 
 namespace xvram {
@@ -71,8 +74,42 @@ struct Runtime::Impl {
   uint64_t capacity = 0; // frames the budget allows now
   uint64_t max_capacity = 0; // frames of the budget at open (the scratch range is this big)
   std::chrono::steady_clock::time_point last_budget_sample{};
-  bool queued_sample = false; // queued_free was sampled after the last operation's submit
-  uint64_t queued_free = 0;
+  // Free device memory sampled every budget_poll_ms by a thread of its own (see
+  // apply_budget): the latest figure and how many samples have been taken.
+  std::thread sampler;
+  std::mutex sample_mu;
+  std::condition_variable sample_cv;
+  bool sampler_stop = false;
+  uint64_t sampled_free = 0;
+  uint64_t sample_seq = 0;  // samples taken by the sampler thread
+  uint64_t applied_seq = 0; // the last of them apply_budget used
+
+  void sampler_loop() {
+    std::unique_lock<std::mutex> lk(sample_mu);
+    while (!sampler_stop) {
+      lk.unlock();
+      uint64_t f = 0, total = 0;
+      const bool ok = !dev->mem_get_info(&f, &total);
+      lk.lock();
+      if (ok) {
+        sampled_free = f;
+        ++sample_seq;
+      }
+      sample_cv.wait_for(lk, std::chrono::milliseconds(cfg.budget_poll_ms),
+                         [this] { return sampler_stop; });
+    }
+  }
+  ~Impl() { stop_sampler(); }
+  void stop_sampler() {
+    if (!sampler.joinable())
+      return;
+    {
+      std::lock_guard<std::mutex> lk(sample_mu);
+      sampler_stop = true;
+    }
+    sample_cv.notify_all();
+    sampler.join();
+  }
   uint32_t growth_samples = 0;
   std::vector<Frame> frames;
   std::map<uint64_t, Alloc> allocs;
@@ -356,25 +393,28 @@ struct Runtime::Impl {
   // least recently used ones, written back when dirty); a higher one is taken only after
   // three consecutive samples agree.
   //
-  // cudaMemGetInfo usually returns in tens of microseconds but now and then takes
-  // milliseconds (up to tens), so an operation samples at its start only when no sample
-  // is younger than budget_poll_ms.  Otherwise it applies the sample taken after the
-  // previous operation had queued its device work (sample_after_submit), where that
-  // latency overlaps the kernels instead of delaying them.
+  // With budget_poll_ms > 0 the samples come from a thread of their own, every
+  // budget_poll_ms, and an operation applies the newest one it has not applied yet:
+  // cudaMemGetInfo usually returns in tens of microseconds but now and then takes tens of
+  // milliseconds, which would otherwise stall the operation (and its kernels' launch).
+  // With 0, every operation samples inline; refresh_budget (force) always does.
   Error apply_budget(bool force) {
-    const auto now = std::chrono::steady_clock::now();
     uint64_t free_b = 0, total_b = 0;
-    if (!force && cfg.budget_poll_ms > 0 &&
-        now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms)) {
-      if (!queued_sample)
+    if (!force && cfg.budget_poll_ms > 0) {
+      std::lock_guard<std::mutex> lk(sample_mu);
+      if (sample_seq == applied_seq)
         return {};
-      queued_sample = false;
-      free_b = queued_free;
+      t.budget_sample_count += sample_seq - applied_seq;
+      applied_seq = sample_seq;
+      free_b = sampled_free;
     } else {
-      queued_sample = false;
-      if (Error e = take_sample(now, &free_b, &total_b))
+      if (Error e = dev->mem_get_info(&free_b, &total_b))
         return e;
+      ++t.budget_sample_count;
     }
+    last_budget_sample = std::chrono::steady_clock::now();
+    t.cuda_free_bytes_end = free_b;
+    t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, free_b);
     const uint64_t reclaimable = free_b + static_cast<uint64_t>(frames.size()) * cb;
     const uint64_t after = reclaimable > cfg.headroom_bytes ? reclaimable - cfg.headroom_bytes : 0;
     const uint64_t target = std::max<uint64_t>(2, std::min(after / cb, max_capacity));
@@ -430,32 +470,6 @@ struct Runtime::Impl {
     } else {
       growth_samples = 0;
     }
-    return {};
-  }
-
-  Error take_sample(std::chrono::steady_clock::time_point now, uint64_t* free_b,
-                    uint64_t* total_b) {
-    last_budget_sample = now;
-    if (Error e = dev->mem_get_info(free_b, total_b))
-      return e;
-    ++t.budget_sample_count;
-    t.cuda_free_bytes_end = *free_b;
-    t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, *free_b);
-    return {};
-  }
-
-  // After an operation has queued its device work: sample free memory for the next
-  // operation's apply_budget once the last sample is half a poll interval old.
-  Error sample_after_submit() {
-    if (cfg.budget_poll_ms == 0)
-      return {}; // every operation samples at its start
-    const auto now = std::chrono::steady_clock::now();
-    if (now - last_budget_sample < std::chrono::milliseconds(cfg.budget_poll_ms) / 2)
-      return {};
-    uint64_t total_b = 0;
-    if (Error e = take_sample(now, &queued_free, &total_b))
-      return e;
-    queued_sample = true;
     return {};
   }
 
@@ -583,6 +597,8 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
     m.allocs.emplace(kScratchId, std::move(scratch));
   }
   m.opened = true;
+  if (cfg.budget_poll_ms > 0)
+    m.sampler = std::thread([&m] { m.sampler_loop(); });
   return {};
 }
 
@@ -595,6 +611,7 @@ Error Runtime::close() {
     if (e && !first)
       first = e;
   };
+  m.stop_sampler();
   keep(m.dev->stream_sync(m.s_h2d));
   keep(m.dev->stream_sync(m.s_compute2));
   keep(m.dev->stream_sync(m.s_compute));
@@ -979,8 +996,6 @@ Error Runtime::gemm(const GemmCall& call) {
   bool in_place = false;
   m.gemm_chunks(call, &keep, &ws, &in_place);
   Error err = in_place ? m.gemm_in_place(call, A, B, C, keep, ws) : m.gemm_streamed(call, A, B, C);
-  if (!err && in_place && call.defer_completion)
-    err = m.sample_after_submit(); // overlaps the kernels just queued
   m.x.last_gemm_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   m.t.last_transaction_ms = m.x.last_gemm_ms;
@@ -1432,7 +1447,7 @@ Error Runtime::prefetch(const std::vector<AccessRange>& ranges) {
       return e;
     m.frames[static_cast<size_t>(a.chunks[c].frame)].prefetched = true;
   }
-  return m.sample_after_submit(); // overlaps the uploads just queued
+  return {};
 }
 
 Error Runtime::transaction(const std::vector<AccessRange>& ranges, uint64_t workspace_bytes,
