@@ -73,7 +73,6 @@ struct Runtime::Impl {
   uint64_t cb = 0;       // chunk bytes
   uint64_t capacity = 0; // frames the budget allows now
   uint64_t max_capacity = 0; // frames of the budget at open (the scratch range is this big)
-  std::chrono::steady_clock::time_point last_budget_sample{};
   // Free device memory sampled every budget_poll_ms by a thread of its own (see
   // apply_budget): the latest figure and how many samples have been taken.
   std::thread sampler;
@@ -412,7 +411,6 @@ struct Runtime::Impl {
         return e;
       ++t.budget_sample_count;
     }
-    last_budget_sample = std::chrono::steady_clock::now();
     t.cuda_free_bytes_end = free_b;
     t.cuda_free_bytes_minimum = std::min(t.cuda_free_bytes_minimum, free_b);
     const uint64_t reclaimable = free_b + static_cast<uint64_t>(frames.size()) * cb;
@@ -563,7 +561,6 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
     return make_error(XVRAM_STATUS_DEVICE_OUT_OF_MEMORY, "runtime", "open",
                       "device budget is smaller than two frames");
   m.max_capacity = m.capacity;
-  m.last_budget_sample = std::chrono::steady_clock::now();
   m.t.cache_target_bytes = m.capacity * m.cb;
   // Lowest and highest targets seen so far (reference src/residency/runtime.cpp:321,
   // :3415-3460).
