@@ -109,6 +109,42 @@ with installed() as fake:
         tel = api.telemetry()
         out["dirty_evictions"] = int(tel.runtime.dirty_evictions)
         out["streamed"] = int(cp.runtime_info().gemm_streamed)
+    elif mode == "misc":
+        # (1) C inside a larger allocation, after 3 MiB of other data: a read of the whole
+        # allocation mixes bytes outside the column blocks with the blocks themselves;
+        # (2) A and B freed before C is read; (3) a GEMM below two waves of tiles runs
+        # whole (no column blocks) but still returns before its kernel.
+        a, b = orc.uniform(m * k, 1), orc.uniform(k * n, 2)
+        c = orc.uniform(ldc * n, 3)
+        lead = orc.uniform(3 * 262144, 4)                     # 3 MiB before C
+        pa, pb = (api.malloc(x.nbytes) for x in (a, b))
+        pbig = api.malloc(lead.nbytes + c.nbytes + 4096)
+        api.h2d(pa, a.ctypes.data, a.nbytes)
+        api.h2d(pb, b.ctypes.data, b.nbytes)
+        api.h2d(pbig, lead.ctypes.data, lead.nbytes)
+        api.h2d(pbig + lead.nbytes, c.ctypes.data, c.nbytes)
+        pc = pbig + lead.nbytes
+        api.check("sgemm", api.sgemm(h, 0, 0, m, n, k, 0.5, pa, m, pb, k, 1.5, pc, ldc))
+        api.free(pa)
+        api.free(pb)
+        whole = np.empty((lead.nbytes + c.nbytes) // 4, np.float32)
+        api.d2h(whole.ctypes.data, pbig, whole.nbytes)
+        got = whole[lead.size:]
+        ref = orc.gemm(0, 0, m, n, k, 0.5, a, m, b, k, 1.5, c, ldc)
+        out["misc_err"] = float(normalized_error(got.reshape(n, ldc)[:, :m], ref, k, 1.0, 1.0))
+        out["lead_kept"] = bool(np.array_equal(whole[:lead.size], lead))
+        blocks_before = int(cp.runtime_info().gemm_column_blocks)
+        sm, sn, sk = 128, 256, 64                            # one tile: launched whole
+        x, y = orc.uniform(sm * sk, 5), orc.uniform(sk * sn, 6)
+        px, py, pz = api.malloc(x.nbytes), api.malloc(y.nbytes), api.malloc(sm * sn * 4)
+        api.h2d(px, x.ctypes.data, x.nbytes)
+        api.h2d(py, y.ctypes.data, y.nbytes)
+        api.check("sgemm", api.sgemm(h, 0, 0, sm, sn, sk, 1.0, px, sm, py, sk, 0.0, pz, sm))
+        z = np.empty(sm * sn, np.float32)
+        api.d2h(z.ctypes.data, pz, z.nbytes)
+        zref = orc.gemm(0, 0, sm, sn, sk, 1.0, x, sm, y, sk, 0.0, None, sm)
+        out["small_err"] = float(normalized_error(z.reshape(sn, sm), zref, sk, 1.0, 1.0))
+        out["small_blocks"] = int(cp.runtime_info().gemm_column_blocks) - blocks_before
     elif mode == "error":
         a, b, c = orc.uniform(m * k, 1), orc.uniform(k * n, 2), orc.uniform(ldc * n, 3)
         pa, pb, pc = (api.malloc(x.nbytes) for x in (a, b, c))
@@ -204,3 +240,13 @@ def test_narrow_first_and_last_blocks():
     r = d["results"]["10"]
     assert r["err"] <= TOLERANCE and r["pad_kept"]
     assert r["digest"] == s["results"]["10"]["digest"]
+
+
+def test_c_inside_a_larger_allocation_and_operands_freed_early():
+    """C at a 3 MiB offset of a larger allocation, A and B freed before C is read, the whole
+    allocation read at once (bytes outside the column blocks and the blocks together);
+    and a one-tile GEMM, which runs whole but still returns before its kernel."""
+    r = run("misc")
+    assert r["misc_err"] <= TOLERANCE and r["lead_kept"]
+    assert r["small_err"] <= TOLERANCE and r["small_blocks"] == 0
+    assert r["deferred"] == 2 and r["shutdown"] == 0
