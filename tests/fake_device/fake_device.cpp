@@ -332,7 +332,7 @@ public:
                           xvram::StreamId) override {
     if (should_fail("sgemm"))
       return injected("sgemm");
-    const xvram::GemmTypes t{xvram::kFp32, xvram::kFp32, p.compute};
+    const xvram::GemmTypes t{xvram::kFp32, xvram::kFp32, static_cast<int>(p.compute)};
     const uint64_t b = p.b + static_cast<uint64_t>(p.op_b == 0 ? n0 * p.ldb : n0) * 4;
     contract<float>(t, p.op_a, p.op_b, m, nj, k, alpha, p.a, p.lda, b, p.ldb, beta, c, ldc);
     ++gemms;
