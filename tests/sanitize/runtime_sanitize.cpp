@@ -15,6 +15,7 @@
 //   5. the live budget: a sampler thread polling every millisecond while free memory
 //      drops and comes back.
 // Exit status 0 means every check passed (and the sanitizers found nothing: they abort).
+// Argument "quick" shortens K (for ThreadSanitizer, which runs the loops ~10x slower).
 #include "device.hpp"
 #include "runtime.hpp"
 
@@ -35,6 +36,7 @@ namespace {
 using namespace xvram;
 
 int failures = 0;
+uint64_t k_scale = 1; // K divisor for a quick run
 
 void expect(bool ok, const char* what) {
   if (!ok) {
@@ -131,7 +133,7 @@ void gemms(bool deferred) {
   cfg.cache_target_bytes = 64ull << 20;
   if (!ok(rt.open(cfg, fake()), "open"))
     return;
-  const uint64_t m = 300, n = 700, k = 48, ldc = m + 3;
+  const uint64_t m = 300, n = 700, k = 48 / k_scale, ldc = m + 3;
   for (int op_a = 0; op_a < 2; ++op_a)
     for (int op_b = 0; op_b < 2; ++op_b) {
       const uint64_t lda = op_a ? k : m, ldb = op_b ? n : k;
@@ -171,7 +173,8 @@ void streamed_and_transaction() {
   cfg.cache_target_bytes = 16ull << 20;
   if (!ok(rt.open(cfg, fake()), "open"))
     return;
-  const uint64_t m = 2048, n = 2048, k = 256; // 20 MiB of operands: 10 chunks, 8 frames
+  // 2048 x 2048 C (16 MiB) plus A and B: more chunks than the 8 frames
+  const uint64_t m = 2048, n = 2048, k = 256 / k_scale;
   Matrix a = make(rt, m * k, 7), b = make(rt, k * n, 8), c = make(rt, m * n, 9);
   GemmCall call;
   call.shape.m = m;
@@ -242,7 +245,9 @@ void live_budget() {
 
 } // namespace
 
-int main() {
+int main(int argc, char** argv) {
+  if (argc > 1 && std::strcmp(argv[1], "quick") == 0)
+    k_scale = 4;
   gemms(false);
   gemms(true);
   streamed_and_transaction();
