@@ -1,5 +1,5 @@
 /*
- * xvram_cuda_compat.h -- the cudaMalloc/cudaMemcpy/cublasSgemm-style C table
+ * xvram/cuda_compat.h -- the cudaMalloc/cudaMemcpy/cublasSgemm-style C table
  * (B200 implementation).
  *
  * This is the drop-in boundary.  It is binary-compatible with the reference's

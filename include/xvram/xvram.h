@@ -1,5 +1,5 @@
 /*
- * xvram.h -- shared v1 ABI types of the xVRAM C interfaces (B200 implementation).
+ * xvram/xvram.h -- shared v1 ABI types of the xVRAM C interfaces (B200 implementation).
  *
  * Binary-compatible with the reference's include/xvram/xvram.h: every structure,
  * enumerator and macro below has the same name, value, field order and size as the

@@ -1,7 +1,7 @@
 /*
  * xvram_b200.h -- native entry points of the B200 implementation.
  *
- * The drop-in boundary is xvram_cuda_compat.h.  The functions here expose the pieces
+ * The drop-in boundary is xvram/cuda_compat.h.  The functions here expose the pieces
  * underneath it to callers that already manage device memory (the tile contraction on
  * raw device pointers) and to measurement and test harnesses (planner inspection,
  * validation, synthetic inputs, the FFMA peak probe).  All functions are plain C:
@@ -11,7 +11,7 @@
 #ifndef XVRAM_B200_H
 #define XVRAM_B200_H
 
-#include "xvram.h"
+#include "xvram/xvram.h"
 
 #if defined(__GNUC__) && defined(XVRAM_BUILDING_CUDA_COMPAT)
 #define XVRAM_B200_API __attribute__((visibility("default")))
@@ -87,8 +87,9 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
  * array compiled into the library, XVRAM_B200_NOALLOC_SCRATCH_BYTES large, which sits in
  * device memory on every GPU where the library's device code is loaded until the process
  * exits.  The call makes no cudaMalloc, cudaFree or other allocating call.  The caller
- * still provides A, B and C.  Arguments and results are those of xvram_b200_sgemm_device;
- * the device is the caller's current device.
+ * still provides A, B and C.  Arguments and results are those of xvram_b200_sgemm_device
+ * (bit-identical results), except that path XVRAM_B200_PATH_TF32X3 is not offered here
+ * and returns XVRAM_STATUS_INVALID_ARGUMENT; the device is the caller's current device.
  *
  * Limits: a problem that needs more scratch than the array
  * (xvram_b200_sgemm_workspace_bytes > XVRAM_B200_NOALLOC_SCRATCH_BYTES, for example a TN
@@ -97,8 +98,18 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
  * and it keeps whatever the last call left there; each call overwrites all the scratch it
  * reads, so nothing needs clearing, but calls that overlap on the GPU (different streams
  * without ordering, or different host threads) race on it and must be serialised by the
- * caller.  The first call on a device looks up the array's device address (and may load
- * the library's device code there); make that first call before any stream capture.
+ * caller.
+ *
+ * First call on a device: it looks up the array's device address (cudaGetSymbolAddress),
+ * which loads this library's device code, the array included, on that device.  Under
+ * CUDA's lazy module loading (the default) each kernel's code is also loaded at its first
+ * launch.  Those loads need device memory, so make the first call on each device -- with
+ * the shapes and operations you will use, since an empty problem returns before loading
+ * anything -- before your allocator takes the GPU's memory (or start the process with
+ * CUDA_MODULE_LOADING=EAGER); a load that finds no room fails the call with
+ * XVRAM_STATUS_DEVICE_OUT_OF_MEMORY.  Make that first call before any stream capture, and
+ * do not reset the device (cudaDeviceReset) afterwards: the address is kept for the life
+ * of the process.
  */
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_noalloc(
     uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
@@ -286,16 +297,6 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_bias_activation(uint64_t y, in
                                                                  uint64_t bias,
                                                                  uint32_t activation,
                                                                  uint64_t stream);
-
-/*
- * Testing seam (no reference counterpart, the role of the reference's fake driver tables in
- * tests/unit/residency_executor_fake_tests.cpp): sessions and the compat adapter created
- * after this call get their device from `create`, which returns a new object implementing
- * this library's internal C++ device interface (xvram_b200/csrc/device.hpp) built with
- * the same compiler -- the host-memory fake in tests/fake_device/.  NULL restores the CUDA
- * device.  Not for production use.
- */
-XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_test_set_device_factory(void* (*create)(void));
 
 /* Extra state of the compat adapter's runtime (not in the reference telemetry). */
 typedef struct xvram_b200_runtime_info_v1 {

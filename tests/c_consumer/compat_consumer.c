@@ -11,7 +11,7 @@
  * double-precision sum (|err| <= 1e-4 + 2e-5 |ref|), check that the padding rows of C
  * were not touched, then free everything and shut down.  Exit status 0 means all passed.
  */
-#include "xvram_cuda_compat.h"
+#include "xvram/cuda_compat.h"
 
 #include <math.h>
 #include <stdio.h>

@@ -12,7 +12,7 @@
  * each result checked element by element against a double (or long double) sum.  Exit
  * status 0 means both passed.
  */
-#include "xvram.h"
+#include "xvram/xvram.h"
 
 #include <math.h>
 #include <stdio.h>

@@ -16,6 +16,12 @@ if str(TESTS) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200 / sm_100a)")
+    # CPU runs bind the test link of the library, which adds the fake-device seam to the
+    # product exports; `-m gpu` runs bind the product library itself.
+    import os
+    if config.getoption("markexpr", "") != "gpu" and not os.environ.get("XVRAM_B200_LIBRARY"):
+        from fake_device import testing_library
+        os.environ["XVRAM_B200_LIBRARY"] = str(testing_library())
 
 
 @pytest.fixture(scope="session")

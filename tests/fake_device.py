@@ -2,7 +2,12 @@
 
 Test infrastructure: compiles the fake with g++ into tests/_build, loads it, and installs
 its factory into the library with xvram_b200_test_set_device_factory, so sessions and the
-compat adapter run the real runtime on host memory without a GPU."""
+compat adapter run the real runtime on host memory without a GPU.
+
+The product libraries do not export that seam.  The CPU suite therefore binds its own
+link of the same objects, tests/_build/libxvram_b200_testing.so (testing_library()),
+through XVRAM_B200_LIBRARY; tests/conftest.py arranges that for every run that is not
+`-m gpu`."""
 from __future__ import annotations
 
 import contextlib
@@ -14,6 +19,17 @@ TESTS = Path(__file__).resolve().parent
 ROOT = TESTS.parent
 SRC = TESTS / "fake_device" / "fake_device.cpp"
 OUT = TESTS / "_build" / "libxvram_fake_device.so"
+TESTING_LIB = TESTS / "_build" / "libxvram_b200_testing.so"
+
+
+def testing_library() -> Path:
+    """Links (if stale) the library objects with the seam exported, and returns the path."""
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    from xvram_b200 import build as b
+    b.build()
+    return b.link(TESTING_LIB, TESTS / "fake_device" / "testing.exports.map")
 
 
 def build() -> C.CDLL:
@@ -39,7 +55,10 @@ def build() -> C.CDLL:
 @contextlib.contextmanager
 def installed(free_bytes: int = 8 << 30, total_bytes: int = 16 << 30):
     """Within the block, new sessions (and a new compat adapter) use the fake device."""
-    from xvram_b200._native import lib
+    import pytest
+    from xvram_b200._native import has_test_seam, lib
+    if not has_test_seam(lib):
+        pytest.skip("needs the test link of the library (XVRAM_B200_LIBRARY, tests/conftest.py)")
     fake = build()
     fake.fake_device_set_memory(free_bytes, total_bytes)
     fake.fake_device_fail(b"", -1)

@@ -5,11 +5,8 @@
 #include <stddef.h>
 #include <stdio.h>
 #include <string.h>
-#ifdef XVRAM_DUMP_REFERENCE
+/* Both header sets are found as <xvram/...> through -I. */
 #include <xvram/cuda_compat.h>
-#else
-#include "xvram_cuda_compat.h"
-#endif
 
 static int first = 1;
 static void sep(void) { printf(first ? "\n" : ",\n"); first = 0; }

@@ -3,8 +3,9 @@
 
     python tests/golden/make_abi_layout.py [/path/to/reference]
 
-Compiles abi_layout_dump.c against <reference>/include (XVRAM_DUMP_REFERENCE) and
-stores what it prints.  tests/test_abi_layout.py compiles the same program against
+Compiles abi_layout_dump.c against <reference>/include and stores what it prints.  The
+reference directory defaults to XVRAM_REFERENCE_DIR, else `reference` beside this
+repository.  tests/test_abi_layout.py compiles the same program against
 this repository's include/ and requires identical output.
 """
 from __future__ import annotations
@@ -28,8 +29,10 @@ def dump(include_args: list[str], defines: list[str]) -> dict:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-    layout = dump(["-I", str(ref / "include")], ["-DXVRAM_DUMP_REFERENCE"])
+    sys.path.insert(0, str(HERE.parent))
+    from reference_tree import reference_dir
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_dir()
+    layout = dump(["-I", str(ref / "include")], [])
     (HERE / "abi_layout.json").write_text(json.dumps(layout, indent=1, sort_keys=True) + "\n")
     print(f"{len(layout)} entries")
 

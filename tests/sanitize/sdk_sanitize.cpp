@@ -17,7 +17,7 @@
 //   * a prefetch, then every release and the session close.
 // Results are checked against double-precision loops.  Exit status 0 means all passed.
 #include "device.hpp"
-#include "xvram.h"
+#include "xvram/xvram.h"
 
 #include <cmath>
 #include <cstdio>

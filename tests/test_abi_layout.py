@@ -38,7 +38,7 @@ def test_headers_compile_as_c_and_cpp(tmp_path):
     import subprocess
     src = tmp_path / "consumer.c"
     src.write_text(
-        '#include "xvram_cuda_compat.h"\n#include "xvram_b200.h"\n'
+        '#include <xvram/cuda_compat.h>\n#include "xvram_b200.h"\n'
         "int main(void){xvram_cuda_compat_config_v1 c = XVRAM_CUDA_COMPAT_CONFIG_V1_INIT;\n"
         "xvram_error_info_v1 e = XVRAM_ERROR_INFO_V1_INIT; (void)e;\n"
         "return c.session.chunk_size_bytes == 67108864u ? 0 : 1;}\n")

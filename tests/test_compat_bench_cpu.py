@@ -22,8 +22,10 @@ from schema_check import check
 
 from xvram_b200 import compat_bench
 
-SCHEMA = Path("/root/reference/schemas/cuda-compat-v1.schema.json")
-TRACE_SCHEMA = Path("/root/reference/schemas/cuda-compat-trace-v1.schema.json")
+from reference_tree import reference_dir
+
+SCHEMA = reference_dir() / "schemas" / "cuda-compat-v1.schema.json"
+TRACE_SCHEMA = reference_dir() / "schemas" / "cuda-compat-trace-v1.schema.json"
 
 SCRIPT = r"""
 import json, sys

@@ -20,7 +20,9 @@ from schema_check import check
 from xvram_b200 import gemm_bench
 
 MiB = 1 << 20
-SCHEMA = Path("/root/reference/schemas/gemm-bench-report-v1.schema.json")
+from reference_tree import reference_dir
+
+SCHEMA = reference_dir() / "schemas" / "gemm-bench-report-v1.schema.json"
 
 
 def test_pattern_closed_form_matches_the_oracle():

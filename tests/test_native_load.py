@@ -1,4 +1,5 @@
-"""The native library loads without a GPU and exports every symbol include/*.h declares."""
+"""The native library loads without a GPU and exports every symbol include/ declares; the
+two drop-in libraries export exactly what the reference's libraries do."""
 from __future__ import annotations
 
 import re
@@ -10,40 +11,58 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def declared_symbols() -> set[str]:
     names = set()
-    for h in (ROOT / "include").glob("*.h"):
+    for h in (ROOT / "include").rglob("*.h"):
         text = h.read_text()
         # function declarations: an API macro, return type, XVRAM_CALL, then the name
         names |= set(re.findall(r"XVRAM_CALL\s*\n?\s*(xvram_[a-z0-9_]+)\s*\(", text))
     return names
 
 
-def test_library_exports_every_declared_symbol():
-    from xvram_b200 import _native
-    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)],
+def _exports(path: Path) -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(path)],
                          capture_output=True, text=True, check=True).stdout
-    exported = {line.split()[-1].split("@")[0] for line in out.splitlines() if " T " in line}
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_library_exports_every_declared_symbol():
+    """libxvram_b200.so exports exactly the declarations of include/, each at its
+    version node; the test-only fake-device seam is not among them."""
+    from xvram_b200 import _native
+    exported = _exports(_native.PRODUCT_LIB_PATH)
+    names = {s.split("@")[0] for s in exported}
     declared = declared_symbols()
     assert declared, "no declarations found"
-    assert declared <= exported, declared - exported
+    assert names == declared, names ^ declared
     assert set(_native.EXPORTED) == declared
-    # nothing else leaks out of the library
-    assert {s for s in exported if not s.startswith("xvram_")} == set()
+    assert "xvram_b200_test_set_device_factory" not in names
+    nodes = {s.split("@@")[0]: s.split("@@")[1] for s in exported}
+    assert nodes.pop("xvram_cuda_compat_get_api") == "XVRAM_CUDA_COMPAT_1.0"
+    assert nodes.pop("xvram_get_api") == "XVRAM_0.1"
+    assert set(nodes.values()) == {"XVRAM_B200_1.0"}
+
+
+def test_compat_library_exports_only_the_compat_table():
+    """libxvram_cuda_compat.so is the compat drop-in: like the reference's compat library
+    (cmake/cuda_compat.exports.map) it exports xvram_cuda_compat_get_api alone, under the
+    version node XVRAM_CUDA_COMPAT_1.0."""
+    from xvram_b200 import _native
+    assert _exports(_native.COMPAT_LIB_PATH) == {
+        "xvram_cuda_compat_get_api@@XVRAM_CUDA_COMPAT_1.0"}
 
 
 def test_sdk_library_exports_only_xvram_get_api():
     """libxvram.so is the SDK drop-in: like the reference's SDK library it exports
     xvram_get_api alone, under the version node XVRAM_0.1."""
     from xvram_b200 import _native
-    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.SDK_LIB_PATH)],
-                         capture_output=True, text=True, check=True).stdout
-    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    exported = _exports(_native.SDK_LIB_PATH)
     assert exported == {"xvram_get_api@@XVRAM_0.1"}, exported
 
 
 def test_library_has_no_cuda_runtime_dependency():
     from xvram_b200 import _native
-    out = subprocess.run(["ldd", str(_native.LIB_PATH)], capture_output=True, text=True).stdout
-    assert "libcudart" not in out  # static runtime; only the driver is needed at run time
+    for path in (_native.PRODUCT_LIB_PATH, _native.COMPAT_LIB_PATH, _native.SDK_LIB_PATH):
+        out = subprocess.run(["ldd", str(path)], capture_output=True, text=True).stdout
+        assert "libcudart" not in out  # static runtime; only the driver is needed at run time
 
 
 def test_get_api_contract_without_gpu():

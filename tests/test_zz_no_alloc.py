@@ -5,16 +5,18 @@ whose allocator already owns all device memory, code inside that allocator's cal
 plugins limited to memory their host hands in).  Its scratch is a fixed array inside the
 library, shared by every call.  These tests call it through the C ABI twice in a row on
 different problems -- the second call finds the first call's leftovers in the array -- and
-compare each result with the allocating entry point xvram_b200_sgemm_device, within the
-tolerance the other parity tests use.  The file sorts last so that a run that stops at the
-first failure has already run every other test; it also passes on its own.
+require each result to be bit-identical to the allocating entry point
+xvram_b200_sgemm_device (both run the same transposes and kernel) and within the SGEMM
+tolerance of the CPU FP64 oracle.  After the first call, a further call must not change
+the device's free memory.  The file sorts last so that a run that stops at the first
+failure has already run every other test; it also passes on its own.
 """
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
-from oracle_lib import TOLERANCE, load_oracle
+from oracle_lib import TOLERANCE, load_oracle, normalized_error
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -24,15 +26,17 @@ if not torch.cuda.is_available():  # pragma: no cover
 from xvram_b200 import device  # noqa: E402
 from xvram_b200._native import lib  # noqa: E402
 
+INVALID_ARGUMENT = 1
 BUDGET_PRESSURE = 7
 SCRATCH_BYTES = 32 << 20
+PATH_TF32X3 = 3
 
 
-def noalloc(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc) -> int:
+def noalloc(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, path=0) -> int:
     stream = torch.cuda.current_stream().cuda_stream
     return lib.xvram_b200_sgemm_device_noalloc(op_a, op_b, m, n, k, alpha, A.data_ptr(), lda,
                                                B.data_ptr(), ldb, beta, C.data_ptr(), ldc, stream,
-                                               0)
+                                               path)
 
 
 def problem(orc, op_a, op_b, m, n, k, seed):
@@ -44,7 +48,7 @@ def problem(orc, op_a, op_b, m, n, k, seed):
     return a, ra, b, rb, c
 
 
-def test_two_calls_in_a_row_match_the_allocating_entry_point():
+def test_two_calls_in_a_row_match_the_allocating_entry_point_and_the_oracle():
     orc = load_oracle()
     cases = [(1, 0, 1000, 900, 1100, 0.5, 1.5, 70),   # TN: both operands transposed
              (0, 0, 777, 555, 333, -1.0, 0.25, 80)]   # NN: only B, fewer bytes than call 1
@@ -58,10 +62,37 @@ def test_two_calls_in_a_row_match_the_allocating_entry_point():
         assert device.sgemm(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, C_ref, m) == 0
         assert noalloc(op_a, op_b, m, n, k, alpha, A, lda, B, ldb, beta, C_new, m) == 0
         assert device.kernel_status() == 0
-        want = C_ref.cpu().numpy().astype(np.float64)
-        got = C_new.cpu().numpy().astype(np.float64)
-        err = float(np.max(np.abs(got - want))) / (k * float(np.abs(a).max()) * float(np.abs(b).max()))
+        want = C_ref.cpu().numpy()
+        got = C_new.cpu().numpy()
+        # Same transposes, same kernel: the results agree bit for bit.
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        ref = orc.gemm(op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, m)
+        err = normalized_error(got, ref, k, float(np.abs(a).max()), float(np.abs(b).max()))
         assert err <= TOLERANCE, err
+
+
+def test_a_call_after_the_first_takes_no_device_memory():
+    orc = load_oracle()
+    m, n, k = 1024, 768, 1536                       # TN: 10.5 MiB of scratch
+    a, lda, b, ldb, c = problem(orc, 1, 0, m, n, k, 90)
+    A, B, C = (torch.from_numpy(x).cuda() for x in (a, b, c))
+    assert noalloc(1, 0, m, n, k, 1.0, A, lda, B, ldb, 0.0, C, m) == 0   # first call: loads
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        assert noalloc(1, 0, m, n, k, 1.0, A, lda, B, ldb, 0.5, C, m) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert device.kernel_status() == 0
+
+
+def test_tensor_core_path_is_not_offered():
+    A = torch.zeros((64, 64), device="cuda")
+    C = torch.full((64, 64), 2.0, device="cuda")
+    assert noalloc(0, 0, 64, 64, 64, 1.0, A, 64, A, 64, 0.0, C, 64, path=PATH_TF32X3) == \
+        INVALID_ARGUMENT
+    torch.cuda.synchronize()
+    assert bool((C == 2.0).all())
 
 
 def test_problem_larger_than_the_scratch_array_is_refused():

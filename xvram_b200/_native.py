@@ -1,17 +1,26 @@
-"""ctypes binding of the native library (xvram_b200/lib/libxvram_cuda_compat.so).
+"""ctypes binding of the native library (xvram_b200/lib/libxvram_b200.so).
 
 The library is the product: there is no Python or CPU fallback.  Importing this
 module without the built library raises immediately; build it with
 ``python -m xvram_b200.build`` (``__graft_entry__.build()`` does the same).
+
+``XVRAM_B200_LIBRARY`` in the environment names another build of the same objects to
+bind instead; the CPU test suite uses it for its link that also exports the
+host-memory fake device seam.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxvram_cuda_compat.so"
-# The same code linked as the SDK drop-in (exports xvram_get_api only).
-SDK_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxvram.so"
+_LIB_DIR = Path(__file__).resolve().parent / "lib"
+PRODUCT_LIB_PATH = _LIB_DIR / "libxvram_b200.so"
+LIB_PATH = Path(os.environ.get("XVRAM_B200_LIBRARY") or PRODUCT_LIB_PATH)
+# The same code linked as the two drop-ins: the compat library exports
+# xvram_cuda_compat_get_api only, the SDK library xvram_get_api only.
+COMPAT_LIB_PATH = _LIB_DIR / "libxvram_cuda_compat.so"
+SDK_LIB_PATH = _LIB_DIR / "libxvram.so"
 
 u32, u64, i32, i64 = C.c_uint32, C.c_uint64, C.c_int32, C.c_int64
 f32, f64 = C.c_float, C.c_double
@@ -127,9 +136,19 @@ def _load() -> C.CDLL:
     lib.xvram_b200_digest_compat.restype = None
     lib.xvram_b200_device_query.argtypes = [i32, C.POINTER(DeviceInfo)]
     lib.xvram_b200_device_query.restype = u32
-    lib.xvram_b200_test_set_device_factory.argtypes = [vp]
-    lib.xvram_b200_test_set_device_factory.restype = u32
+    if has_test_seam(lib):
+        lib.xvram_b200_test_set_device_factory.argtypes = [vp]
+        lib.xvram_b200_test_set_device_factory.restype = u32
     return lib
+
+
+def has_test_seam(handle: C.CDLL) -> bool:
+    """True for the test suite's link, which exports the fake-device seam."""
+    try:
+        handle.xvram_b200_test_set_device_factory
+    except AttributeError:
+        return False
+    return True
 
 
 lib = _load()
@@ -139,7 +158,6 @@ EXPORTED = (
     "xvram_cuda_compat_get_api",
     "xvram_get_api",
     "xvram_b200_bias_activation",
-    "xvram_b200_test_set_device_factory",
     "xvram_b200_device_query",
     "xvram_b200_digest_bench",
     "xvram_b200_digest_compat",

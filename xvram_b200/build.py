@@ -1,12 +1,20 @@
-"""Builds the native library xvram_b200/lib/libxvram_cuda_compat.so for sm_100a.
+"""Builds the native libraries under xvram_b200/lib for sm_100a.
 
     python -m xvram_b200.build            # incremental
     python -m xvram_b200.build --clean
 
+One set of objects is linked three times, each with its own export list:
+
+* libxvram_b200.so        the native library (compat table, SDK table, xvram_b200_*);
+                          the Python package binds this one.
+* libxvram_cuda_compat.so the compat drop-in: exports xvram_cuda_compat_get_api alone,
+                          at version node XVRAM_CUDA_COMPAT_1.0, as the reference's does.
+* libxvram.so             the SDK drop-in: exports xvram_get_api alone (XVRAM_0.1).
+
 Every CUDA source is compiled with `-gencode arch=compute_100a,code=sm_100a`; host
-sources with g++ -std=c++20.  The library links the CUDA runtime statically and
-resolves driver entry points at run time, so it only needs libcuda.so.1 from the
-driver on the machine that loads it.
+sources with g++ -std=c++20.  The libraries link the CUDA runtime statically and
+resolve driver entry points at run time, so they only need libcuda.so.1 from the
+driver on the machine that loads them.
 """
 from __future__ import annotations
 
@@ -21,9 +29,12 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
-LIB = PKG / "lib" / "libxvram_cuda_compat.so"
-# The same objects linked as the SDK drop-in: exports xvram_get_api only.
+LIB = PKG / "lib" / "libxvram_b200.so"
+COMPAT_LIB = PKG / "lib" / "libxvram_cuda_compat.so"
 SDK_LIB = PKG / "lib" / "libxvram.so"
+# (library, export map in csrc/)
+LINKS = ((LIB, "native.exports.map"), (COMPAT_LIB, "compat.exports.map"),
+         (SDK_LIB, "sdk.exports.map"))
 INCLUDE = ROOT / "include"
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.environ.get("NVCC", f"{CUDA_HOME}/bin/nvcc")
@@ -40,7 +51,7 @@ def _sources():
 
 
 def _headers_mtime() -> float:
-    hs = list(CSRC.glob("*.hpp")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    hs = list(CSRC.glob("*.hpp")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.rglob("*.h"))
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 
@@ -71,17 +82,33 @@ def build(verbose: bool = False) -> Path:
         if verbose:
             print(" ".join(cmd))
         _run(cmd)
-    newest = max(o.stat().st_mtime for o in objs)
-    for lib, script in ((LIB, "exports.map"), (SDK_LIB, "sdk.exports.map")):
-        if lib.exists() and lib.stat().st_mtime >= max(newest, (CSRC / script).stat().st_mtime):
-            continue
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC",
-               f"-Xlinker=--version-script={CSRC / script}", "-Xlinker=--no-undefined",
-               *map(str, objs), "-o", str(lib), "-lpthread", "-ldl", "-lrt"]
-        if verbose:
-            print(" ".join(cmd))
-        _run(cmd)
+    for lib, script in LINKS:
+        link(lib, CSRC / script, objs, verbose)
     return LIB
+
+
+def objects() -> list[Path]:
+    """The compiled objects every library is linked from (after build())."""
+    cu, cpp = _sources()
+    return [BUILD / (src.name + ".o") for src in cu + cpp]
+
+
+def link(lib: Path, export_map: Path, objs: list[Path] | None = None,
+         verbose: bool = False) -> Path:
+    """Links `objs` (default: all objects) into `lib` with the given version script,
+    unless `lib` is newer than both."""
+    objs = objects() if objs is None else objs
+    newest = max(max(o.stat().st_mtime for o in objs), export_map.stat().st_mtime)
+    if lib.exists() and lib.stat().st_mtime >= newest:
+        return lib
+    lib.parent.mkdir(parents=True, exist_ok=True)
+    cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC",
+           f"-Xlinker=--version-script={export_map}", "-Xlinker=--no-undefined",
+           *map(str, objs), "-o", str(lib), "-lpthread", "-ldl", "-lrt"]
+    if verbose:
+        print(" ".join(cmd))
+    _run(cmd)
+    return lib
 
 
 def main() -> None:
@@ -91,7 +118,7 @@ def main() -> None:
     a = ap.parse_args()
     if a.clean:
         shutil.rmtree(BUILD, ignore_errors=True)
-        for lib in (LIB, SDK_LIB):
+        for lib, _ in LINKS:
             if lib.exists():
                 lib.unlink()
     print(build(a.verbose))

@@ -14,7 +14,7 @@
 // Calls are serialised by a mutex and run on the calling thread; the caller's current
 // CUDA device is restored on return.
 #include "xvram_b200.h"
-#include "xvram_cuda_compat.h"
+#include "xvram/cuda_compat.h"
 
 #include "device.hpp"
 #include "runtime.hpp"

@@ -466,8 +466,7 @@ xvram_b200_device_query(int32_t ordinal, xvram_b200_device_info_v1* out) {
   return XVRAM_STATUS_SUCCESS;
 }
 
-extern "C" XVRAM_B200_API xvram_status XVRAM_CALL
-xvram_b200_test_set_device_factory(void* (*create)(void)) {
+extern "C" xvram_status xvram_b200_test_set_device_factory(void* (*create)(void)) {
   xvram::g_external_factory = create;
   xvram::device_factory() = create ? &xvram::external_factory : &xvram::default_factory;
   return XVRAM_STATUS_SUCCESS;

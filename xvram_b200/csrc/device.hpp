@@ -126,3 +126,12 @@ std::unique_ptr<Device> make_cuda_device();
 DeviceFactory& device_factory();
 
 } // namespace xvram
+
+// Testing seam (the role of the reference's fake driver tables in
+// tests/unit/residency_executor_fake_tests.cpp): sessions and the compat adapter created
+// after this call get their device from `create`, which returns a new object implementing
+// the Device interface above, built with the same compiler -- the host-memory fake in
+// tests/fake_device/.  NULL restores the CUDA device.  The product libraries do not export
+// it; only the test suite's own link of the same objects does.
+extern "C" __attribute__((visibility("default"))) xvram_status
+xvram_b200_test_set_device_factory(void* (*create)(void));

@@ -31,7 +31,9 @@ std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of noalloc_scratch on the current device; the first call per device looks
-// it up (this may load the library's device code on that device).
+// it up (this may load the library's device code on that device).  The address is cached
+// for the life of the process, so a cudaDeviceReset of that device afterwards is not
+// supported (the next call would use the old context's address).
 cudaError_t scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -62,6 +64,8 @@ xvram_status status_of(cudaError_t e) {
   case cudaErrorInvalidDevice:
   case cudaErrorInsufficientDriver:
     return XVRAM_STATUS_UNAVAILABLE;
+  case cudaErrorMemoryAllocation: // loading the device code (and the array) found no room
+    return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
   default:
     return XVRAM_STATUS_CUDA_ERROR;
   }

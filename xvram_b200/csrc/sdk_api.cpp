@@ -21,7 +21,7 @@
 //     the three-term TF32 tensor-core kernel, which is FP32-accurate where the
 //     reference's single-pass TF32 is not.
 //   * Tile hints are ignored: the panel planner picks the geometry from the budget.
-#include "xvram.h"
+#include "xvram/xvram.h"
 
 #include "device.hpp"
 #include "runtime.hpp"

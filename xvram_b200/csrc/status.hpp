@@ -5,7 +5,7 @@
 // (reference include/xvram/xvram.h:87-97).
 #pragma once
 
-#include "xvram.h"
+#include "xvram/xvram.h"
 
 #include <cstdint>
 #include <cstring>
