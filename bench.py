@@ -93,12 +93,16 @@ def cpu_reference_rate(threads: int, target_s: float):
     return kind, desc, run, count
 
 
-def cpu_baseline_obj(threads: int, target_s: float = 10.0) -> dict:
+def cpu_baseline_obj(threads: int, target_s: float = 30.0) -> dict:
+    """The whole C2 output (50.3 M outputs, 412 GFLOP) when the host does it within
+    `target_s` (about 10 s on 16 cores), else the largest sample that fits."""
     kind, desc, run, count = cpu_reference_rate(threads, target_s)
     dt = run(count)
     flop = 2.0 * K * count
+    whole = "all" if count == M * N else f"a sample of {count}"
     return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-            "sample": f"{desc}: {count} of {M * N} outputs ({flop / 1e9:.1f} GFLOP) in {dt:.1f} s"}
+            "sample": f"{desc}: {whole} of {M * N} outputs ({flop / 1e9:.1f} GFLOP) in "
+                      f"{dt:.1f} s"}
 
 
 def run_reference_arm(args) -> None:
@@ -221,106 +225,230 @@ class ClockSampler:
                 "interval_ms": self.interval_ms}
 
 
-# ---------------------------------------------------------------- out-of-core workload
-def run_out_of_core(args) -> None:
-    """One streamed GEMM through the compat ABI with operands far above the device budget
-    (BASELINE config 3 scaled to the host's memory: NT, alpha 1, beta 1, n^3 with n =
-    --ooc-n, budget --ooc-budget-gib).  Reports the blas_sgemm time, the host-link bytes it
-    moved, eviction / frame-reuse counters and the fraction of
-    max(FLOP / P_fp32, algorithmic H2D bytes / BW_h2d, C bytes / BW_d2h)."""
+# ---------------------------------------------------------------- out-of-core workloads
+def _rows_of(seed: int, n: int, first: int, count: int) -> "np.ndarray":
+    """Rows [first, first + count) across all n columns of the n x n column-major matrix
+    drawn from `seed` (element (i, k) is draw i + k n of the counter-based stream), as a
+    (count, n) float64 array -- recomputed, not read back."""
     import numpy as np
-    import torch
+    from xvram_b200 import device as xd
+    out = np.empty((n, count), np.float32)
+    for kk in range(n):
+        xd.fill_uniform(out[kk], seed, first_index=first + kk * n, threads=1)
+    return out.T.astype(np.float64)
+
+
+def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2d_gbs: float,
+                   d2h_gbs: float, device_ordinal: int = 0) -> dict:
+    """One or more streamed GEMMs through the compat ABI with operands far above the device
+    budget (BASELINE config 3's form: NT, alpha 1, beta 1, n^3, cache_target_bytes =
+    budget): the operands are written through memcpy(H2D) into the adapter's host backing
+    (256 MiB at a time, no full host copies), then each blas_sgemm call is timed on the host
+    clock up to its completion (XVRAM_B200_SYNC_GEMM is not needed: a streamed GEMM
+    completes before the call returns).  No warm-up: the first call pays the plan and the
+    frame pool, as a caller's would.  Parity: a 64 x 64 block of C is read back and checked
+    against an FP64 recomputation of the same block from the seeded generators."""
+    import numpy as np
 
     from xvram_b200 import compat as cp
     from xvram_b200 import device as xd
 
-    n = args.ooc_n
-    budget = int(args.ooc_budget_gib * (1 << 30))
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    stream = torch.cuda.Stream(device=dev)
-    peak_tflops, probes = measure_fp32_peak(dev, stream)
-    h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
-
+    seeds = (100, 101, 102)
+    budget = int(budget_gib * (1 << 30))
     api = cp.CompatApi()
     cfg = cp.compat_config_init()
     cfg.session.cache_target_bytes = budget
+    cfg.session.device_ordinal = device_ordinal
     api.check("initialize", api.initialize(cfg))
-    arrs = []
-    for seed in (100, 101, 102):
-        x = np.empty((n, n), np.float32)
-        xd.fill_uniform(x, seed)
-        arrs.append(x)
+    stage = np.empty(64 << 20, np.float32)
     ptrs = []
-    for x in arrs:
-        d = api.malloc(x.nbytes)
-        api.h2d(d, x.ctypes.data, x.nbytes)
+    t_fill = time.perf_counter()
+    for seed in seeds:
+        d = api.malloc(n * n * 4)
+        for off in range(0, n * n, stage.size):
+            cnt = min(stage.size, n * n - off)
+            xd.fill_uniform(stage[:cnt], seed, first_index=off)
+            api.h2d(d + 4 * off, stage.ctypes.data, 4 * cnt)
         ptrs.append(d)
+    t_fill = time.perf_counter() - t_fill
+    del stage
     h = api.blas_create()
     flop = 2.0 * n ** 3
     times, moved = [], []
-    with ClockSampler(0, 200) as clocks:
-        for _ in range(max(args.steps, 1)):
+    with ClockSampler(device_ordinal, 200) as clocks:
+        for _ in range(max(steps, 1)):
             t0 = api.telemetry().runtime
             b0 = (t0.bytes_h2d, t0.bytes_d2h)
             start = time.perf_counter()
             api.check("sgemm", api.sgemm(h, 0, 1, n, n, n, 1.0, ptrs[0], n, ptrs[1], n, 1.0,
                                          ptrs[2], n))
+            api.check("synchronize", api.t.synchronize())
             times.append(time.perf_counter() - start)
             t1 = api.telemetry().runtime
             moved.append((t1.bytes_h2d - b0[0], t1.bytes_d2h - b0[1]))
+    # parity on a 64 x 64 block (C = C0 + calls * A B^T in exact arithmetic)
+    s, i0, j0 = 64, (n // 3) // 64 * 64, (2 * n // 3) // 64 * 64
+    got = np.empty((s, s), np.float32)                       # [j, i]
+    for jj in range(s):
+        api.d2h(got[jj].ctypes.data, ptrs[2] + 4 * (i0 + (j0 + jj) * n), 4 * s)
+    a_rows = _rows_of(seeds[0], n, i0, s)                    # A[i0.., :]
+    b_rows = _rows_of(seeds[1], n, j0, s)                    # op(B)[:, j0..] = B[j0.., :]^T
+    c0 = np.empty((s, s), np.float32)
+    for jj in range(s):
+        xd.fill_uniform(c0[jj], seeds[2], first_index=i0 + (j0 + jj) * n, threads=1)
+    want = c0.astype(np.float64).T + len(times) * (a_rows @ b_rows.T)   # [i, j]
+    err = float(np.max(np.abs(got.T.astype(np.float64) - want))) / (len(times) * n)
     tel = api.telemetry()
     info = cp.runtime_info()
+    for d in ptrs:
+        api.free(d)
+    api.blas_destroy(h)
     api.shutdown()
     sec = min(times)
     h2d_b, d2h_b = moved[times.index(sec)]
     alg_h2d = 3 * n * n * 4          # A + B + C_in, each once
     alg_d2h = n * n * 4              # C_out
-    t_roof = max(flop / (peak_tflops * 1e12), alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
-    line = {
-        "metric": METRIC, "workload": f"C3 scaled: {n}^3 NT alpha 1 beta 1, {n * n * 4 >> 30} GiB "
-                                      f"per operand, device budget {args.ooc_budget_gib} GiB",
-        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": len(times),
-        "ms_per_step": 1e3 * sec, "dtype": "f32", "data": "synthetic",
+    t_fp32 = flop / (peak_tflops * 1e12)
+    t_roof = max(t_fp32, alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
+    rt = tel.runtime
+    return {
+        "workload": f"C3 form, out of core through the compat ABI: {n}^3 NT alpha 1 beta 1, "
+                    f"{n * n * 4 >> 30} GiB per operand, device budget {budget_gib:g} GiB, 1 GPU",
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "steps": len(times), "warmup": 0,
+        "ms_per_step": 1e3 * sec, "step_ms": [round(1e3 * t, 1) for t in times],
+        "operand_bytes_over_budget": 3 * n * n * 4 / budget,
         "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
-                     "p_fp32_tflops": peak_tflops, "fp32_probes": probes, "h2d_gbs": h2d_gbs,
-                     "d2h_gbs": d2h_gbs,
-                     "bound": "fp32" if flop / (peak_tflops * 1e12) >= alg_h2d / (h2d_gbs * 1e9)
-                     else "host-link"},
-        "host_link": {"h2d_bytes": h2d_b, "d2h_bytes": d2h_b,
+                     "bound": "fp32" if t_fp32 >= alg_h2d / (h2d_gbs * 1e9) else "host-link",
+                     "p_fp32_tflops": peak_tflops, "h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs},
+        "host_link": {"h2d_bytes": h2d_b, "d2h_bytes": d2h_b, "algorithmic_h2d_bytes": alg_h2d,
                       "h2d_over_algorithmic": h2d_b / alg_h2d,
-                      "achieved_h2d_gbs": h2d_b / sec / 1e9},
+                      "achieved_h2d_gbs": h2d_b / sec / 1e9,
+                      "achieved_d2h_gbs": d2h_b / sec / 1e9},
         "plan": {"block_m": int(info.last_block_m), "block_n": int(info.last_block_n),
                  "panel_k": int(info.last_panel_k), "steps": int(info.last_steps),
                  "panel_slots": int(info.last_panel_slots)},
-        "residency": {"cache_target_bytes": int(tel.runtime.cache_target_bytes),
-                      "resident_bytes_peak": int(tel.runtime.resident_bytes_peak),
-                      "clean_evictions": int(tel.runtime.clean_evictions),
-                      "dirty_evictions": int(tel.runtime.dirty_evictions),
-                      "handle_reuses": int(tel.runtime.handle_reuses),
-                      "mappings": int(tel.runtime.mappings), "unmaps": int(tel.runtime.unmaps),
+        "residency": {"gemm_streamed": int(info.gemm_streamed),
+                      "gemm_in_place": int(info.gemm_in_place),
+                      "cache_target_bytes": int(rt.cache_target_bytes),
+                      "resident_bytes_peak": int(rt.resident_bytes_peak),
+                      "clean_evictions": int(rt.clean_evictions),
+                      "dirty_evictions": int(rt.dirty_evictions),
+                      "handle_reuses": int(rt.handle_reuses),
+                      "mappings": int(rt.mappings), "unmaps": int(rt.unmaps),
+                      "maps_equal_unmaps": int(rt.mappings) == int(rt.unmaps),
                       "tiles_retired": int(tel.tiles_retired)},
+        "check": {"block": [i0, j0, s], "max_abs_err_over_k_vs_fp64": err,
+                  "within_1e-6": err <= 1e-6},
+        "setup_s": {"fill_and_memcpy_h2d": round(t_fill, 1)},
         "clocks": clocks.summary(),
     }
-    print(json.dumps(line), flush=True)
 
 
-# --------------------------------------------------- strong-scaled partitioned SGEMM (C4)
-def run_sharded_c4(args) -> None:
+def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: int, rank: int,
+                    local: int, dev, barrier, max_over_ranks, peak: float, h2d: float,
+                    d2h: float) -> dict:
     """BASELINE config 4's form (NN, beta 0, C rows sharded over the GPUs, B read from the
-    host once per node and all-gathered over NVLink) as one fixed total problem, M x N x K
-    = --c4-m x --c4-n x --c4-k, split over however many ranks run it (strong scaling).
-    Full C4 (256 GiB of C, 32 GiB of B in every rank's host memory) does not fit the host
-    RAM of one box; the default 65536 x 65536 x 16384 keeps its shape class.  Each step is
-    one xvram_b200_sgemm_sharded call from pinned host memory to pinned host memory,
-    timed between barriers, max over ranks."""
+    host once per node and all-gathered over NVLink) as one fixed total problem split over
+    however many ranks run it (strong scaling).  Each step is one xvram_b200_sgemm_sharded
+    call from pinned host memory to pinned host memory, timed between barriers, max over
+    ranks; rows per rank from xvram_b200_shard_rows.  Every rank returns the same dict."""
+    import numpy as np
+    import torch
+
+    from xvram_b200 import device as xd
+    from xvram_b200 import shard
+
+    r0, mr = shard.rows(Mt, world, rank)
+    m_max = max(shard.rows(Mt, world, q)[1] for q in range(world))
+    # op N operands: A_local is mr x K (rows r0.. of the seeded M x K matrix), B is K x N.
+    a_h = torch.empty((Kt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x K
+    b_h = torch.empty((Nt, Kt), dtype=torch.float32).pin_memory()           # column-major K x N
+    c_h = torch.empty((Nt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x N
+    if mr:
+        for kk in range(Kt):  # A_local column k holds rows r0..r0+mr of column k
+            xd.fill_uniform(a_h[kk, :mr], 40, first_index=kk * Mt + r0, threads=1)
+    xd.fill_uniform(b_h, 41)
+    uid = shard.exchange_unique_id(rank) if world > 1 else shard.unique_id()
+    group = shard.ShardGroup(uid, rank, world)
+
+    def step():
+        st = group.sgemm(0, 0, mr, Nt, Kt, 1.0, a_h, max(mr, 1), b_h, Kt, 0.0, c_h,
+                         max(mr, 1), panel_k=2048)
+        assert st == 0, st
+
+    for _ in range(warmup):
+        step()
+    times = []
+    with ClockSampler(local, 200) as clocks:
+        for _ in range(steps):
+            barrier()
+            t0 = time.perf_counter()
+            step()
+            barrier()
+            times.append(max_over_ranks(time.perf_counter() - t0))
+    plan = group.last_plan()
+    group.close()
+    # sampled check: 16 outputs of this rank against FP64 (the operands' generator is
+    # counter-based, so any element can be recomputed)
+    rng = np.random.default_rng(rank)
+    worst = 0.0
+    if mr > 0:
+        for r, c in zip(rng.integers(0, mr, 16), rng.integers(0, Nt, 16)):
+            ref = float(a_h[:, int(r)].double().numpy() @ b_h[int(c)].double().numpy())
+            worst = max(worst, abs(float(c_h[int(c), int(r)]) - ref) / Kt)
+    worst = max_over_ranks(worst)
+    h2d_moved = max_over_ranks(float(plan["h2d_bytes"]))
+    sec = statistics.median(times)
+    flop = 2.0 * Mt * Nt * Kt
+    t_compute = flop / world / (peak * 1e12)
+    h2d_rank = 4.0 * (m_max * Kt + Kt * Nt / world)   # A rows + a 1/P share of B, once
+    d2h_rank = 4.0 * m_max * Nt
+    t_roof = max(t_compute, h2d_rank / (h2d * 1e9), d2h_rank / (d2h * 1e9))
+    del a_h, b_h, c_h
+    return {
+        "workload": f"C4 form, strong-scaled: {Mt} x {Nt} x {Kt} NN beta 0, C rows over "
+                    f"{world} GPU(s), B from host once per node + NCCL all-gather",
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": 1e3 * sec, "scaling": "strong",
+        "step_ms": [round(1e3 * t, 2) for t in times],
+        "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec, "per": "rank",
+                     "p_fp32_tflops_per_gpu": peak, "h2d_gbs_concurrent": h2d,
+                     "d2h_gbs_concurrent": d2h,
+                     "bound": "fp32" if t_compute >= max(h2d_rank / (h2d * 1e9),
+                                                         d2h_rank / (d2h * 1e9)) else "host-link"},
+        "host_link": {"h2d_bytes_per_rank_max": h2d_moved,
+                      "h2d_over_algorithmic": h2d_moved / h2d_rank,
+                      "d2h_bytes_per_rank": d2h_rank},
+        "plan": {key: plan[key] for key in ("row_groups", "group_rows", "block_n", "panel_k",
+                                            "gathers", "device_bytes")},
+        "check": {"sampled_outputs_per_rank": 16, "max_abs_err_over_k_vs_fp64": worst,
+                  "within_1e-6": worst <= 1e-6},
+        "clocks": clocks.summary(),
+    }
+
+
+def run_out_of_core(args) -> None:
+    """--workload c3s: the compat out-of-core leg alone (n = --ooc-n, budget
+    --ooc-budget-gib), printed as one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(device=dev)
+    peak_tflops, probes = measure_fp32_peak(dev, stream)
+    h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
+    leg = ooc_compat_leg(args.ooc_n, args.ooc_budget_gib, args.steps, peak_tflops, h2d_gbs,
+                         d2h_gbs)
+    leg["roofline"]["fp32_probes"] = probes
+    print(json.dumps({"metric": METRIC, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
+                      **leg}), flush=True)
+
+
+def run_sharded_c4(args) -> None:
+    """--workload c4s: the strong-scaled C4-form leg alone (--c4-m x --c4-n x --c4-k)."""
     import datetime
 
     import torch
     import torch.distributed as dist
-
-    from xvram_b200 import device as xd
-    from xvram_b200 import shard
 
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
@@ -330,10 +458,6 @@ def run_sharded_c4(args) -> None:
                                 timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    Mt, Nt, Kt = args.c4_m, args.c4_n, args.c4_k
-    per = (Mt + world - 1) // world
-    r0 = min(Mt, rank * per)
-    mr = min(Mt, r0 + per) - r0
 
     def barrier():
         if world > 1:
@@ -350,70 +474,11 @@ def run_sharded_c4(args) -> None:
     peak, probes = measure_fp32_peak(dev, stream)
     h2d, d2h = measure_link(dev, stream, barrier)
     h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
-    # op N operands: A_local is mr x K (rows r0.. of the seeded M x K matrix), B is K x N.
-    a_h = torch.empty((Kt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x K
-    b_h = torch.empty((Nt, Kt), dtype=torch.float32).pin_memory()           # column-major K x N
-    c_h = torch.empty((Nt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x N
-    for kk in range(0, Kt, 1024):  # A_local column k holds rows r0..r0+mr of column k
-        rows = a_h[kk:kk + 1024]
-        for j in range(rows.shape[0]):
-            xd.fill_uniform(rows[j, :mr], 40, first_index=(kk + j) * Mt + r0)
-    xd.fill_uniform(b_h, 41)
-    uid = shard.exchange_unique_id(rank) if world > 1 else shard.unique_id()
-    group = shard.ShardGroup(uid, rank, world)
-
-    def step():
-        st = group.sgemm(0, 0, mr, Nt, Kt, 1.0, a_h, max(mr, 1), b_h, Kt, 0.0, c_h,
-                         max(mr, 1), panel_k=2048)
-        assert st == 0, st
-
-    for _ in range(args.warmup):
-        step()
-    times = []
-    with ClockSampler(local, 200) as clocks:
-        for _ in range(args.steps):
-            barrier()
-            t0 = time.perf_counter()
-            step()
-            barrier()
-            times.append(max_over_ranks(time.perf_counter() - t0))
-    group.close()
-    # spot check: a few outputs of this rank against FP64 (the operands' generator is
-    # counter-based, so any element can be recomputed)
-    import numpy as np
-    rng = np.random.default_rng(rank)
-    rows = rng.integers(0, max(mr, 1), 4)
-    cols = rng.integers(0, Nt, 4)
-    worst = 0.0
-    if mr > 0:
-        for r, c in zip(rows, cols):
-            arow = a_h[:, int(r)].double().numpy()
-            bcol = b_h[c].double().numpy()
-            ref = float(arow @ bcol)
-            worst = max(worst, abs(float(c_h[c, r]) - ref) / Kt)
-    worst = max_over_ranks(worst)
-    sec = statistics.median(times)
-    flop = 2.0 * Mt * Nt * Kt
-    t_compute = flop / world / (peak * 1e12)
-    h2d_rank = 4.0 * (per * Kt + Kt * Nt / world)
-    d2h_rank = 4.0 * per * Nt
-    t_roof = max(t_compute, h2d_rank / (h2d * 1e9), d2h_rank / (d2h * 1e9))
+    leg = ooc_sharded_leg(args.c4_m, args.c4_n, args.c4_k, args.steps, args.warmup, world, rank,
+                          local, dev, barrier, max_over_ranks, peak, h2d, d2h)
+    leg["roofline"]["fp32_probes"] = probes
     if rank == 0:
-        print(json.dumps({
-            "metric": METRIC,
-            "workload": f"C4 form, strong-scaled: {Mt} x {Nt} x {Kt} NN beta 0, C rows over "
-                        f"{world} GPU(s), B from host once per node + NCCL all-gather",
-            "value": flop / sec / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 * sec, "scaling": "strong",
-            "step_ms": [round(1e3 * t, 2) for t in times],
-            "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
-                         "p_fp32_tflops_per_gpu": peak, "fp32_probes": probes, "h2d_gbs_concurrent": h2d,
-                         "d2h_gbs_concurrent": d2h,
-                         "bound": "fp32" if t_compute >= max(h2d_rank / (h2d * 1e9),
-                                                             d2h_rank / (d2h * 1e9)) else "host-link"},
-            "check": {"sampled_outputs_per_rank": 4, "max_abs_err_over_k_vs_fp64": worst},
-            "clocks": clocks.summary(),
-        }), flush=True)
+        print(json.dumps({"metric": METRIC, **leg}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -728,9 +793,19 @@ def main_gpu(args) -> None:
     # the job's host link is as slow as its slowest GPU's
     h2d, d2h = -max_over_ranks(-h2d), -max_over_ranks(-d2h)
 
-    # ---------------- kernel-only: inputs resident in HBM
+    # ---------------- kernel-only: inputs resident in HBM.  At N > 1 the job is one
+    # problem split by C rows: each rank holds its A rows, its C rows and a 1/N column
+    # slice of the shared B, and every step first all-gathers B over NVLink (NCCL, on the
+    # timed stream) and then runs the kernel on the gathered B.
+    B_slice = B[rank * (N // world):(rank + 1) * (N // world)].clone() if world > 1 else None
+    B_run = torch.empty_like(B) if world > 1 else B
+    if world > 1:
+        assert N % world == 0
+
     def launch():
-        st = xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B, K, BETA, Cd, M, stream=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(B_run, B_slice)
+        st = xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B_run, K, BETA, Cd, M, stream=stream)
         assert st == 0, st
 
     with torch.cuda.stream(stream):
@@ -754,10 +829,25 @@ def main_gpu(args) -> None:
     peak_again, probes_again = measure_fp32_peak(dev, stream)
     peak_tflops = max(peak_tflops, peak_again)
     probes = {key: max(probes[key], probes_again[key]) for key in probes}
-    kernel_ms = start.elapsed_time(stop) / args.steps
-    kernel_ms_max = max_over_ranks(kernel_ms)
-    value = world * FLOP / (kernel_ms_max * 1e-3) / 1e12
+    step_ms = start.elapsed_time(stop) / args.steps
+    step_ms_max = max_over_ranks(step_ms)
+    value = world * FLOP / (step_ms_max * 1e-3) / 1e12
+    # The dominant kernel alone (its launches timed on the same stream, no gather), for
+    # the roofline: at N = 1 this is the step itself.
+    if world > 1:
+        k0e, k1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            k0e.record(stream)
+            for _ in range(args.steps):
+                assert xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B_run, K, BETA, Cd, M,
+                                stream=stream) == 0
+            k1e.record(stream)
+        k1e.synchronize()
+        kernel_ms = k0e.elapsed_time(k1e) / args.steps
+    else:
+        kernel_ms = step_ms
     achieved = FLOP / (kernel_ms * 1e-3) / 1e12
+    del B_slice
 
     # ---------------- kernel-only, tensor-core path (three-term TF32 on tcgen05/TMEM)
     tc_need = lib.xvram_b200_sgemm_workspace_bytes(OP_A | 0x100, OP_B, M, N, K)
@@ -908,13 +998,29 @@ def main_gpu(args) -> None:
     # the three H2D copies precede the GEMM in series; C's D2H can overlap the kernel.
     t_floor_api = h2d_bytes / (h2d * 1e9) + max(kernel_ms * 1e-3, d2h_bytes / (d2h * 1e9))
 
-    traffic = None
-    tfile = ROOT / "profiles" / "sgemm_ffma_c2_traffic.json"
+    # DRAM bytes per launch of the dominant kernel on this workload, from the committed ncu
+    # capture of this bench's own TN launch (profiles/sgemm_ffma_c2_tn_traffic.json).
+    traffic, traffic_source = None, None
+    tfile = ROOT / "profiles" / "sgemm_ffma_c2_tn_traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+            tj = json.loads(tfile.read_text())
+            traffic = tj.get("dram_bytes_per_launch")
+            traffic_source = f"{tfile.relative_to(ROOT)}: {tj.get('kernel')} ({tj.get('command')})"
         except (ValueError, OSError):
             traffic = None
+
+    # ---------------- out of core: the metric's own configurations, after the C2 legs
+    del A, B, Cd, B_run
+    torch.cuda.empty_cache()
+    ooc = {}
+    if not args.skip_ooc:
+        if world == 1:
+            ooc["compat_c3_form"] = ooc_compat_leg(args.ooc_n, args.ooc_budget_gib, 1,
+                                                   peak_tflops, h2d, d2h, local)
+        ooc["sharded_c4_form"] = ooc_sharded_leg(args.c4_m, args.c4_n, args.c4_k, 2, 1, world,
+                                                 rank, local, dev, barrier, max_over_ranks,
+                                                 peak_tflops, h2d, d2h)
 
     if rank == 0:
         cpu = None
@@ -923,14 +1029,19 @@ def main_gpu(args) -> None:
         line = {
             "metric": METRIC,
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": kernel_ms_max, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "per_gpu": f"M={M} N={N} K={K}",
-                       "parallelism": f"C rows split over {world} GPU(s), replicas",
+                       "parallelism": (f"one {M * world} x {N} x {K} problem split by C rows "
+                                       f"over {world} GPUs; each step all-gathers B from "
+                                       f"1/{world} column slices over NVLink (NCCL), then "
+                                       "the kernel" if world > 1 else "1 GPU"),
                        "l2": "inputs larger than L2 (416 MiB working set per step)",
                        "seeds": "A 10, B 11, C 12 (counter-based uniform[-1,1))"},
             "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak_tflops,
                          "unit": "TFLOP/s", "frac": achieved / peak_tflops, "traffic": traffic,
+                         "traffic_source": traffic_source,
+                         "kernel_ms": kernel_ms,
                          "peak_source": "measured FP32 pipe probes, this run: the higher of scalar "
                                         "FFMA (xvram_b200_ffma_probe) and packed FFMA2 "
                                         "(xvram_b200_ffma2_probe)",
@@ -1003,6 +1114,7 @@ def main_gpu(args) -> None:
             "compat_trace": ({"path": args.trace, "records": trace_records,
                               "format": "xvram.cuda_compat_trace v1 (JSON lines)"}
                              if trace_records is not None else None),
+            "ooc": ooc or None,
             "gpu_launches": args.steps * (1 + int(OP_A == 1) + int(OP_B == 0)),
             "gpu_launches_e2e": launches_e2e,
             "clocks": clocks.summary(),
@@ -1036,6 +1148,8 @@ def main() -> None:
     ap.add_argument("--mlp-budget-gib", type=float, default=8.0)
     ap.add_argument("--ooc-n", type=int, default=65536)
     ap.add_argument("--ooc-budget-gib", type=float, default=10.0)
+    ap.add_argument("--skip-ooc", action="store_true",
+                    help="leave the out-of-core legs (the 'ooc' key) out of the default run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -251,6 +251,68 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void*
                                                                    uint64_t* out_group);
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_destroy(uint64_t group);
 
+/*
+ * Collectives supplied by the caller, for a group that should not (or cannot) use NCCL:
+ * an application with its own communicator, or a host-memory test device.  Both functions
+ * are called by every rank in the same order and must act as the collective of that name
+ * over the group's ranks, enqueued on `stream` (the group's native collective stream, a
+ * cudaStream_t of the group's device) or completed before returning:
+ *   all_reduce_max_u64: buffer[0..count) = elementwise maximum over the ranks, in place;
+ *   all_gather_f32:     recv[q count .. (q+1) count) = rank q's send, for every q; send
+ *                       may be recv + rank * count (in place).
+ * Pointers are device addresses of the group's device.  A non-SUCCESS return fails the
+ * call that issued it and leaves the group unusable (POISONED).
+ */
+typedef struct xvram_b200_shard_collectives_v1 {
+  uint32_t struct_size; /* sizeof(xvram_b200_shard_collectives_v1) */
+  uint32_t reserved0;
+  void* context; /* passed back as the first argument */
+  xvram_status(XVRAM_CALL* all_reduce_max_u64)(void* context, uint64_t* buffer, uint64_t count,
+                                               uint64_t stream);
+  xvram_status(XVRAM_CALL* all_gather_f32)(void* context, const float* send, float* recv,
+                                           uint64_t count, uint64_t stream);
+} xvram_b200_shard_collectives_v1;
+
+/* Creates this rank's group with the caller's collectives instead of NCCL, on the calling
+ * thread's current device.  No reference counterpart. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create_custom(
+    const xvram_b200_shard_collectives_v1* ops, int32_t rank, int32_t world, uint64_t* out_group);
+
+/* The rows of an m-row C that `rank` of `world` owns in the partition this library uses:
+ * whole 128-row tiles dealt out as evenly as possible (rank r gets tiles
+ * [r T / world, (r + 1) T / world) of T = ceil(m / 128)), the last tile cut at m.  Ranks
+ * past the tile count get *row_count = 0.  Pass those rows of A and C to
+ * xvram_b200_sgemm_sharded.  No reference counterpart. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_rows(int64_t m, int32_t world,
+                                                           int32_t rank, int64_t* row_begin,
+                                                           int64_t* row_count);
+
+/* The plan the group's ranks agreed on for the last xvram_b200_sgemm_sharded call, and
+ * what this rank moved.  Every rank of a group reports the same fields down to
+ * device_bytes; rank, h2d_bytes and d2h_bytes are this rank's. */
+typedef struct xvram_b200_shard_plan_v1 {
+  uint32_t struct_size; /* set by the caller to sizeof(xvram_b200_shard_plan_v1) */
+  int32_t world;
+  uint64_t m_max;         /* largest m_local over the ranks */
+  uint64_t avail_min;     /* smallest device memory the ranks offered (bytes) */
+  uint64_t row_groups;    /* row groups of A kept resident in turn */
+  uint64_t group_rows;    /* rows per group (a multiple of 128) */
+  uint64_t block_n;       /* C column block width */
+  uint64_t panel_k;       /* K panel depth of A's first arrival */
+  uint64_t b_slice_cols;  /* op(B) = N: block columns each rank copies (0 for op T) */
+  uint64_t b_slice_k;     /* op(B) = T: k rows each rank copies (0 for op N) */
+  uint64_t slice_elems;   /* floats each rank contributes to one B all-gather */
+  uint64_t device_bytes;  /* device memory the plan's buffers take on each rank */
+  int32_t rank;
+  uint32_t reserved0;
+  uint64_t gathers;       /* B all-gathers issued */
+  uint64_t h2d_bytes;     /* host -> device bytes this rank copied */
+  uint64_t d2h_bytes;     /* device -> host bytes this rank copied */
+} xvram_b200_shard_plan_v1;
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_last_plan(uint64_t group,
+                                                                xvram_b200_shard_plan_v1* out);
+
 /* All-gather of row blocks, collectively on every rank of the group, enqueued on `stream`
  * (a cudaStream_t of the group's device): rank q's block (rows x cols, column-major,
  * ld_block) becomes rows [q rows, (q + 1) rows) of every rank's dst (world rows x cols,

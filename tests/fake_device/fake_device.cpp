@@ -347,6 +347,38 @@ public:
   }
   uint64_t native_stream(xvram::StreamId) override { return 0; }
 
+  xvram::Error make_current(int* previous) override {
+    *previous = 0;
+    return {};
+  }
+  void restore_current(int) override {}
+  xvram::Error mem_alloc(uint64_t bytes, uint64_t* out) override {
+    if (should_fail("mem_alloc"))
+      return injected("mem_alloc");
+    void* p = std::aligned_alloc(256, (std::max<uint64_t>(bytes, 1) + 255) / 256 * 256);
+    if (!p)
+      return xvram::make_error(XVRAM_STATUS_DEVICE_OUT_OF_MEMORY, "fake", "mem_alloc", "no memory");
+    *out = reinterpret_cast<uint64_t>(p);
+    return {};
+  }
+  xvram::Error mem_free(uint64_t p) override {
+    std::free(reinterpret_cast<void*>(p));
+    return {};
+  }
+  xvram::Error event_query(xvram::EventId, bool* done) override {
+    *done = true; // immediate streams: everything recorded has completed
+    return {};
+  }
+  xvram::Error transpose_f32(uint64_t src, int64_t lds, uint64_t dst, int64_t ldd, int64_t rows,
+                             int64_t cols, xvram::StreamId) override {
+    const float* s = reinterpret_cast<const float*>(src);
+    float* d = reinterpret_cast<float*>(dst);
+    for (int64_t c = 0; c < cols; ++c)
+      for (int64_t r = 0; r < rows; ++r)
+        d[c + r * ldd] = s[r + c * lds];
+    return {};
+  }
+
   uint64_t next_id = 0;
   uint64_t maps = 0, gemms = 0, conversions = 0;
 };

@@ -67,6 +67,25 @@ class DeviceInfo(C.Structure):
     ]
 
 
+class ShardCollectives(C.Structure):
+    """xvram_b200_shard_collectives_v1 (include/xvram_b200.h)."""
+
+    ALL_REDUCE = C.CFUNCTYPE(u32, vp, C.POINTER(u64), u64, u64)
+    ALL_GATHER = C.CFUNCTYPE(u32, vp, C.POINTER(f32), C.POINTER(f32), u64, u64)
+    _fields_ = [("struct_size", u32), ("reserved0", u32), ("context", vp),
+                ("all_reduce_max_u64", ALL_REDUCE), ("all_gather_f32", ALL_GATHER)]
+
+
+class ShardPlan(C.Structure):
+    """xvram_b200_shard_plan_v1 (include/xvram_b200.h)."""
+
+    _fields_ = [("struct_size", u32), ("world", i32),
+                ("m_max", u64), ("avail_min", u64), ("row_groups", u64), ("group_rows", u64),
+                ("block_n", u64), ("panel_k", u64), ("b_slice_cols", u64), ("b_slice_k", u64),
+                ("slice_elems", u64), ("device_bytes", u64), ("rank", i32), ("reserved0", u32),
+                ("gathers", u64), ("h2d_bytes", u64), ("d2h_bytes", u64)]
+
+
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
@@ -88,6 +107,13 @@ def _load() -> C.CDLL:
     lib.xvram_b200_shard_unique_id.restype = u32
     lib.xvram_b200_shard_group_create.argtypes = [vp, u64, i32, i32, C.POINTER(u64)]
     lib.xvram_b200_shard_group_create.restype = u32
+    lib.xvram_b200_shard_group_create_custom.argtypes = [C.POINTER(ShardCollectives), i32, i32,
+                                                         C.POINTER(u64)]
+    lib.xvram_b200_shard_group_create_custom.restype = u32
+    lib.xvram_b200_shard_rows.argtypes = [i64, i32, i32, C.POINTER(i64), C.POINTER(i64)]
+    lib.xvram_b200_shard_rows.restype = u32
+    lib.xvram_b200_shard_last_plan.argtypes = [u64, C.POINTER(ShardPlan)]
+    lib.xvram_b200_shard_last_plan.restype = u32
     lib.xvram_b200_shard_group_destroy.argtypes = [u64]
     lib.xvram_b200_shard_group_destroy.restype = u32
     lib.xvram_b200_shard_allgather_rows.argtypes = [u64, vp, i64, i64, i64, vp, i64, vp, u64, u64]
@@ -169,6 +195,9 @@ EXPORTED = (
     "xvram_b200_shard_unique_id",
     "xvram_b200_shard_group_create",
     "xvram_b200_shard_group_destroy",
+    "xvram_b200_shard_group_create_custom",
+    "xvram_b200_shard_rows",
+    "xvram_b200_shard_last_plan",
     "xvram_b200_shard_allgather_rows",
     "xvram_b200_sgemm_sharded",
     "xvram_b200_fill_uniform",

@@ -392,6 +392,54 @@ public:
 
   uint64_t native_stream(StreamId s) override { return reinterpret_cast<uint64_t>(stream(s)); }
 
+  Error make_current(int* previous) override {
+    XV_RT("cudaGetDevice", cudaGetDevice(previous));
+    XV_RT("cudaSetDevice", cudaSetDevice(ordinal_));
+    return {};
+  }
+  void restore_current(int previous) override { cudaSetDevice(previous); }
+
+  Error mem_alloc(uint64_t bytes, uint64_t* out) override {
+    XV_RT("cudaSetDevice", cudaSetDevice(ordinal_));
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      Error err = rt_error("cudaMalloc", e);
+      if (e == cudaErrorMemoryAllocation)
+        err.status = XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
+      return err;
+    }
+    *out = reinterpret_cast<uint64_t>(p);
+    return {};
+  }
+  Error mem_free(uint64_t p) override {
+    XV_RT("cudaFree", cudaFree(reinterpret_cast<void*>(p)));
+    return {};
+  }
+
+  Error event_query(EventId e, bool* done) override {
+    const cudaError_t q = cudaEventQuery(event(e));
+    if (q == cudaErrorNotReady) {
+      *done = false;
+      return {};
+    }
+    XV_RT("cudaEventQuery", q);
+    *done = true;
+    return {};
+  }
+
+  Error transpose_f32(uint64_t src, int64_t lds, uint64_t dst, int64_t ldd, int64_t rows,
+                      int64_t cols, StreamId s) override {
+    if (rows > INT32_MAX || cols > INT32_MAX)
+      return make_error(XVRAM_STATUS_INTERNAL, "executor", "transpose", "block exceeds int32");
+    XV_RT("transpose_f32", transpose_f32_async(reinterpret_cast<const float*>(src), lds,
+                                               reinterpret_cast<float*>(dst), ldd,
+                                               static_cast<int>(rows), static_cast<int>(cols),
+                                               stream(s)));
+    return {};
+  }
+
 private:
   static CUmemAllocationProp alloc_prop_for(int ordinal) {
     CUmemAllocationProp p{};

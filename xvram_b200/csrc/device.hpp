@@ -116,6 +116,21 @@ public:
   virtual Error kernel_status(StreamId s, uint32_t* word) = 0;
   // The native handle of stream s (a cudaStream_t) handed to transaction callbacks.
   virtual uint64_t native_stream(StreamId s) = 0;
+
+  // --- used by the multi-GPU executor (sharded.cpp) --------------------------------------
+  // Makes this device the calling thread's current one; *previous receives the one that
+  // was current, for restore_current.
+  virtual Error make_current(int* previous) = 0;
+  virtual void restore_current(int previous) = 0;
+  // Plain device allocations (256-byte aligned) for the executor's own buffers.
+  virtual Error mem_alloc(uint64_t bytes, uint64_t* out) = 0;
+  virtual Error mem_free(uint64_t p) = 0;
+  // *done = whether everything before event e's record has completed (non-blocking).
+  virtual Error event_query(EventId e, bool* done) = 0;
+  // dst (cols x rows, column-major, ldd) = src^T (src: rows x cols, column-major, lds):
+  // FP32 values moved, not rounded.
+  virtual Error transpose_f32(uint64_t src, int64_t lds, uint64_t dst, int64_t ldd, int64_t rows,
+                              int64_t cols, StreamId s) = 0;
 };
 
 using DeviceFactory = std::unique_ptr<Device> (*)();

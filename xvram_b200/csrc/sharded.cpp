@@ -22,13 +22,20 @@
 // Kernels only read local HBM; nothing loads from a peer's memory, and every TMA load
 // targets only the issuing CTA.
 //
+// The executor reaches the GPU only through the runtime's Device interface (device.hpp)
+// and its peers only through a ShardComm (below): NCCL for groups made from a unique id,
+// or caller-supplied collectives (xvram_b200_shard_group_create_custom).  The same
+// schedule therefore also runs on the host-memory fake device with host collectives,
+// which is how the CPU test suite checks the partition, the B slices and the plan
+// agreement across ranks.
+//
 // NCCL is loaded at run time (dlopen of libnccl.so.2, whichever the process already has),
 // so the library keeps no link-time NCCL dependency.  Communicator creation is
 // non-blocking with a deadline, and every host wait on a collective is bounded: a peer
 // that never arrives produces TIMEOUT and an aborted communicator, not a hang.
 #include "xvram_b200.h"
 
-#include "kernels.hpp"
+#include "device.hpp"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -38,11 +45,16 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <thread>
 #include <vector>
 
 namespace {
+
+using xvram::Device;
+using xvram::EventId;
+using xvram::StreamId;
 
 struct NcclApi {
   decltype(&ncclGetUniqueId) get_unique_id = nullptr;
@@ -81,56 +93,127 @@ constexpr double kInitTimeoutS = 120.0;
 constexpr double kWaitTimeoutS = 60.0;
 constexpr uint64_t kHeadroomBytes = 1ull << 30; // left free on the device for everything else
 constexpr uint64_t kDefaultBlockN = 1024;       // C block width (columns)
-constexpr uint64_t kTileM = 128;                // row granularity of a row group
+constexpr uint64_t kTileM = 128;                // row granularity of partitions and row groups
 // B and C block buffers in flight: block j+2's copies may start while block j's
 // write-back is still running.
 constexpr int kSlots = 3;
 
+double seconds_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// The collectives a shard group needs, enqueued on the group's collective stream (its
+// native handle).  Buffers are device addresses of the group's device.
+class ShardComm {
+public:
+  virtual ~ShardComm() = default;
+  // In place: buf[0..count) = elementwise maximum over the ranks.
+  virtual xvram_status all_reduce_max_u64(uint64_t* buf, uint64_t count, uint64_t stream) = 0;
+  // recv = the ranks' `count`-float sends, in rank order; send may be recv + rank * count.
+  virtual xvram_status all_gather_f32(const float* send, float* recv, uint64_t count,
+                                      uint64_t stream) = 0;
+  // Polled while the host waits on the device: non-SUCCESS once the collectives failed.
+  virtual xvram_status health() = 0;
+  virtual void abort() = 0;
+};
+
+class NcclComm final : public ShardComm {
+public:
+  explicit NcclComm(ncclComm_t c) : comm_(c) {}
+  ~NcclComm() override {
+    if (comm_)
+      nccl().destroy(comm_);
+  }
+  xvram_status all_reduce_max_u64(uint64_t* buf, uint64_t count, uint64_t stream) override {
+    return issued(nccl().all_reduce(buf, buf, count, ncclUint64, ncclMax, comm_,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+  }
+  xvram_status all_gather_f32(const float* send, float* recv, uint64_t count,
+                              uint64_t stream) override {
+    return issued(nccl().all_gather(send, recv, count, ncclFloat, comm_,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+  }
+  xvram_status health() override {
+    ncclResult_t ar = ncclSuccess;
+    if (!comm_)
+      return XVRAM_STATUS_POISONED;
+    if (nccl().async_error(comm_, &ar) == ncclSuccess && ar != ncclSuccess &&
+        ar != ncclInProgress)
+      return XVRAM_STATUS_CUDA_ERROR;
+    return XVRAM_STATUS_SUCCESS;
+  }
+  void abort() override {
+    if (comm_)
+      nccl().abort(comm_);
+    comm_ = nullptr;
+  }
+
+private:
+  // A non-blocking communicator may return ncclInProgress while it is still enqueueing a
+  // call: wait (bounded) until the call has been issued before the next NCCL call.
+  xvram_status issued(ncclResult_t nr) {
+    if (nr == ncclSuccess)
+      return XVRAM_STATUS_SUCCESS;
+    if (nr != ncclInProgress)
+      return XVRAM_STATUS_CUDA_ERROR;
+    const auto t0 = std::chrono::steady_clock::now();
+    ncclResult_t st = ncclInProgress;
+    while (st == ncclInProgress) {
+      if (nccl().async_error(comm_, &st) != ncclSuccess || seconds_since(t0) > kWaitTimeoutS)
+        return XVRAM_STATUS_TIMEOUT;
+    }
+    return st == ncclSuccess ? XVRAM_STATUS_SUCCESS : XVRAM_STATUS_CUDA_ERROR;
+  }
+  ncclComm_t comm_ = nullptr;
+};
+
+// Collectives the caller supplies (xvram_b200_shard_collectives_v1).
+class CallbackComm final : public ShardComm {
+public:
+  explicit CallbackComm(const xvram_b200_shard_collectives_v1& ops) : ops_(ops) {}
+  xvram_status all_reduce_max_u64(uint64_t* buf, uint64_t count, uint64_t stream) override {
+    return ops_.all_reduce_max_u64(ops_.context, buf, count, stream);
+  }
+  xvram_status all_gather_f32(const float* send, float* recv, uint64_t count,
+                              uint64_t stream) override {
+    return ops_.all_gather_f32(ops_.context, send, recv, count, stream);
+  }
+  xvram_status health() override { return XVRAM_STATUS_SUCCESS; }
+  void abort() override {}
+
+private:
+  xvram_b200_shard_collectives_v1 ops_;
+};
+
 struct Buffer {
-  void* p = nullptr;
-  size_t bytes = 0;
-  cudaError_t ensure(size_t want) {
-    if (bytes >= want)
-      return cudaSuccess;
-    release();
-    const cudaError_t e = cudaMalloc(&p, want);
-    if (e == cudaSuccess)
-      bytes = want;
-    else
-      p = nullptr;
-    return e;
-  }
-  void release() {
-    if (p)
-      cudaFree(p);
-    p = nullptr;
-    bytes = 0;
-  }
+  uint64_t p = 0;
+  uint64_t bytes = 0;
 };
 
 struct ShardGroup {
-  ncclComm_t comm = nullptr;
+  std::unique_ptr<Device> dev;
+  std::unique_ptr<ShardComm> comm;
   int rank = 0, world = 1, device = 0;
-  cudaStream_t h2d = nullptr, coll = nullptr, comp[2] = {}, d2h = nullptr;
-  // Per double-buffer slot: B block copied / gathered (and canonical) / no longer read;
+  StreamId h2d = 0, coll = 0, comp[2] = {}, d2h = 0;
+  // Per buffer slot: B block copied / gathered (and canonical) / no longer read;
   // C block copied in / computed / copied out.
-  cudaEvent_t b_loaded[kSlots] = {}, b_ready[kSlots] = {}, b_free[kSlots] = {};
-  cudaEvent_t c_loaded[kSlots] = {}, c_done[kSlots] = {}, c_free[kSlots] = {};
+  EventId b_loaded[kSlots] = {}, b_ready[kSlots] = {}, b_free[kSlots] = {};
+  EventId c_loaded[kSlots] = {}, c_done[kSlots] = {}, c_free[kSlots] = {};
   // A raw panel slot reusable (K-major A), all of A canonical, end of a row group per
   // compute stream, end of the call, plan exchange done.
-  cudaEvent_t a_free[2] = {}, a_all = nullptr, group_end[2] = {}, out = nullptr,
-              plan_ev = nullptr;
-  std::vector<cudaEvent_t> a_ev; // one per A panel: panel p resident (and canonical)
+  EventId a_free[2] = {}, a_all = 0, group_end[2] = {}, out = 0, plan_ev = 0;
+  std::vector<EventId> a_ev; // one per A panel: panel p resident (and canonical)
   Buffer a_canon, a_raw[2], b_raw[kSlots], b_canon[kSlots], c_blk[kSlots], plan_dev;
   uint64_t* plan_host = nullptr; // 2 x u64, page-locked
   bool aborted = false;
   std::mutex mu;
   // Device memory this group may use (free + its own buffers), as sampled for the last
   // call, with that call's shape: a repeat of the same shape within a second reuses it
-  // instead of calling cudaMemGetInfo, whose latency now and then reaches milliseconds.
+  // instead of asking the device again, whose latency now and then reaches milliseconds.
   uint64_t avail_sampled = 0;
   uint64_t shape_sampled[6] = {};
   std::chrono::steady_clock::time_point when_sampled{};
+  xvram_b200_shard_plan_v1 last{};
 
   static constexpr int kBuffers = 3 + 3 * kSlots + 1;
   Buffer* buffers[kBuffers] = {&a_canon,    &a_raw[0],   &a_raw[1],   &b_raw[0], &b_raw[1],
@@ -141,6 +224,21 @@ struct ShardGroup {
     for (const Buffer* b : buffers)
       n += b->bytes;
     return n;
+  }
+  bool ensure(Buffer& b, uint64_t want) {
+    if (b.bytes >= want)
+      return true;
+    release(b);
+    if (dev->mem_alloc(want, &b.p))
+      return false;
+    b.bytes = want;
+    return true;
+  }
+  void release(Buffer& b) {
+    if (b.p)
+      dev->mem_free(b.p);
+    b.p = 0;
+    b.bytes = 0;
   }
 };
 
@@ -156,37 +254,26 @@ uint64_t env_u64(const char* name, uint64_t fallback) {
   return (end && *end == '\0' && x > 0) ? static_cast<uint64_t>(x) : fallback;
 }
 
-xvram_status cuda_status(cudaError_t e) {
-  if (e == cudaSuccess)
-    return XVRAM_STATUS_SUCCESS;
-  return e == cudaErrorMemoryAllocation ? XVRAM_STATUS_DEVICE_OUT_OF_MEMORY
-                                        : XVRAM_STATUS_CUDA_ERROR;
-}
-
 void abort_group(ShardGroup& g) {
   if (g.comm)
-    nccl().abort(g.comm);
-  g.comm = nullptr;
+    g.comm->abort();
   g.aborted = true;
 }
 
-// Waits for `e` with a deadline, watching the communicator for asynchronous errors.
-xvram_status bounded_wait(ShardGroup& g, cudaEvent_t e) {
+// Waits for `e` with a deadline, watching the collectives for asynchronous errors.
+xvram_status bounded_wait(ShardGroup& g, EventId e) {
   const auto start = std::chrono::steady_clock::now();
   for (;;) {
-    const cudaError_t q = cudaEventQuery(e);
-    if (q == cudaSuccess)
+    bool done = false;
+    if (g.dev->event_query(e, &done))
+      return XVRAM_STATUS_CUDA_ERROR;
+    if (done)
       return XVRAM_STATUS_SUCCESS;
-    if (q != cudaErrorNotReady)
-      return XVRAM_STATUS_CUDA_ERROR;
-    ncclResult_t ar = ncclSuccess;
-    if (g.comm && nccl().async_error(g.comm, &ar) == ncclSuccess && ar != ncclSuccess &&
-        ar != ncclInProgress) {
+    if (xvram_status h = g.comm->health(); h != XVRAM_STATUS_SUCCESS) {
       abort_group(g);
-      return XVRAM_STATUS_CUDA_ERROR;
+      return h;
     }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count() >
-        kWaitTimeoutS) {
+    if (seconds_since(start) > kWaitTimeoutS) {
       abort_group(g);
       return XVRAM_STATUS_TIMEOUT;
     }
@@ -194,68 +281,83 @@ xvram_status bounded_wait(ShardGroup& g, cudaEvent_t e) {
   }
 }
 
-// A non-blocking communicator may return ncclInProgress while it is still enqueueing a
-// call: wait (bounded) until the call has been issued before the next NCCL call.
-xvram_status nccl_issued(ShardGroup& g, ncclResult_t nr) {
-  if (nr == ncclSuccess)
-    return XVRAM_STATUS_SUCCESS;
-  if (nr != ncclInProgress) {
-    abort_group(g);
-    return XVRAM_STATUS_CUDA_ERROR;
-  }
-  const auto t0 = std::chrono::steady_clock::now();
-  ncclResult_t st = ncclInProgress;
-  while (st == ncclInProgress) {
-    if (nccl().async_error(g.comm, &st) != ncclSuccess ||
-        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() >
-            kWaitTimeoutS) {
-      st = ncclInternalError;
-      break;
-    }
-  }
-  if (st != ncclSuccess) {
-    abort_group(g);
-    return XVRAM_STATUS_TIMEOUT;
-  }
-  return XVRAM_STATUS_SUCCESS;
-}
-
 void destroy_group(ShardGroup* g) {
   if (!g)
     return;
-  int saved = 0;
-  cudaGetDevice(&saved);
-  cudaSetDevice(g->device);
-  for (auto* s : {g->h2d, g->coll, g->comp[0], g->comp[1], g->d2h})
-    if (s) {
-      cudaStreamSynchronize(s);
-      cudaStreamDestroy(s);
-    }
-  for (auto* arr : {g->b_loaded, g->b_ready, g->b_free, g->c_loaded, g->c_done, g->c_free})
-    for (int i = 0; i < kSlots; ++i)
-      if (arr[i])
-        cudaEventDestroy(arr[i]);
-  for (auto* arr : {g->a_free, g->group_end})
-    for (int i = 0; i < 2; ++i)
-      if (arr[i])
-        cudaEventDestroy(arr[i]);
-  for (auto* e : {g->a_all, g->out, g->plan_ev})
-    if (e)
-      cudaEventDestroy(e);
-  for (cudaEvent_t e : g->a_ev)
-    cudaEventDestroy(e);
-  for (Buffer* b : g->buffers)
-    b->release();
-  if (g->plan_host)
-    cudaFreeHost(g->plan_host);
-  if (g->comm)
-    nccl().destroy(g->comm);
-  cudaSetDevice(saved);
+  if (g->dev) {
+    int prev = 0;
+    const bool switched = !g->dev->make_current(&prev);
+    for (StreamId s : {g->h2d, g->coll, g->comp[0], g->comp[1], g->d2h})
+      if (s)
+        g->dev->stream_sync(s);
+    for (Buffer* b : g->buffers)
+      g->release(*b);
+    if (g->plan_host)
+      g->dev->host_free(g->plan_host);
+    g->comm.reset();
+    g->dev->close(); // streams and events
+    if (switched)
+      g->dev->restore_current(prev);
+  }
   delete g;
 }
 
-// The geometry every rank derives from the same agreed numbers.
-struct Plan {
+// Opens the group's device (the current CUDA device, or the installed test device) and
+// creates its streams, events and plan-exchange buffers.
+xvram_status setup_group(ShardGroup& g) {
+  g.dev = xvram::device_factory()();
+  int ordinal = 0;
+  if (cudaGetDevice(&ordinal) != cudaSuccess) { // no CUDA here: only a test device opens
+    cudaGetLastError();
+    ordinal = 0;
+  }
+  xvram::DeviceInfo info;
+  if (xvram::Error e = g.dev->open(ordinal, &info))
+    return e.status;
+  g.device = ordinal;
+  Device& d = *g.dev;
+  for (StreamId* s : {&g.h2d, &g.coll, &g.comp[0], &g.comp[1], &g.d2h})
+    if (d.stream_create(s))
+      return XVRAM_STATUS_CUDA_ERROR;
+  for (EventId* arr : {g.b_loaded, g.b_ready, g.b_free, g.c_loaded, g.c_done, g.c_free})
+    for (int i = 0; i < kSlots; ++i)
+      if (d.event_create(&arr[i]))
+        return XVRAM_STATUS_CUDA_ERROR;
+  for (EventId* arr : {g.a_free, g.group_end})
+    for (int i = 0; i < 2; ++i)
+      if (d.event_create(&arr[i]))
+        return XVRAM_STATUS_CUDA_ERROR;
+  for (EventId* e : {&g.a_all, &g.out, &g.plan_ev})
+    if (d.event_create(e))
+      return XVRAM_STATUS_CUDA_ERROR;
+  void* ph = nullptr;
+  if (d.host_alloc(2 * sizeof(uint64_t), &ph))
+    return XVRAM_STATUS_HOST_OUT_OF_MEMORY;
+  g.plan_host = static_cast<uint64_t*>(ph);
+  if (!g.ensure(g.plan_dev, 256))
+    return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
+  return XVRAM_STATUS_SUCCESS;
+}
+
+} // namespace
+
+namespace xvram {
+
+// Rows [*begin, *begin + *count) of an m-row C that rank `rank` of `world` owns: whole
+// 128-row tiles dealt out as evenly as possible (rank r takes tiles [r T / P, (r+1) T / P)),
+// the last tile cut at m.  Ranks beyond the tile count get no rows.
+void shard_rows(uint64_t m, int world, int rank, uint64_t* begin, uint64_t* count) {
+  const uint64_t tiles = (m + kTileM - 1) / kTileM;
+  const uint64_t t0 = tiles * static_cast<uint64_t>(rank) / static_cast<uint64_t>(world);
+  const uint64_t t1 = tiles * static_cast<uint64_t>(rank + 1) / static_cast<uint64_t>(world);
+  const uint64_t r0 = std::min(m, t0 * kTileM), r1 = std::min(m, t1 * kTileM);
+  *begin = r0;
+  *count = r1 - r0;
+}
+
+// The geometry every rank derives from the same agreed numbers (largest row count over the
+// ranks, smallest device memory available), so every rank issues the same collectives.
+struct ShardPlan {
   uint64_t groups = 0; // row groups (0: nothing to do on any rank)
   uint64_t mg = 0;     // rows per group
   uint64_t nb = 0;     // C block width
@@ -265,31 +367,353 @@ struct Plan {
   uint64_t slice_elems = 0;
   uint64_t bytes_a_canon = 0, bytes_a_raw = 0, bytes_b_raw = 0, bytes_b_canon = 0,
            bytes_c = 0;
+  uint64_t device_bytes() const {
+    return bytes_a_canon + 2 * bytes_a_raw + kSlots * (bytes_b_raw + bytes_b_canon + bytes_c);
+  }
 };
 
-// Sizes the buffers for `mg` rows per group.
-void size_plan(Plan& pl, uint32_t op_a, uint32_t op_b, uint64_t n, uint64_t k, int P) {
+namespace {
+void size_plan(ShardPlan& pl, uint32_t op_a, uint32_t op_b, uint64_t k, int P) {
   pl.ldm = up4(std::max<uint64_t>(pl.mg, 1));
   pl.bytes_a_canon = pl.ldm * k * 4;
   pl.bytes_a_raw = op_a != 0 ? up4(pl.kb) * std::max<uint64_t>(pl.mg, 1) * 4 : 0;
   pl.bytes_c = pl.ldm * pl.nb * 4;
   if (op_b == 0) {
     pl.wc = (pl.nb + P - 1) / P;
+    pl.wk = 0;
     pl.slice_elems = pl.wc * pl.ldk;
     pl.bytes_b_raw = pl.slice_elems * static_cast<uint64_t>(P) * 4;
     pl.bytes_b_canon = pl.ldn * k * 4;
   } else {
     pl.wk = (k + P - 1) / P;
+    pl.wc = 0;
     pl.slice_elems = pl.wk * pl.ldn;
     pl.bytes_b_raw = 0;
     pl.bytes_b_canon = pl.slice_elems * static_cast<uint64_t>(P) * 4;
   }
-  (void)n;
+}
+} // namespace
+
+// Plans the call from the agreed numbers; false when not even one 128-row group fits.
+bool make_shard_plan(uint32_t op_a, uint32_t op_b, uint64_t m_max, uint64_t avail_min,
+                     uint64_t n, uint64_t k, int world, uint64_t panel_k, uint64_t block_n,
+                     ShardPlan* out) {
+  ShardPlan pl;
+  pl.kb = std::min<uint64_t>(up(panel_k > 0 ? panel_k : 1024, 32), up(k, 32));
+  pl.nb = std::min<uint64_t>(n, up(block_n, 32));
+  pl.ldk = up4(k);
+  pl.ldn = up4(pl.nb);
+  // Largest row group (multiple of 128 rows, at most all rows) whose buffers fit.
+  pl.mg = up(std::max<uint64_t>(m_max, 1), kTileM);
+  size_plan(pl, op_a, op_b, k, world);
+  while (pl.device_bytes() > avail_min && pl.mg > kTileM) {
+    pl.mg = std::max<uint64_t>(kTileM, up(pl.mg / 2, kTileM));
+    size_plan(pl, op_a, op_b, k, world);
+  }
+  pl.groups = m_max == 0 ? 0 : (m_max + pl.mg - 1) / pl.mg;
+  *out = pl;
+  return pl.device_bytes() <= avail_min;
 }
 
-uint64_t plan_bytes(const Plan& pl) {
-  return pl.bytes_a_canon + 2 * pl.bytes_a_raw +
-         kSlots * (pl.bytes_b_raw + pl.bytes_b_canon + pl.bytes_c);
+// Rank `rank`'s slice of C block [n0, n0 + nbj) of B: for op(B) = N (B stored K x N) the
+// block columns [*first, *first + *count) relative to n0; for op(B) = T (B stored N x K)
+// the k range [*first, *first + *count).
+void shard_b_slice(const ShardPlan& pl, uint32_t op_b, uint64_t nbj, uint64_t k, int rank,
+                   uint64_t* first, uint64_t* count) {
+  if (op_b == 0) {
+    const uint64_t c0 = static_cast<uint64_t>(rank) * pl.wc;
+    *first = c0;
+    *count = c0 < nbj ? std::min(pl.wc, nbj - c0) : 0;
+  } else {
+    const uint64_t q0 = static_cast<uint64_t>(rank) * pl.wk;
+    *first = q0;
+    *count = q0 < k ? std::min(pl.wk, k - q0) : 0;
+  }
+}
+
+} // namespace xvram
+
+namespace {
+
+xvram_status status_of(const xvram::Error& e) {
+  return e ? (e.status ? e.status : XVRAM_STATUS_CUDA_ERROR) : XVRAM_STATUS_SUCCESS;
+}
+
+// The body of xvram_b200_sgemm_sharded, with g's device current and g.mu held.
+xvram_status run_sharded(ShardGroup& g, uint32_t op_a, uint32_t op_b, uint64_t M, uint64_t N,
+                         uint64_t K, float alpha, const float* a, uint64_t lda, const float* b,
+                         uint64_t ldb, float beta, float* c, uint64_t ldc, int64_t panel_k) {
+  Device& d = *g.dev;
+  const int P = g.world, r = g.rank;
+  using xvram::CopyDir;
+  xvram_b200_shard_plan_v1 info{};
+  info.struct_size = sizeof info;
+  info.world = P;
+  info.rank = r;
+
+  // ---- 1. agree on the plan: max rows over ranks, min device memory available.
+  const uint64_t shape[6] = {M, N, K, op_a, op_b, static_cast<uint64_t>(panel_k)};
+  const auto now = std::chrono::steady_clock::now();
+  uint64_t avail = g.avail_sampled;
+  if (std::memcmp(shape, g.shape_sampled, sizeof shape) != 0 ||
+      now - g.when_sampled > std::chrono::seconds(1) || avail == 0) {
+    uint64_t free_b = 0, total_b = 0;
+    if (xvram::Error e = d.mem_get_info(&free_b, &total_b))
+      return status_of(e);
+    avail = free_b + g.held_bytes() - g.plan_dev.bytes;
+    g.avail_sampled = avail;
+    std::memcpy(g.shape_sampled, shape, sizeof shape);
+    g.when_sampled = now;
+  }
+  avail = avail > kHeadroomBytes ? avail - kHeadroomBytes : 0;
+  avail = std::min(avail, env_u64("XVRAM_B200_SHARD_BUDGET_BYTES", UINT64_MAX));
+  g.plan_host[0] = M;
+  g.plan_host[1] = UINT64_MAX - avail;
+  {
+    const uint64_t ph = reinterpret_cast<uint64_t>(g.plan_host);
+    xvram::Error e = d.copy_2d(g.plan_dev.p, 16, ph, 16, 16, 1, CopyDir::h2d, g.coll);
+    if (e) {
+      g.aborted = true;
+      return status_of(e);
+    }
+    if (P > 1) {
+      const xvram_status st = g.comm->all_reduce_max_u64(
+          reinterpret_cast<uint64_t*>(g.plan_dev.p), 2, d.native_stream(g.coll));
+      if (st != XVRAM_STATUS_SUCCESS) {
+        abort_group(g);
+        return st;
+      }
+    }
+    e = d.copy_2d(ph, 16, g.plan_dev.p, 16, 16, 1, CopyDir::d2h, g.coll);
+    if (!e)
+      e = d.event_record(g.plan_ev, g.coll);
+    if (e) {
+      g.aborted = true;
+      return status_of(e);
+    }
+    if (xvram_status st = bounded_wait(g, g.plan_ev); st != XVRAM_STATUS_SUCCESS)
+      return st;
+  }
+  const uint64_t m_max = g.plan_host[0];
+  const uint64_t avail_min = UINT64_MAX - g.plan_host[1];
+  info.m_max = m_max;
+  info.avail_min = avail_min;
+  if (m_max == 0) {
+    g.last = info;
+    return XVRAM_STATUS_SUCCESS; // no rank has rows: nothing to compute or gather
+  }
+
+  xvram::ShardPlan pl;
+  if (!xvram::make_shard_plan(op_a, op_b, m_max, avail_min, N, K, P,
+                              static_cast<uint64_t>(panel_k),
+                              env_u64("XVRAM_B200_SHARD_BLOCK_N", kDefaultBlockN), &pl))
+    return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY; // same verdict on every rank
+  info.row_groups = pl.groups;
+  info.group_rows = pl.mg;
+  info.block_n = pl.nb;
+  info.panel_k = pl.kb;
+  info.b_slice_cols = pl.wc;
+  info.b_slice_k = pl.wk;
+  info.slice_elems = pl.slice_elems;
+  info.device_bytes = pl.device_bytes();
+
+  // ---- 2. buffers (all released first when any must grow, so the old ones never
+  // coexist with the new ones).
+  {
+    constexpr int kData = ShardGroup::kBuffers - 1; // all but plan_dev
+    const uint64_t want[kData] = {pl.bytes_a_canon, pl.bytes_a_raw,   pl.bytes_a_raw,
+                                  pl.bytes_b_raw,   pl.bytes_b_raw,   pl.bytes_b_raw,
+                                  pl.bytes_b_canon, pl.bytes_b_canon, pl.bytes_b_canon,
+                                  pl.bytes_c,       pl.bytes_c,       pl.bytes_c};
+    bool grow = false;
+    for (int i = 0; i < kData; ++i)
+      grow = grow || g.buffers[i]->bytes < want[i];
+    bool ok = true;
+    if (grow) {
+      for (int i = 0; i < kData; ++i)
+        g.release(*g.buffers[i]);
+      for (int i = 0; i < kData && ok; ++i)
+        if (want[i])
+          ok = g.ensure(*g.buffers[i], want[i]);
+    }
+    if (!ok) {
+      // The other ranks planned with the same numbers; this rank failing leaves them to
+      // time out in the next all-gather, so the group is not reusable.
+      abort_group(g);
+      return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY;
+    }
+    const uint64_t panels = (K + pl.kb - 1) / pl.kb;
+    while (g.a_ev.size() < panels) {
+      EventId ev = 0;
+      if (xvram::Error e = d.event_create(&ev))
+        return status_of(e);
+      g.a_ev.push_back(ev);
+    }
+  }
+
+  // ---- 3. enqueue
+  const uint64_t ah = reinterpret_cast<uint64_t>(a), bh = reinterpret_cast<uint64_t>(b),
+                 ch = reinterpret_cast<uint64_t>(c);
+  const uint64_t a_canon = g.a_canon.p;
+  const uint64_t blocks = (N + pl.nb - 1) / pl.nb;
+  const uint64_t panels = (K + pl.kb - 1) / pl.kb;
+  const int64_t ldm = static_cast<int64_t>(pl.ldm), ldn = static_cast<int64_t>(pl.ldn);
+  const xvram::GemmTypes fp32{};
+  uint64_t q = 0; // global block counter: slot q % kSlots, compute stream q & 1
+  xvram::Error e;
+  auto h2d = [&](uint64_t dst, uint64_t dp, uint64_t src, uint64_t sp, uint64_t w, uint64_t h) {
+    info.h2d_bytes += w * h;
+    return d.copy_2d(dst, dp, src, sp, w, h, CopyDir::h2d, g.h2d);
+  };
+  for (uint64_t grp = 0; grp < pl.groups && !e; ++grp) {
+    const uint64_t r0 = grp * pl.mg;
+    const uint64_t mr = r0 < M ? std::min(pl.mg, M - r0) : 0;
+    if (grp > 0) {
+      // a_canon is rewritten: every kernel of the previous group must be done.
+      for (int i = 0; i < 2 && !e; ++i)
+        e = d.stream_wait_event(g.h2d, g.group_end[i]);
+      if (!e)
+        e = d.stream_wait_event(g.comp[0], g.group_end[1]);
+      if (!e)
+        e = d.stream_wait_event(g.comp[1], g.group_end[0]);
+    }
+    for (uint64_t j = 0; j < blocks && !e; ++j, ++q) {
+      const int s = static_cast<int>(q % kSlots);
+      const StreamId cs = g.comp[q & 1];
+      const uint64_t n0 = j * pl.nb, nbj = std::min(pl.nb, N - n0);
+      const uint64_t braw = g.b_raw[s].p, bcan = g.b_canon[s].p, cblk = g.c_blk[s].p;
+
+      // (a) this rank's slice of B's block j, then the in-place all-gather
+      uint64_t first = 0, count = 0;
+      xvram::shard_b_slice(pl, op_b, nbj, K, r, &first, &count);
+      e = d.stream_wait_event(g.h2d, g.b_free[s]);
+      if (!e && count) {
+        if (op_b == 0) // B stored K x N: block columns [first, first + count)
+          e = h2d(braw + first * pl.ldk * 4, pl.ldk * 4, bh + (n0 + first) * ldb * 4, ldb * 4,
+                  K * 4, count);
+        else // B stored N x K: k range [first, first + count) of rows [n0, n0 + nbj)
+          e = h2d(bcan + first * pl.ldn * 4, pl.ldn * 4, bh + (n0 + first * ldb) * 4, ldb * 4,
+                  nbj * 4, count);
+      }
+      if (!e)
+        e = d.event_record(g.b_loaded[s], g.h2d);
+      if (!e)
+        e = d.stream_wait_event(g.coll, g.b_loaded[s]);
+      if (!e && P > 1) {
+        float* base = reinterpret_cast<float*>(op_b == 0 ? braw : bcan);
+        const xvram_status st = g.comm->all_gather_f32(
+            base + static_cast<uint64_t>(r) * pl.slice_elems, base, pl.slice_elems,
+            d.native_stream(g.coll));
+        if (st != XVRAM_STATUS_SUCCESS) {
+          abort_group(g);
+          return st;
+        }
+        ++info.gathers;
+      }
+      if (!e && op_b == 0) // K-major block -> N-major (nbj x K, ld ldn)
+        e = d.transpose_f32(braw, static_cast<int64_t>(pl.ldk), bcan, ldn,
+                            static_cast<int64_t>(K), static_cast<int64_t>(nbj), g.coll);
+      if (!e)
+        e = d.event_record(g.b_ready[s], g.coll);
+
+      // (b) C's block j (rows [r0, r0 + mr) of this rank)
+      if (!e && mr > 0 && beta != 0.0f) {
+        e = d.stream_wait_event(g.h2d, g.c_free[s]);
+        if (!e)
+          e = h2d(cblk, pl.ldm * 4, ch + (r0 + n0 * ldc) * 4, ldc * 4, mr * 4, nbj);
+        if (!e)
+          e = d.event_record(g.c_loaded[s], g.h2d);
+      }
+
+      // (c) the kernel(s)
+      if (!e)
+        e = d.stream_wait_event(cs, g.b_ready[s]);
+      if (!e && mr > 0)
+        e = d.stream_wait_event(cs, beta != 0.0f ? g.c_loaded[s] : g.c_free[s]);
+      if (!e && mr > 0 && j == 0) {
+        // First block of the group: A arrives panel by panel and each panel's kernel
+        // starts as soon as it is resident (beta on the first, 1 afterwards).
+        for (uint64_t p = 0; p < panels && !e; ++p) {
+          const uint64_t k0 = p * pl.kb, kr = std::min(pl.kb, K - k0);
+          const int as = static_cast<int>(p & 1);
+          if (op_a == 0) { // A stored M x K: kr columns of mr floats
+            e = h2d(a_canon + k0 * pl.ldm * 4, pl.ldm * 4, ah + (r0 + k0 * lda) * 4, lda * 4,
+                    mr * 4, kr);
+            if (!e)
+              e = d.event_record(g.a_ev[p], g.h2d);
+            if (!e)
+              e = d.stream_wait_event(cs, g.a_ev[p]);
+          } else { // A stored K x M: mr columns of kr floats, then transposed on arrival
+            const uint64_t raw = g.a_raw[as].p;
+            e = d.stream_wait_event(g.h2d, g.a_free[as]);
+            if (!e)
+              e = h2d(raw, up4(pl.kb) * 4, ah + (k0 + r0 * lda) * 4, lda * 4, kr * 4, mr);
+            if (!e)
+              e = d.event_record(g.a_ev[p], g.h2d);
+            if (!e)
+              e = d.stream_wait_event(cs, g.a_ev[p]);
+            if (!e)
+              e = d.transpose_f32(raw, static_cast<int64_t>(up4(pl.kb)), a_canon + k0 * pl.ldm * 4,
+                                  ldm, static_cast<int64_t>(kr), static_cast<int64_t>(mr), cs);
+            if (!e)
+              e = d.event_record(g.a_free[as], cs);
+          }
+          if (!e && p + 1 == panels)
+            e = d.event_record(g.a_all, cs);
+          if (!e)
+            e = d.gemm(fp32, 0, 1, static_cast<int64_t>(mr), static_cast<int64_t>(nbj),
+                       static_cast<int64_t>(kr), alpha, a_canon + k0 * pl.ldm * 4, ldm,
+                       bcan + k0 * pl.ldn * 4, ldn, p == 0 ? beta : 1.0f, cblk, ldm, 0, 0, cs);
+        }
+      } else if (!e && mr > 0) {
+        e = d.stream_wait_event(cs, g.a_all);
+        if (!e)
+          e = d.gemm(fp32, 0, 1, static_cast<int64_t>(mr), static_cast<int64_t>(nbj),
+                     static_cast<int64_t>(K), alpha, a_canon, ldm, bcan, ldn, beta, cblk, ldm, 0,
+                     0, cs);
+      }
+      if (!e)
+        e = d.event_record(g.b_free[s], cs);
+
+      // (d) C's block j back to the host
+      if (!e && mr > 0) {
+        e = d.event_record(g.c_done[s], cs);
+        if (!e)
+          e = d.stream_wait_event(g.d2h, g.c_done[s]);
+        if (!e) {
+          info.d2h_bytes += mr * 4 * nbj;
+          e = d.copy_2d(ch + (r0 + n0 * ldc) * 4, ldc * 4, cblk, pl.ldm * 4, mr * 4, nbj,
+                        CopyDir::d2h, g.d2h);
+        }
+        if (!e)
+          e = d.event_record(g.c_free[s], g.d2h);
+      }
+    }
+    for (int i = 0; i < 2 && !e; ++i)
+      e = d.event_record(g.group_end[i], g.comp[i]);
+  }
+  // The call is over when both compute streams (which waited for every gather) and the
+  // last write-back are done.
+  for (int i = 0; i < 2 && !e; ++i)
+    e = d.stream_wait_event(g.d2h, g.group_end[i]);
+  if (!e)
+    e = d.event_record(g.out, g.d2h);
+  if (e) {
+    g.aborted = true;
+    return status_of(e);
+  }
+  xvram_status st = bounded_wait(g, g.out);
+  if (st == XVRAM_STATUS_SUCCESS) {
+    uint32_t word = 0;
+    if (d.kernel_status(g.d2h, &word))
+      st = XVRAM_STATUS_CUDA_ERROR;
+    else if (word)
+      st = XVRAM_STATUS_TIMEOUT;
+  }
+  if (st != XVRAM_STATUS_SUCCESS)
+    g.aborted = true;
+  g.last = info;
+  return st;
 }
 
 } // namespace
@@ -320,43 +744,20 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void*
   auto* g = new ShardGroup;
   g->rank = rank;
   g->world = world;
-  if (cudaGetDevice(&g->device) != cudaSuccess) {
-    delete g;
-    return XVRAM_STATUS_CUDA_ERROR;
-  }
-  cudaError_t e = cudaSuccess;
-  for (auto* s : {&g->h2d, &g->coll, &g->comp[0], &g->comp[1], &g->d2h})
-    if (e == cudaSuccess)
-      e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
-  for (auto* arr : {g->b_loaded, g->b_ready, g->b_free, g->c_loaded, g->c_done, g->c_free})
-    for (int i = 0; i < kSlots; ++i)
-      if (e == cudaSuccess)
-        e = cudaEventCreateWithFlags(&arr[i], cudaEventDisableTiming);
-  for (auto* arr : {g->a_free, g->group_end})
-    for (int i = 0; i < 2; ++i)
-      if (e == cudaSuccess)
-        e = cudaEventCreateWithFlags(&arr[i], cudaEventDisableTiming);
-  for (auto* ev : {&g->a_all, &g->out, &g->plan_ev})
-    if (e == cudaSuccess)
-      e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
-  if (e == cudaSuccess)
-    e = cudaHostAlloc(reinterpret_cast<void**>(&g->plan_host), 2 * sizeof(uint64_t),
-                      cudaHostAllocDefault);
-  if (e == cudaSuccess)
-    e = g->plan_dev.ensure(256);
-  if (e != cudaSuccess) {
+  if (xvram_status st = setup_group(*g); st != XVRAM_STATUS_SUCCESS) {
     destroy_group(g);
-    return XVRAM_STATUS_CUDA_ERROR;
+    return st;
   }
   ncclUniqueId id;
   std::memcpy(&id, unique_id, NCCL_UNIQUE_ID_BYTES);
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
-  ncclResult_t r = nccl().init_rank_config(&g->comm, world, id, rank, &cfg);
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = nccl().init_rank_config(&comm, world, id, rank, &cfg);
   const auto start = std::chrono::steady_clock::now();
   while (r == ncclInProgress || r == ncclSuccess) {
     ncclResult_t state = ncclSuccess;
-    if (nccl().async_error(g->comm, &state) != ncclSuccess) {
+    if (nccl().async_error(comm, &state) != ncclSuccess) {
       r = ncclInternalError;
       break;
     }
@@ -364,21 +765,60 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create(const void*
       r = state;
       break;
     }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count() >
-        kInitTimeoutS) {
+    if (seconds_since(start) > kInitTimeoutS) {
       r = ncclInternalError;
       break;
     }
     std::this_thread::sleep_for(std::chrono::milliseconds(1));
   }
   if (r != ncclSuccess) {
-    if (g->comm)
-      nccl().abort(g->comm);
-    g->comm = nullptr;
+    if (comm)
+      nccl().abort(comm);
     destroy_group(g);
     return XVRAM_STATUS_UNAVAILABLE;
   }
+  g->comm = std::make_unique<NcclComm>(comm);
   *out_group = reinterpret_cast<uint64_t>(g);
+  return XVRAM_STATUS_SUCCESS;
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_group_create_custom(
+    const xvram_b200_shard_collectives_v1* ops, int32_t rank, int32_t world,
+    uint64_t* out_group) {
+  if (!ops || ops->struct_size < sizeof(xvram_b200_shard_collectives_v1) || !out_group ||
+      world < 1 || rank < 0 || rank >= world || !ops->all_reduce_max_u64 || !ops->all_gather_f32)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  auto* g = new ShardGroup;
+  g->rank = rank;
+  g->world = world;
+  if (xvram_status st = setup_group(*g); st != XVRAM_STATUS_SUCCESS) {
+    destroy_group(g);
+    return st;
+  }
+  g->comm = std::make_unique<CallbackComm>(*ops);
+  *out_group = reinterpret_cast<uint64_t>(g);
+  return XVRAM_STATUS_SUCCESS;
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_rows(int64_t m, int32_t world,
+                                                           int32_t rank, int64_t* row_begin,
+                                                           int64_t* row_count) {
+  if (m < 0 || world < 1 || rank < 0 || rank >= world || !row_begin || !row_count)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  uint64_t b0 = 0, n = 0;
+  xvram::shard_rows(static_cast<uint64_t>(m), world, rank, &b0, &n);
+  *row_begin = static_cast<int64_t>(b0);
+  *row_count = static_cast<int64_t>(n);
+  return XVRAM_STATUS_SUCCESS;
+}
+
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_last_plan(uint64_t group,
+                                                                xvram_b200_shard_plan_v1* out) {
+  auto* g = reinterpret_cast<ShardGroup*>(group);
+  if (!g || !out || out->struct_size < sizeof(xvram_b200_shard_plan_v1))
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g->mu);
+  *out = g->last;
   return XVRAM_STATUS_SUCCESS;
 }
 
@@ -394,6 +834,7 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_allgather_rows(
     return XVRAM_STATUS_INVALID_ARGUMENT;
   if (g->aborted)
     return XVRAM_STATUS_POISONED;
+  // Device pointers and a native stream of the caller: CUDA devices only.
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   float* stage = static_cast<float*>(staging);
   float* mine = stage + per_rank * static_cast<uint64_t>(g->rank);
@@ -405,11 +846,13 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_allgather_rows(
   if (e != cudaSuccess)
     return XVRAM_STATUS_CUDA_ERROR;
   // 2. every rank's block into every rank's staging buffer (in place)
-  if (g->world > 1)
-    if (xvram_status st = nccl_issued(*g, nccl().all_gather(mine, stage, per_rank, ncclFloat,
-                                                            g->comm, s));
-        st != XVRAM_STATUS_SUCCESS)
+  if (g->world > 1) {
+    const xvram_status st = g->comm->all_gather_f32(mine, stage, per_rank, stream);
+    if (st != XVRAM_STATUS_SUCCESS) {
+      abort_group(*g);
       return st;
+    }
+  }
   // 3. block q becomes rows [q rows, (q + 1) rows) of dst
   for (int q = 0; q < g->world; ++q) {
     e = cudaMemcpy2DAsync(dst + static_cast<uint64_t>(q) * static_cast<uint64_t>(rows),
@@ -439,292 +882,14 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
   std::lock_guard<std::mutex> lock(g->mu);
   if (g->aborted || !g->comm)
     return XVRAM_STATUS_POISONED;
-  int saved = 0;
-  cudaGetDevice(&saved);
-  cudaSetDevice(g->device);
-  struct Restore {
-    int d;
-    ~Restore() { cudaSetDevice(d); }
-  } restore{saved};
-
-  const int P = g->world, r = g->rank;
-  const uint64_t M = static_cast<uint64_t>(m_local), N = static_cast<uint64_t>(n),
-                 K = static_cast<uint64_t>(k);
-
-  // ---- 1. agree on the plan: max rows over ranks, min device memory available.
-  const uint64_t shape[6] = {M, N, K, op_a, op_b, static_cast<uint64_t>(panel_k)};
-  const auto now = std::chrono::steady_clock::now();
-  uint64_t avail = g->avail_sampled;
-  if (std::memcmp(shape, g->shape_sampled, sizeof shape) != 0 ||
-      now - g->when_sampled > std::chrono::seconds(1) || avail == 0) {
-    uint64_t free_b = 0, total_b = 0;
-    if (cudaError_t e = cudaMemGetInfo(&free_b, &total_b); e != cudaSuccess)
-      return cuda_status(e);
-    avail = free_b + g->held_bytes() - g->plan_dev.bytes;
-    g->avail_sampled = avail;
-    std::memcpy(g->shape_sampled, shape, sizeof shape);
-    g->when_sampled = now;
-  }
-  avail = avail > kHeadroomBytes ? avail - kHeadroomBytes : 0;
-  avail = std::min(avail, env_u64("XVRAM_B200_SHARD_BUDGET_BYTES", UINT64_MAX));
-  g->plan_host[0] = M;
-  g->plan_host[1] = UINT64_MAX - avail;
-  {
-    cudaError_t e = cudaMemcpyAsync(g->plan_dev.p, g->plan_host, 2 * sizeof(uint64_t),
-                                    cudaMemcpyHostToDevice, g->coll);
-    if (e != cudaSuccess) {
-      g->aborted = true;
-      return cuda_status(e);
-    }
-    if (P > 1) {
-      if (xvram_status st = nccl_issued(
-              *g, nccl().all_reduce(g->plan_dev.p, g->plan_dev.p, 2, ncclUint64, ncclMax, g->comm,
-                                    g->coll));
-          st != XVRAM_STATUS_SUCCESS)
-        return st;
-    }
-    e = cudaMemcpyAsync(g->plan_host, g->plan_dev.p, 2 * sizeof(uint64_t), cudaMemcpyDeviceToHost,
-                        g->coll);
-    if (e == cudaSuccess)
-      e = cudaEventRecord(g->plan_ev, g->coll);
-    if (e != cudaSuccess) {
-      g->aborted = true;
-      return cuda_status(e);
-    }
-    if (xvram_status st = bounded_wait(*g, g->plan_ev); st != XVRAM_STATUS_SUCCESS)
-      return st;
-  }
-  const uint64_t m_max = g->plan_host[0];
-  const uint64_t avail_min = UINT64_MAX - g->plan_host[1];
-  if (m_max == 0)
-    return XVRAM_STATUS_SUCCESS; // no rank has rows: nothing to compute or gather
-
-  Plan pl;
-  pl.kb = std::min<uint64_t>(up(panel_k > 0 ? static_cast<uint64_t>(panel_k) : 1024, 32), up(K, 32));
-  pl.nb = std::min<uint64_t>(N, up(env_u64("XVRAM_B200_SHARD_BLOCK_N", kDefaultBlockN), 32));
-  pl.ldk = up4(K);
-  pl.ldn = up4(pl.nb);
-  // Largest row group (multiple of 128 rows, at most all rows) whose buffers fit.
-  pl.mg = up(m_max, kTileM);
-  size_plan(pl, op_a, op_b, N, K, P);
-  while (plan_bytes(pl) > avail_min && pl.mg > kTileM) {
-    pl.mg = std::max<uint64_t>(kTileM, up(pl.mg / 2, kTileM));
-    size_plan(pl, op_a, op_b, N, K, P);
-  }
-  if (plan_bytes(pl) > avail_min)
-    return XVRAM_STATUS_DEVICE_OUT_OF_MEMORY; // same verdict on every rank
-  pl.groups = (m_max + pl.mg - 1) / pl.mg;
-
-  // ---- 2. buffers (all released first when any must grow, so the old ones never
-  // coexist with the new ones).
-  {
-    constexpr int kData = ShardGroup::kBuffers - 1; // all but plan_dev
-    const uint64_t want[kData] = {pl.bytes_a_canon, pl.bytes_a_raw,   pl.bytes_a_raw,
-                                  pl.bytes_b_raw,   pl.bytes_b_raw,   pl.bytes_b_raw,
-                                  pl.bytes_b_canon, pl.bytes_b_canon, pl.bytes_b_canon,
-                                  pl.bytes_c,       pl.bytes_c,       pl.bytes_c};
-    bool grow = false;
-    for (int i = 0; i < kData; ++i)
-      grow = grow || g->buffers[i]->bytes < want[i];
-    cudaError_t e = cudaSuccess;
-    if (grow) {
-      for (int i = 0; i < kData; ++i)
-        g->buffers[i]->release();
-      for (int i = 0; i < kData && e == cudaSuccess; ++i)
-        if (want[i])
-          e = g->buffers[i]->ensure(want[i]);
-    }
-    if (e != cudaSuccess) {
-      // The other ranks planned with the same numbers; this rank failing leaves them to
-      // time out in the next all-gather, so the group is not reusable.
-      abort_group(*g);
-      return cuda_status(e);
-    }
-    const uint64_t panels = (K + pl.kb - 1) / pl.kb;
-    while (g->a_ev.size() < panels) {
-      cudaEvent_t ev = nullptr;
-      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
-        return cuda_status(e);
-      g->a_ev.push_back(ev);
-    }
-  }
-
-  // ---- 3. enqueue
-  const char* ah = reinterpret_cast<const char*>(a);
-  const char* bh = reinterpret_cast<const char*>(b);
-  char* ch = reinterpret_cast<char*>(c);
-  float* a_canon = static_cast<float*>(g->a_canon.p);
-  const uint64_t blocks = (N + pl.nb - 1) / pl.nb;
-  const uint64_t panels = (K + pl.kb - 1) / pl.kb;
-  const long long ldm = static_cast<long long>(pl.ldm), ldn = static_cast<long long>(pl.ldn);
-  uint64_t q = 0; // global block counter: slot q % kSlots, compute stream q & 1
-  cudaError_t e = cudaSuccess;
-  for (uint64_t grp = 0; grp < pl.groups && e == cudaSuccess; ++grp) {
-    const uint64_t r0 = grp * pl.mg;
-    const uint64_t mr = r0 < M ? std::min(pl.mg, M - r0) : 0;
-    if (grp > 0) {
-      // a_canon is rewritten: every kernel of the previous group must be done.
-      for (int i = 0; i < 2 && e == cudaSuccess; ++i)
-        e = cudaStreamWaitEvent(g->h2d, g->group_end[i], 0);
-      if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(g->comp[0], g->group_end[1], 0);
-      if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(g->comp[1], g->group_end[0], 0);
-    }
-    for (uint64_t j = 0; j < blocks && e == cudaSuccess; ++j, ++q) {
-      const int s = static_cast<int>(q % kSlots);
-      cudaStream_t cs = g->comp[q & 1];
-      const uint64_t n0 = j * pl.nb, nbj = std::min(pl.nb, N - n0);
-      char* braw = static_cast<char*>(g->b_raw[s].p);
-      char* bcan = static_cast<char*>(g->b_canon[s].p);
-      const float* bcanf = reinterpret_cast<const float*>(bcan);
-      float* cblk = static_cast<float*>(g->c_blk[s].p);
-
-      // (a) this rank's slice of B's block j, then the in-place all-gather
-      e = cudaStreamWaitEvent(g->h2d, g->b_free[s], 0);
-      if (e == cudaSuccess) {
-        if (op_b == 0) { // B stored K x N: slice = columns [c0, c0 + wc) of the block
-          const uint64_t c0 = static_cast<uint64_t>(r) * pl.wc;
-          const uint64_t cols = c0 < nbj ? std::min(pl.wc, nbj - c0) : 0;
-          if (cols)
-            e = cudaMemcpy2DAsync(braw + c0 * pl.ldk * 4, pl.ldk * 4,
-                                  bh + (n0 + c0) * static_cast<uint64_t>(ldb) * 4,
-                                  static_cast<size_t>(ldb) * 4, K * 4, cols,
-                                  cudaMemcpyHostToDevice, g->h2d);
-        } else { // B stored N x K: slice = k range [q0, q0 + wk) of rows [n0, n0 + nbj)
-          const uint64_t q0 = static_cast<uint64_t>(r) * pl.wk;
-          const uint64_t ks = q0 < K ? std::min(pl.wk, K - q0) : 0;
-          if (ks)
-            e = cudaMemcpy2DAsync(bcan + q0 * pl.ldn * 4, pl.ldn * 4,
-                                  bh + (n0 + q0 * static_cast<uint64_t>(ldb)) * 4,
-                                  static_cast<size_t>(ldb) * 4, nbj * 4, ks,
-                                  cudaMemcpyHostToDevice, g->h2d);
-        }
-      }
-      if (e == cudaSuccess)
-        e = cudaEventRecord(g->b_loaded[s], g->h2d);
-      if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(g->coll, g->b_loaded[s], 0);
-      if (e == cudaSuccess && P > 1) {
-        char* base = op_b == 0 ? braw : bcan;
-        if (xvram_status st = nccl_issued(
-                *g, nccl().all_gather(base + static_cast<uint64_t>(r) * pl.slice_elems * 4, base,
-                                      pl.slice_elems, ncclFloat, g->comm, g->coll));
-            st != XVRAM_STATUS_SUCCESS)
-          return st;
-      }
-      if (e == cudaSuccess && op_b == 0) // K-major block -> N-major (nbj x K, ld ldn)
-        e = xvram::transpose_f32_async(reinterpret_cast<const float*>(braw),
-                                       static_cast<long long>(pl.ldk),
-                                       reinterpret_cast<float*>(bcan), ldn, static_cast<int>(K),
-                                       static_cast<int>(nbj), g->coll);
-      if (e == cudaSuccess)
-        e = cudaEventRecord(g->b_ready[s], g->coll);
-
-      // (b) C's block j (rows [r0, r0 + mr) of this rank)
-      if (e == cudaSuccess && mr > 0 && beta != 0.0f) {
-        e = cudaStreamWaitEvent(g->h2d, g->c_free[s], 0);
-        if (e == cudaSuccess)
-          e = cudaMemcpy2DAsync(cblk, pl.ldm * 4,
-                                ch + (r0 + n0 * static_cast<uint64_t>(ldc)) * 4,
-                                static_cast<size_t>(ldc) * 4, mr * 4, nbj, cudaMemcpyHostToDevice,
-                                g->h2d);
-        if (e == cudaSuccess)
-          e = cudaEventRecord(g->c_loaded[s], g->h2d);
-      }
-
-      // (c) the kernel(s)
-      if (e == cudaSuccess)
-        e = cudaStreamWaitEvent(cs, g->b_ready[s], 0);
-      if (e == cudaSuccess && mr > 0)
-        e = cudaStreamWaitEvent(cs, beta != 0.0f ? g->c_loaded[s] : g->c_free[s], 0);
-      if (e == cudaSuccess && mr > 0 && j == 0) {
-        // First block of the group: A arrives panel by panel and each panel's kernel
-        // starts as soon as it is resident (beta on the first, 1 afterwards).
-        for (uint64_t p = 0; p < panels && e == cudaSuccess; ++p) {
-          const uint64_t k0 = p * pl.kb, kr = std::min(pl.kb, K - k0);
-          const int as = static_cast<int>(p & 1);
-          if (op_a == 0) { // A stored M x K: kr columns of mr floats
-            e = cudaMemcpy2DAsync(a_canon + k0 * pl.ldm, pl.ldm * 4,
-                                  ah + (r0 + k0 * static_cast<uint64_t>(lda)) * 4,
-                                  static_cast<size_t>(lda) * 4, mr * 4, kr, cudaMemcpyHostToDevice,
-                                  g->h2d);
-            if (e == cudaSuccess)
-              e = cudaEventRecord(g->a_ev[p], g->h2d);
-            if (e == cudaSuccess)
-              e = cudaStreamWaitEvent(cs, g->a_ev[p], 0);
-          } else { // A stored K x M: mr columns of kr floats, then transposed on arrival
-            float* raw = static_cast<float*>(g->a_raw[as].p);
-            e = cudaStreamWaitEvent(g->h2d, g->a_free[as], 0);
-            if (e == cudaSuccess)
-              e = cudaMemcpy2DAsync(raw, up4(pl.kb) * 4,
-                                    ah + (k0 + r0 * static_cast<uint64_t>(lda)) * 4,
-                                    static_cast<size_t>(lda) * 4, kr * 4, mr,
-                                    cudaMemcpyHostToDevice, g->h2d);
-            if (e == cudaSuccess)
-              e = cudaEventRecord(g->a_ev[p], g->h2d);
-            if (e == cudaSuccess)
-              e = cudaStreamWaitEvent(cs, g->a_ev[p], 0);
-            if (e == cudaSuccess)
-              e = xvram::transpose_f32_async(raw, static_cast<long long>(up4(pl.kb)),
-                                             a_canon + k0 * pl.ldm, ldm, static_cast<int>(kr),
-                                             static_cast<int>(mr), cs);
-            if (e == cudaSuccess)
-              e = cudaEventRecord(g->a_free[as], cs);
-          }
-          if (e == cudaSuccess && p + 1 == panels)
-            e = cudaEventRecord(g->a_all, cs);
-          if (e == cudaSuccess)
-            e = xvram::sgemm_ffma(0, 1, static_cast<int>(mr), static_cast<int>(nbj),
-                                  static_cast<int>(kr), alpha, a_canon + k0 * pl.ldm, ldm,
-                                  bcanf + k0 * pl.ldn, ldn, p == 0 ? beta : 1.0f, cblk, ldm, cs);
-        }
-      } else if (e == cudaSuccess && mr > 0) {
-        e = cudaStreamWaitEvent(cs, g->a_all, 0);
-        if (e == cudaSuccess)
-          e = xvram::sgemm_ffma(0, 1, static_cast<int>(mr), static_cast<int>(nbj),
-                                static_cast<int>(K), alpha, a_canon, ldm, bcanf, ldn, beta, cblk,
-                                ldm, cs);
-      }
-      if (e == cudaSuccess)
-        e = cudaEventRecord(g->b_free[s], cs);
-
-      // (d) C's block j back to the host
-      if (e == cudaSuccess && mr > 0) {
-        e = cudaEventRecord(g->c_done[s], cs);
-        if (e == cudaSuccess)
-          e = cudaStreamWaitEvent(g->d2h, g->c_done[s], 0);
-        if (e == cudaSuccess)
-          e = cudaMemcpy2DAsync(ch + (r0 + n0 * static_cast<uint64_t>(ldc)) * 4,
-                                static_cast<size_t>(ldc) * 4, cblk, pl.ldm * 4, mr * 4, nbj,
-                                cudaMemcpyDeviceToHost, g->d2h);
-        if (e == cudaSuccess)
-          e = cudaEventRecord(g->c_free[s], g->d2h);
-      }
-    }
-    for (int i = 0; i < 2 && e == cudaSuccess; ++i)
-      e = cudaEventRecord(g->group_end[i], g->comp[i]);
-  }
-  // The call is over when both compute streams (which waited for every gather) and the
-  // last write-back are done.
-  for (int i = 0; i < 2 && e == cudaSuccess; ++i)
-    e = cudaStreamWaitEvent(g->d2h, g->group_end[i], 0);
-  if (e == cudaSuccess)
-    e = cudaEventRecord(g->out, g->d2h);
-  if (e != cudaSuccess) {
-    g->aborted = true;
-    return cuda_status(e);
-  }
-  xvram_status st = bounded_wait(*g, g->out);
-  if (st == XVRAM_STATUS_SUCCESS) {
-    unsigned int word = 0;
-    if (xvram::read_and_clear_kernel_error(&word, g->d2h) != cudaSuccess)
-      st = XVRAM_STATUS_CUDA_ERROR;
-    else if (word)
-      st = XVRAM_STATUS_TIMEOUT;
-  }
-  if (st != XVRAM_STATUS_SUCCESS)
-    g->aborted = true;
+  int previous = 0;
+  if (xvram::Error e = g->dev->make_current(&previous))
+    return status_of(e);
+  const xvram_status st =
+      run_sharded(*g, op_a, op_b, static_cast<uint64_t>(m_local), static_cast<uint64_t>(n),
+                  static_cast<uint64_t>(k), alpha, a, static_cast<uint64_t>(lda), b,
+                  static_cast<uint64_t>(ldb), beta, c, static_cast<uint64_t>(ldc), panel_k);
+  g->dev->restore_current(previous);
   return st;
 }
 
