@@ -231,7 +231,10 @@ def test_workspace_query():
 @pytest.mark.parametrize("op_a,op_b", [(0, 1), (1, 0)])
 @pytest.mark.parametrize("shape", [(2560, 2048, 96),   # 160 tiles: 12-tile tail, split
                                    (1300, 700, 64),    # 33 tiles: all half-width
-                                   (2560, 1280, 64)])  # 100 tiles: tail too big to split
+                                   (2560, 1280, 64),   # 100 tiles: tail too big to split
+                                   (2000, 3000, 700),  # 192 tiles: 44-tile tail, split
+                                   (4096, 8192, 160),  # 1024 tiles: 136-tile tail, not split
+                                   (2560, 1280, 256)])  # 100 tiles: one partial wave
 def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape):
     """The TMA kernel runs a last, at most half-full wave as half-width tiles; every output
     is still one FFMA chain in k order, so its bits equal the generic kernel's."""
@@ -242,3 +245,4 @@ def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape):
         outs.append(out)
     assert np.array_equal(outs[0], outs[1])
     check(outs[0], ref, c, m, k, a, b)
+

@@ -21,6 +21,11 @@ constexpr double kStepOverheadS = 15e-6; // launch + event bookkeeping per step
 // (fewer steps) amortise it; measured at ~1 ms per 16384 x 16384 step (55 waves).
 constexpr double kTileFixedS = 12e-6;
 constexpr int64_t kMaxSteps = 1 << 15;     // steps a plan may have
+// Plans predicted within this fraction of the fastest are treated as equally fast, and the
+// one that moves the fewest host bytes wins: the time model is approximate to about this
+// much, while host traffic decides how far the link stays from saturation -- and links are
+// shared when several GPUs of a node stream at once.
+constexpr double kTrafficSlack = 0.02;
 constexpr int kMaxSimulations = 96;          // candidates simulated per plan
 constexpr int32_t kNever = INT32_MAX;
 
@@ -345,23 +350,36 @@ PlanStatus make_panel_plan(const PlanProblem& p, const PlanLimits& lim, Plan* ou
     std::stable_sort(cands.begin(), cands.end(),
                      [](const Cand& x, const Cand& y) { return x.lb < y.lb; });
 
+    // Every simulated plan is kept; the choice is made once the search ends (fewest H2D
+    // bytes among the plans within kTrafficSlack of the fastest, then fewest steps).
+    std::vector<std::pair<Geo, Plan>> sims;
+    double fastest = 0.0;
     for (const Cand& cd : cands) {
-      if (found && (cd.lb > best_plan.est_seconds || considered >= kMaxSimulations))
+      if (!sims.empty() &&
+          (cd.lb > fastest * (1 + kTrafficSlack) || considered >= kMaxSimulations))
         break;
       if (!simulate(p, lim, cd.g, false, &trial))
         continue;
       ++considered;
+      if (sims.empty() || trial.est_seconds < fastest)
+        fastest = trial.est_seconds;
+      sims.emplace_back(cd.g, trial);
+    }
+    for (const auto& [g, pl] : sims) {
+      if (pl.est_seconds > fastest * (1 + kTrafficSlack))
+        continue;
       const bool better =
-          !found || trial.est_seconds < best_plan.est_seconds * (1 - 1e-9) ||
-          (trial.est_seconds <= best_plan.est_seconds * (1 + 1e-9) &&
-           (trial.h2d_bytes < best_plan.h2d_bytes ||
-            (trial.h2d_bytes == best_plan.h2d_bytes &&
-             trial.blocks_m * trial.blocks_n * trial.panels_k <
-                 best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k)));
+          !found || pl.h2d_bytes < best_plan.h2d_bytes ||
+          (pl.h2d_bytes == best_plan.h2d_bytes &&
+           (pl.blocks_m * pl.blocks_n * pl.panels_k <
+                best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k ||
+            (pl.blocks_m * pl.blocks_n * pl.panels_k ==
+                 best_plan.blocks_m * best_plan.blocks_n * best_plan.panels_k &&
+             pl.est_seconds < best_plan.est_seconds)));
       if (better) {
         found = true;
-        best = cd.g;
-        best_plan = trial;
+        best = g;
+        best_plan = pl;
       }
     }
     if (found || forced)

@@ -96,8 +96,8 @@ struct FfmaParams {
   int m, n, k;
   int k_tiles;
   int tiles_m, tiles_n;
-  // Blocks [0, full_tiles) compute whole tiles; every later pair of blocks splits one of
-  // the remaining tiles into two half-width tiles (see launch_tma).
+  // Work units [0, full_tiles) are whole tiles; every later pair of units splits one of
+  // the remaining tiles into two half-width tiles (see launch_tma).  Unit u runs as block u.
   int full_tiles;
   float alpha, beta;
   float* c;
@@ -261,6 +261,103 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tmap_a, const CUt
     tma_load_2d(sb, tmap_b, &full[s], n0, k0);
 }
 
+// After a wait ran out: never leave the CTA with copies still landing in its shared
+// memory.  Thread 0 waits for the last fill of every slot it armed (loads
+// [issued - kStages, issued) of its running count), with a bound ten times the pipeline
+// wait's, since only a copy the hardware never completes can reach it; past that bound
+// bit 2 of the error word is set and the CTA returns anyway.
+__device__ __forceinline__ void drain_loads(uint64_t* full, int issued,
+                                            unsigned long long timeout_ns) {
+  for (int L = issued > kStages ? issued - kStages : 0; L < issued; ++L)
+    if (!mbar_wait_bounded(&full[L % kStages], (L / kStages) & 1, 10ull * timeout_ns)) {
+      atomicOr(&xvram_kernel_error, 4u);
+      return;
+    }
+}
+
+// Where work unit u sits in C.  Grouped rasterisation: 8 consecutive M tiles sweep the N
+// tiles together so the B stage tiles they share stay in L2.  A half unit's TMA box starts
+// at its own first column; the box's second half (columns of the partner, or past N where
+// TMA fills zeros) is loaded and not used.
+struct UnitCoords {
+  int m0, n0;
+  bool half;
+};
+template <int BN> __device__ __forceinline__ UnitCoords unit_coords(const FfmaParams& p, int u) {
+  const bool half = u >= p.full_tiles;
+  const int tile_lin = half ? p.full_tiles + ((u - p.full_tiles) >> 1) : u;
+  const int half_index = half ? ((u - p.full_tiles) & 1) : 0;
+  const int group_span = 8 * p.tiles_n;
+  const int first_m = (tile_lin / group_span) * 8;
+  const int group_m = min(8, p.tiles_m - first_m);
+  const int tile_m = first_m + (tile_lin % group_span) % group_m;
+  const int tile_n = (tile_lin % group_span) / group_m;
+  return {tile_m * kBM, tile_n * BN + half_index * (BN / 2), half};
+}
+
+// The epilogue reads this thread's C entries; ask L2 for their lines before the K loop,
+// so those reads hit L2 afterwards instead of waiting on DRAM.
+template <bool A_KMAJOR, bool B_KMAJOR, int NJ>
+__device__ __forceinline__ void prefetch_c(const FfmaParams& p, int m0, int n0) {
+  if (p.beta == 0.0f)
+    return;
+  const int tm = threadIdx.x & 15;
+  const int tn = threadIdx.x >> 4;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
+    if (col < p.n) {
+      const float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+      for (int i = 0; i < 8; i += (A_KMAJOR ? 1 : 4)) { // M-major rows come in fours
+        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+        if (row < p.m)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(cc + row));
+      }
+    }
+  }
+}
+
+// C = alpha * acc + beta * C for the thread's 8 x NJ entries, two columns at a time: their
+// 16 C reads are issued before any store (a read after a store to another column would
+// wait for it -- the addresses are not provably distinct).
+template <bool A_KMAJOR, bool B_KMAJOR, int NJ>
+__device__ __forceinline__ void epilogue(const FfmaParams& p, int m0, int n0,
+                                         float2 (&acc)[8][NJ / 2]) {
+  const int tm = threadIdx.x & 15;
+  const int tn = threadIdx.x >> 4;
+  const float alpha = p.alpha, beta = p.beta;
+#pragma unroll
+  for (int j0 = 0; j0 < NJ; j0 += 2) {
+    float cv[2][8];
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      const float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+        cv[jj][i] = (beta != 0.0f && col < p.n && row < p.m) ? cc[row] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      if (col >= p.n)
+        continue;
+      float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
+        if (row < p.m) {
+          const float v = alpha * acc_at(acc[i][(j0 + jj) >> 1], jj & 1);
+          cc[row] = (beta == 0.0f) ? v : fmaf(beta, cv[jj][i], v);
+        }
+      }
+    }
+  }
+}
+
 // The K loop and epilogue of one CTA tile computing the thread's first NJ columns (NJ = TN
 // for a whole tile, TN / 2 for a half-width tile).  Every output element is one FFMA chain
 // in k order whichever NJ computes it, so whole and half tiles give identical bits.
@@ -273,23 +370,7 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
   const int tid = threadIdx.x;
   const int tm = tid & 15;
   const int tn = tid >> 4;
-  // The epilogue reads this thread's C entries; ask L2 for their lines now, so those reads
-  // hit L2 after the K loop instead of waiting on DRAM.
-  if (p.beta != 0.0f) {
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int col = n0 + frag_index<B_KMAJOR>(tn, j);
-      if (col < p.n) {
-        const float* cc = p.c + static_cast<long long>(col) * p.ldc;
-#pragma unroll
-        for (int i = 0; i < 8; i += (A_KMAJOR ? 1 : 4)) { // M-major rows come in fours
-          const int row = m0 + frag_index<A_KMAJOR>(tm, i);
-          if (row < p.m)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(cc + row));
-        }
-      }
-    }
-  }
+  prefetch_c<A_KMAJOR, B_KMAJOR, NJ>(p, m0, n0);
   float2 acc[8][NJ / 2];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -337,50 +418,12 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
     }
   }
   if (aborted) {
-    // Never leave the CTA with copies still landing in its shared memory: thread 0 waits
-    // (bounded) for the last fill of every stage it armed; then everyone returns.
     if (tid == 0)
-      for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
-        if (!mbar_wait_bounded(&full[kt % kStages], (kt / kStages) & 1, p.timeout_ns)) {
-          atomicOr(&xvram_kernel_error, 4u);
-          break;
-        }
+      drain_loads(full, issued, p.timeout_ns);
     return;
   }
 
-  // ------------------------------------------------------------------- epilogue
-  // Two columns at a time: their 16 C reads are issued before any store (a read after a
-  // store to another column would wait for it -- the addresses are not provably distinct).
-  const float alpha = p.alpha, beta = p.beta;
-#pragma unroll
-  for (int j0 = 0; j0 < NJ; j0 += 2) {
-    float cv[2][8];
-#pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
-      const float* cc = p.c + static_cast<long long>(col) * p.ldc;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
-        cv[jj][i] = (beta != 0.0f && col < p.n && row < p.m) ? cc[row] : 0.0f;
-      }
-    }
-#pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
-      if (col >= p.n)
-        continue;
-      float* cc = p.c + static_cast<long long>(col) * p.ldc;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = m0 + frag_index<A_KMAJOR>(tm, i);
-        if (row < p.m) {
-          const float v = alpha * acc_at(acc[i][(j0 + jj) >> 1], jj & 1);
-          cc[row] = (beta == 0.0f) ? v : fmaf(beta, cv[jj][i], v);
-        }
-      }
-    }
-  }
+  epilogue<A_KMAJOR, B_KMAJOR, NJ>(p, m0, n0, acc);
 }
 
 template <bool A_KMAJOR, bool B_KMAJOR, int TN>
@@ -401,21 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Blocks past full_tiles come in pairs that share one tile, each taking half of its
   // columns: the last, partial wave then lasts about half a tile.
-  const int bid = blockIdx.x;
-  const bool half = bid >= p.full_tiles;
-  const int tile_lin = half ? p.full_tiles + ((bid - p.full_tiles) >> 1) : bid;
-  const int half_index = half ? ((bid - p.full_tiles) & 1) : 0;
-  // Grouped rasterisation: 8 consecutive M tiles sweep the N tiles together so the
-  // B stage tiles they share stay in L2.
-  const int group_span = 8 * p.tiles_n;
-  const int first_m = (tile_lin / group_span) * 8;
-  const int group_m = min(8, p.tiles_m - first_m);
-  const int tile_m = first_m + (tile_lin % group_span) % group_m;
-  const int tile_n = (tile_lin % group_span) / group_m;
-  const int m0 = tile_m * kBM;
-  // A half tile's TMA box starts at its own first column; the box's second half (columns
-  // of the partner, or past N where TMA fills zeros) is loaded and not used.
-  const int n0 = tile_n * BN + half_index * (BN / 2);
+  const UnitCoords uc = unit_coords<BN>(p, blockIdx.x);
+  const bool half = uc.half;
+  const int m0 = uc.m0, n0 = uc.n0;
 
   const int tid = threadIdx.x;
   if (tid == 0) {
