@@ -377,6 +377,10 @@ typedef struct xvram_b200_runtime_info_v1 {
      those kernels ran as. */
   uint64_t gemm_deferred;
   uint64_t gemm_column_blocks;
+  /* Streamed GEMMs: panel loads into a slot that held another panel (the slot's frames stay
+     mapped, so the reference-format counters -- evictions and handle reuses, which count
+     VMM unmaps and remaps -- do not include them). */
+  uint64_t panel_slot_refills;
 } xvram_b200_runtime_info_v1;
 
 XVRAM_B200_API xvram_status XVRAM_CALL

@@ -195,10 +195,12 @@ def scenario_out_of_core(oracle):
                handle_reuses=t.runtime.handle_reuses, mappings=t.runtime.mappings,
                unmaps=t.runtime.unmaps, bytes_h2d=t.runtime.bytes_h2d,
                bytes_d2h=t.runtime.bytes_d2h, cache_target=t.runtime.cache_target_bytes,
-               resident_peak=t.runtime.resident_bytes_peak)
+               resident_peak=t.runtime.resident_bytes_peak,
+               panel_slot_refills=info.panel_slot_refills)
     res["shutdown"] = api.shutdown()
     t = api.telemetry()
     res["mappings_end"], res["unmaps_end"] = t.runtime.mappings, t.runtime.unmaps
+    res["event_boundaries_end"] = t.runtime.event_boundaries
     return res
 
 

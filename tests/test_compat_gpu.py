@@ -56,10 +56,12 @@ def test_out_of_core_eviction_and_reuse():
     assert r["ok"], r
     assert r["streamed"] == 2 and r["in_place"] == 0
     assert r["tiles_submitted"] == r["tiles_retired"] > 2
-    assert r["clean_evictions"] > 0 and r["handle_reuses"] > 0
+    # the reference's counters: evictions and handle reuses are VMM unmaps and remaps
     assert r["dirty_evictions"] > 0           # the device-resident A/B written back first
+    assert r["handle_reuses"] > 0             # the second streamed GEMM remaps used frames
+    assert r["panel_slot_refills"] > 0        # panels replaced in mapped slots (own counter)
     assert r["resident_peak"] <= r["cache_target"]
-    assert r["mappings_end"] == r["unmaps_end"]
+    assert r["mappings_end"] == r["unmaps_end"] == r["event_boundaries_end"]
     assert r["shutdown"] == 0
 
 

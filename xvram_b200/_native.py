@@ -51,7 +51,7 @@ class RuntimeInfo(C.Structure):
         ("last_block_m", u64), ("last_block_n", u64), ("last_panel_k", u64),
         ("last_steps", u64), ("last_panel_slots", u64),
         ("last_gemm_ms", f64),
-        ("gemm_deferred", u64), ("gemm_column_blocks", u64),
+        ("gemm_deferred", u64), ("gemm_column_blocks", u64), ("panel_slot_refills", u64),
     ]
 
 

@@ -581,6 +581,7 @@ private:
     info_.last_gemm_ms = x.last_gemm_ms;
     info_.gemm_deferred = x.gemm_deferred;
     info_.gemm_column_blocks = x.gemm_column_blocks;
+    info_.panel_slot_refills = x.panel_slot_refills;
   }
 
   template <class F> xvram_status run(const char* op, F&& fn) {

@@ -198,7 +198,6 @@ struct Runtime::Impl {
       if (Error e = dev->event_sync(f.last_use))
         return e;
       f.pending = false;
-      ++t.event_boundaries;
     }
     if (f.uploading) {
       if (Error e = dev->event_sync(f.ready))
@@ -237,37 +236,58 @@ struct Runtime::Impl {
 
   // Takes frame `fi` away from its chunk: waits for the chunk's last device use, writes
   // it back to the host when the device copy is newer, and unmaps it.
-  Error evict_frame(size_t fi) {
-    Frame& f = frames[fi];
-    if (!f.owner || f.owner == kArenaOwner)
-      return {};
-    Alloc& a = allocs.at(f.owner);
-    Chunk& ch = a.chunks[f.chunk];
-    if (Error e = wait_idle(f))
-      return e;
-    const uint64_t off = static_cast<uint64_t>(f.chunk) * cb;
-    const uint64_t len = chunk_len(a, f.chunk);
-    if (ch.written && ch.dev_valid && !ch.backing_valid) {
-      if (Error e = ensure_backing(a))
+  Error evict_frame(size_t fi) { return evict_frames({fi}); }
+
+  // Takes the frames `fis` away from their chunks together: every dirty chunk's D2H copy is
+  // issued first, then one wait covers them all, then the frames are unmapped.  Evicting
+  // many frames (a streamed GEMM taking the whole pool, a budget shrink) thus costs one
+  // round trip instead of one per dirty chunk, and the copies queue back to back on the
+  // copy engine.  Frames that are free or hold the arena are skipped.
+  Error evict_frames(const std::vector<size_t>& fis) {
+    std::vector<size_t> owned, dirty;
+    for (size_t fi : fis) {
+      Frame& f = frames[fi];
+      if (!f.owner || f.owner == kArenaOwner)
+        continue;
+      if (Error e = wait_idle(f))
         return e;
-      if (Error e = dev->copy_2d(reinterpret_cast<uint64_t>(a.host) + off, len, a.va + off, len,
-                                 len, 1, CopyDir::d2h, s_d2h))
-        return e;
+      owned.push_back(fi);
+      Alloc& a = allocs.at(f.owner);
+      Chunk& ch = a.chunks[f.chunk];
+      if (ch.written && ch.dev_valid && !ch.backing_valid) {
+        if (Error e = ensure_backing(a))
+          return e;
+        const uint64_t off = static_cast<uint64_t>(f.chunk) * cb;
+        const uint64_t len = chunk_len(a, f.chunk);
+        if (Error e = dev->copy_2d(reinterpret_cast<uint64_t>(a.host) + off, len, a.va + off,
+                                   len, len, 1, CopyDir::d2h, s_d2h))
+          return e;
+        dirty.push_back(fi);
+        t.bytes_d2h += len;
+      }
+    }
+    if (!dirty.empty())
       if (Error e = dev->stream_sync(s_d2h))
         return e;
-      ch.backing_valid = true;
+    for (size_t fi : dirty) {
+      Frame& f = frames[fi];
+      allocs.at(f.owner).chunks[f.chunk].backing_valid = true;
       ++t.dirty_evictions;
       ++t.writebacks_completed;
-      t.bytes_d2h += len;
-    } else {
-      ++t.clean_evictions;
     }
-    if (Error e = dev->unmap(a.va + off, cb))
-      return e;
-    ++t.unmaps;
-    ch.frame = -1;
-    ch.dev_valid = false;
-    f.owner = 0;
+    t.clean_evictions += owned.size() - dirty.size();
+    for (size_t fi : owned) {
+      Frame& f = frames[fi];
+      Alloc& a = allocs.at(f.owner);
+      Chunk& ch = a.chunks[f.chunk];
+      if (Error e = dev->unmap(a.va + static_cast<uint64_t>(f.chunk) * cb, cb))
+        return e;
+      ++t.unmaps;
+      ++t.event_boundaries; // a safe unmap: after the frame's completion events (wait_idle)
+      ch.frame = -1;
+      ch.dev_valid = false;
+      f.owner = 0;
+    }
     update_resident();
     return {};
   }
@@ -379,11 +399,10 @@ struct Runtime::Impl {
   }
 
   Error evict_all() {
-    for (size_t i = 0; i < frames.size(); ++i)
-      if (frames[i].owner && frames[i].owner != kArenaOwner)
-        if (Error e = evict_frame(i))
-          return e;
-    return {};
+    std::vector<size_t> all(frames.size());
+    for (size_t i = 0; i < all.size(); ++i)
+      all[i] = i;
+    return evict_frames(all);
   }
 
   // Live budget (reference src/residency/runtime.cpp:3213-3468): between operations, the
@@ -418,23 +437,30 @@ struct Runtime::Impl {
     const uint64_t target = std::max<uint64_t>(2, std::min(after / cb, max_capacity));
     if (target < capacity) {
       growth_samples = 0;
+      if (frames.size() > target) {
+        // The frames to release, free ones first, then least recently used; their dirty
+        // chunks are written back together.
+        std::vector<size_t> order;
+        for (size_t i = 0; i < frames.size(); ++i)
+          if (frames[i].owner != kArenaOwner)
+            order.push_back(i);
+        std::stable_sort(order.begin(), order.end(), [this](size_t x, size_t y) {
+          const uint64_t kx = frames[x].owner ? frames[x].touch + 1 : 0;
+          const uint64_t ky = frames[y].owner ? frames[y].touch + 1 : 0;
+          return kx < ky;
+        });
+        order.resize(std::min<size_t>(order.size(), frames.size() - target));
+        if (Error e = evict_frames(order))
+          return e;
+      }
       while (frames.size() > target) {
         size_t victim = frames.size();
-        uint64_t oldest = UINT64_MAX;
-        for (size_t i = 0; i < frames.size(); ++i) {
-          if (frames[i].owner == kArenaOwner)
-            continue;
-          const uint64_t key = frames[i].owner ? frames[i].touch + 1 : 0; // free frames first
-          if (key < oldest) {
-            oldest = key;
+        for (size_t i = 0; i < frames.size() && victim == frames.size(); ++i)
+          if (!frames[i].owner)
             victim = i;
-          }
-        }
         if (victim == frames.size())
           return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "budget", "shrink",
                             "no frame can be released");
-        if (Error e = evict_frame(victim))
-          return e;
         if (Error e = wait_idle(frames[victim]))
           return e;
         Frame gone = frames[victim];
@@ -620,6 +646,7 @@ Error Runtime::close() {
       if (a.chunks[c].frame >= 0) {
         keep(m.dev->unmap(a.va + c * m.cb, m.cb));
         ++m.t.unmaps;
+        ++m.t.event_boundaries; // after the stream drains above
         m.frames[static_cast<size_t>(a.chunks[c].frame)].owner = 0;
         a.chunks[c].frame = -1;
       }
@@ -687,6 +714,7 @@ Error Runtime::release(uint64_t id) {
     if (Error e = m.dev->unmap(a.va + c * m.cb, m.cb))
       return e;
     ++m.t.unmaps;
+    ++m.t.event_boundaries; // after wait_idle
     f.owner = 0;
     ch.frame = -1;
   }
@@ -1255,12 +1283,11 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
     for (uint32_t li = st.load_begin; li < st.load_begin + st.load_count && !err; ++li) {
       const PanelLoad& ld = plan.loads[li];
       const size_t sl = static_cast<size_t>(ld.slot);
-      // A slot is reused only after the event of its last GEMM: an event boundary, as
-      // when the reference retires a mapping after its completion event.
+      // A slot is refilled only after the event of its last GEMM (device-side ordering;
+      // the slot's frames stay mapped).
       if (used_rec[sl]) {
         if ((err = dev->stream_wait_event(s_h2d, used[sl])))
           break;
-        ++t.event_boundaries;
       }
       const int64_t lk0 = static_cast<int64_t>(ld.kpanel) * kb;
       const int64_t lkr = std::min(kb, K - lk0);
@@ -1301,10 +1328,8 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
         break;
       t.bytes_h2d += width * height;
       ++t.cache_misses;
-      if (ld.evicts) {
-        ++t.clean_evictions;
-        ++t.handle_reuses;
-      }
+      if (ld.evicts)
+        ++x.panel_slot_refills;
     }
     if (err)
       break;

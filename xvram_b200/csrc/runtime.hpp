@@ -124,6 +124,10 @@ struct RuntimeExtra {
   // they were launched as.
   uint64_t gemm_deferred = 0;
   uint64_t gemm_column_blocks = 0;
+  // Streamed GEMMs: panel loads into a slot that held another panel.  The slot's frames
+  // stay mapped, so these are not evictions or handle reuses in the reference's sense
+  // (those count VMM unmaps and remaps) and are counted here instead.
+  uint64_t panel_slot_refills = 0;
 };
 
 class Runtime {

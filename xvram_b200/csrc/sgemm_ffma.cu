@@ -41,6 +41,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -50,6 +51,11 @@ namespace xvram {
 // Bit 0: a consumer gave up on a full barrier; bit 1: the producer gave up on an
 // empty barrier; bit 2: the producer gave up draining its own copies.
 __device__ unsigned int xvram_kernel_error = 0;
+
+// Test hook: nonzero makes every later FFMA TMA launch stall on a barrier nothing completes
+// for this many ns and then abort through the error word.  Only the test suite's link of the
+// library exports the setter (xvram_b200_test_set_kernel_stall, at the end of this file).
+std::atomic<unsigned long long> g_test_stall_ns{0};
 
 namespace {
 
@@ -103,6 +109,9 @@ struct FfmaParams {
   float* c;
   long long ldc;
   unsigned long long timeout_ns;
+  // Test hook (0 in production): every CTA first waits this long on a barrier that nothing
+  // completes, so its bounded wait runs out and the kernel takes its abort path.
+  unsigned long long stall_ns;
 };
 
 // Fragment loads for one group of 4 consecutive k (g = 0..7 inside a 32-wide stage).
@@ -379,7 +388,11 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
       acc[i][j] = make_float2(0.0f, 0.0f);
 
   bool aborted = false;
-  for (int kt = 0; kt < p.k_tiles; ++kt) {
+  if (p.stall_ns && !mbar_wait_bounded(empty + kStages, 0, p.stall_ns)) {
+    atomicOr(&xvram_kernel_error, 1u);
+    aborted = true;
+  }
+  for (int kt = 0; kt < p.k_tiles && !aborted; ++kt) {
     const int s = kt % kStages;
     const uint32_t phase = (kt / kStages) & 1;
     if (!mbar_wait_bounded(&full[s], phase, p.timeout_ns)) {
@@ -454,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kWarps);
     }
+    mbar_init(&empty[kStages], 1); // the stall hook's barrier: nothing arrives on it
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -827,6 +841,7 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
   p.c = c;
   p.ldc = ldc;
   p.timeout_ns = kernel_wait_limit_ns();
+  p.stall_ns = g_test_stall_ns.load(std::memory_order_relaxed);
   if (static_cast<long long>(p.tiles_m) * p.tiles_n > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
   return tn == 16 ? launch_tn<16>(a_kmajor, b_kmajor, ta, tb, p, stream)
@@ -863,3 +878,10 @@ unsigned long long kernel_wait_limit_ns() {
 }
 
 } // namespace xvram
+
+// Testing seam (not exported by the product libraries; tests/fake_device/testing.exports.map
+// adds it to the test suite's link): the kernel-stall hook above, in nanoseconds (0: off).
+extern "C" __attribute__((visibility("default"))) void
+xvram_b200_test_set_kernel_stall(unsigned long long ns) {
+  xvram::g_test_stall_ns.store(ns, std::memory_order_relaxed);
+}
