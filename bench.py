@@ -363,12 +363,14 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
     r0, mr = shard.rows(Mt, world, rank)
     m_max = max(shard.rows(Mt, world, q)[1] for q in range(world))
     # op N operands: A_local is mr x K (rows r0.. of the seeded M x K matrix), B is K x N.
-    a_h = torch.empty((Kt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x K
-    b_h = torch.empty((Nt, Kt), dtype=torch.float32).pin_memory()           # column-major K x N
-    c_h = torch.empty((Nt, max(mr, 1)), dtype=torch.float32).pin_memory()   # column-major mr x N
+    # Allocated page-locked directly (no pageable copy first: full C4's C is 256 GiB).
+    a_h = torch.empty((Kt, max(mr, 1)), dtype=torch.float32, pin_memory=True)  # mr x K, col-major
+    b_h = torch.empty((Nt, Kt), dtype=torch.float32, pin_memory=True)          # K x N, col-major
+    c_h = torch.empty((Nt, max(mr, 1)), dtype=torch.float32, pin_memory=True)  # mr x N, col-major
     if mr:
+        threads = 0 if mr >= (1 << 17) else 1   # all host threads only for long columns
         for kk in range(Kt):  # A_local column k holds rows r0..r0+mr of column k
-            xd.fill_uniform(a_h[kk, :mr], 40, first_index=kk * Mt + r0, threads=1)
+            xd.fill_uniform(a_h[kk, :mr], 40, first_index=kk * Mt + r0, threads=threads)
     xd.fill_uniform(b_h, 41)
     uid = shard.exchange_unique_id(rank) if world > 1 else shard.unique_id()
     group = shard.ShardGroup(uid, rank, world)
@@ -1172,8 +1174,8 @@ def main() -> None:
     ap.add_argument("--skip-ooc", action="store_true",
                     help="leave the out-of-core legs (the 'ooc' key) out of the default run")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    if args.warmup < 3 and args.workload == "c2" and args.impl == "ours":
+        args.warmup = 3   # the headline line's rule; the single-leg workloads take what is given
     if args.impl == "reference":
         run_reference_arm(args)
         return

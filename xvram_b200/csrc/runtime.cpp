@@ -5,7 +5,9 @@
 #include <algorithm>
 #include <chrono>
 #include <condition_variable>
+#include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <set>
@@ -48,6 +50,25 @@ struct Alloc {
   bool live = true;
   bool zero_fill = false; // never-written bytes read as zero (host and device)
 };
+
+// Budget sampler threads of open runtimes.  At process exit the CUDA runtime tears its
+// state down from an exit handler; a sampler of a runtime its owner never closed (a
+// session left open until exit) must not query the device after that.  The first sampler
+// registers stop_all_samplers with std::atexit -- after the CUDA runtime has registered
+// its own teardown, so it runs before it -- and it stops and joins every live sampler.
+std::mutex g_samplers_mu;
+std::set<std::function<void()>*> g_samplers; // each entry stops one sampler
+std::once_flag g_samplers_hook;
+
+void stop_all_samplers() {
+  std::vector<std::function<void()>*> live;
+  {
+    std::lock_guard<std::mutex> lk(g_samplers_mu);
+    live.assign(g_samplers.begin(), g_samplers.end());
+  }
+  for (auto* stop : live)
+    (*stop)();
+}
 
 struct Frame {
   uint64_t handle = 0;
@@ -99,7 +120,17 @@ struct Runtime::Impl {
     }
   }
   ~Impl() { stop_sampler(); }
+  // Registered in g_samplers while the sampler runs (see stop_all_samplers).
+  std::function<void()> stop_hook = [this] { stop_sampler(); };
+  std::mutex stop_mu; // serialises stop_sampler between the owner and the exit handler
+  void start_sampler() {
+    std::call_once(g_samplers_hook, [] { std::atexit(stop_all_samplers); });
+    sampler = std::thread([this] { sampler_loop(); });
+    std::lock_guard<std::mutex> lk(g_samplers_mu);
+    g_samplers.insert(&stop_hook);
+  }
   void stop_sampler() {
+    std::lock_guard<std::mutex> stop_lk(stop_mu);
     if (!sampler.joinable())
       return;
     {
@@ -108,6 +139,8 @@ struct Runtime::Impl {
     }
     sample_cv.notify_all();
     sampler.join();
+    std::lock_guard<std::mutex> lk(g_samplers_mu);
+    g_samplers.erase(&stop_hook);
   }
   uint32_t growth_samples = 0;
   std::vector<Frame> frames;
@@ -621,7 +654,7 @@ Error Runtime::open(const RuntimeConfig& cfg, std::unique_ptr<Device> device) {
   }
   m.opened = true;
   if (cfg.budget_poll_ms > 0)
-    m.sampler = std::thread([&m] { m.sampler_loop(); });
+    m.start_sampler();
   return {};
 }
 

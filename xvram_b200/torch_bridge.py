@@ -27,6 +27,7 @@ neither).  There is no CPU fallback: without a GPU every call raises.
 from __future__ import annotations
 
 import ctypes
+import atexit
 import threading
 
 import torch
@@ -215,6 +216,19 @@ class HostGemm:
 
 _host = None
 _host_lock = threading.Lock()
+
+
+def _close_host_session() -> None:
+    """Closes the host-tensor session at interpreter exit, before the CUDA runtime's own
+    teardown (its worker and budget sampler must not outlive the device)."""
+    global _host
+    with _host_lock:
+        if _host is not None:
+            _host.close()
+            _host = None
+
+
+atexit.register(_close_host_session)
 
 
 def _host_session() -> HostGemm:
