@@ -337,7 +337,13 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
                       "dirty_evictions": int(rt.dirty_evictions),
                       "handle_reuses": int(rt.handle_reuses),
                       "mappings": int(rt.mappings), "unmaps": int(rt.unmaps),
+                      "event_boundaries": int(rt.event_boundaries),
                       "maps_equal_unmaps": int(rt.mappings) == int(rt.unmaps),
+                      "panel_slot_refills": int(info.panel_slot_refills),
+                      "counters_note": "evictions and handle reuses count VMM unmaps and "
+                                       "remaps, as the reference's do; a streamed GEMM "
+                                       "refills the panel slots of its mapped frame arena "
+                                       "in place (panel_slot_refills)",
                       "tiles_retired": int(tel.tiles_retired)},
         "check": {"block": [i0, j0, s], "max_abs_err_over_k_vs_fp64": err,
                   "within_1e-6": err <= 1e-6},
@@ -371,7 +377,22 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
         threads = 0 if mr >= (1 << 17) else 1   # all host threads only for long columns
         for kk in range(Kt):  # A_local column k holds rows r0..r0+mr of column k
             xd.fill_uniform(a_h[kk, :mr], 40, first_index=kk * Mt + r0, threads=threads)
-    xd.fill_uniform(b_h, 41)
+    # B: every rank holds the whole K x N matrix but copies only its 1/P column slice of
+    # each C block to the GPU (the others arrive over NVLink).  With several ranks the rank
+    # fills just those columns, plus the columns of its sampled checks (the generator is
+    # counter-based, so every rank writes the same values into a column it fills).
+    rng = np.random.default_rng(rank)
+    samples = list(zip(rng.integers(0, max(mr, 1), 16), rng.integers(0, Nt, 16)))
+    if world == 1:
+        xd.fill_uniform(b_h, 41)
+    else:
+        nb = min(Nt, -(-env_int("XVRAM_B200_SHARD_BLOCK_N", 1024) // 32) * 32)
+        wc = -(-nb // world)
+        cols = {int(c) for _, c in samples}
+        for n0 in range(0, Nt, nb):
+            cols.update(range(n0 + rank * wc, min(n0 + (rank + 1) * wc, n0 + nb, Nt)))
+        for j in sorted(cols):
+            xd.fill_uniform(b_h[j], 41, first_index=j * Kt, threads=1)
     uid = shard.exchange_unique_id(rank) if world > 1 else shard.unique_id()
     group = shard.ShardGroup(uid, rank, world)
 
@@ -394,10 +415,9 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
     group.close()
     # sampled check: 16 outputs of this rank against FP64 (the operands' generator is
     # counter-based, so any element can be recomputed)
-    rng = np.random.default_rng(rank)
     worst = 0.0
     if mr > 0:
-        for r, c in zip(rng.integers(0, mr, 16), rng.integers(0, Nt, 16)):
+        for r, c in samples:
             ref = float(a_h[:, int(r)].double().numpy() @ b_h[int(c)].double().numpy())
             worst = max(worst, abs(float(c_h[int(c), int(r)]) - ref) / Kt)
     worst = max_over_ranks(worst)

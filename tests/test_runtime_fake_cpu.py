@@ -258,3 +258,42 @@ def test_compat_adapter_on_the_fake():
     assert r.returncode == 0, r.stderr[-2000:]
     err, reuses, tiles = r.stdout.split()
     assert float(err) <= TOLERANCE and int(reuses) > 0 and int(tiles) > 1
+
+
+@pytest.mark.parametrize("policy", ["clock", "lru"])
+def test_victim_policy_clock_spares_dirty_lru_takes_oldest(policy):
+    """Four 2 MiB frames hold A0..A3, each written while resident (dirty on the device).
+    A4 and A5 are written while the pool is full, so they stay host-side.  Prefetching A4
+    evicts one of A0..A3 and uploads A4, which is then resident and clean.  Prefetching A5
+    needs a frame again: LRU evicts the least recently used chunk, one of A0..A3, writing
+    it back first (a dirty eviction); CLOCK, the reference's default (reference
+    src/residency/policy.cpp:17-28), takes its victim from the cheapest cost class --
+    clean before dirty -- so it evicts A4 without a write-back."""
+    code = {"clock": sdk.CACHE_POLICY_CLOCK, "lru": sdk.CACHE_POLICY_LRU}[policy]
+    cfg = sdk.session_config(cache_target_bytes=8 * MiB, chunk_size_bytes=2 * MiB,
+                             device_headroom_bytes=512 * MiB, cache_policy=code)
+    with installed(), sdk.Sdk(cfg) as s:
+        blocks = []
+        for i in range(6):
+            a = s.alloc(2 * MiB)
+            a.write(np.full(MiB // 2, float(i + 1), dtype=np.float32))
+            blocks.append(a)
+
+        def prefetch(a):
+            d = s.prefetch_desc([(a, 0, 2 * MiB, sdk.READ)])
+            op = C.c_void_p()
+            s.check("prefetch", s.t.prefetch_submit(s.session, C.byref(d), C.byref(op)))
+            assert s.wait(op.value).result == sdk.SUCCESS
+            s.t.operation_release(op.value)
+
+        prefetch(blocks[4])
+        t0 = s.telemetry()
+        prefetch(blocks[5])
+        t1 = s.telemetry()
+        delta = (t1.clean_evictions - t0.clean_evictions, t1.dirty_evictions - t0.dirty_evictions)
+        assert delta == ((1, 0) if policy == "clock" else (0, 1)), delta
+        assert t1.handle_reuses == t0.handle_reuses + 1
+        for i, a in enumerate(blocks):                       # nothing lost either way
+            assert download(a, MiB // 2)[0] == i + 1
+        t2 = s.telemetry()
+        assert t2.event_boundaries == t2.unmaps

@@ -136,6 +136,7 @@ public:
     rc.cache_target_bytes = config->session.cache_target_bytes;
     rc.headroom_bytes = config->session.device_headroom_bytes;
     rc.budget_poll_ms = config->session.budget_poll_ms;
+    rc.cache_policy = config->session.cache_policy;
     Error err;
     try {
       DeviceScope scope(rc.device_ordinal);

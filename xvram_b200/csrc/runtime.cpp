@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <climits>
 #include <condition_variable>
 #include <cstdlib>
 #include <cstring>
@@ -81,6 +82,7 @@ struct Frame {
   bool pending = false;   // last_use has been recorded
   bool uploading = false; // ready has been recorded and not yet observed complete
   bool prefetched = false; // made resident by a prefetch and not yet used by an operation
+  bool referenced = false; // CLOCK's reference bit: used since the hand last passed
 };
 
 } // namespace
@@ -143,6 +145,7 @@ struct Runtime::Impl {
     g_samplers.erase(&stop_hook);
   }
   uint32_t growth_samples = 0;
+  size_t clock_hand = 0; // CLOCK: where the next victim search starts
   std::vector<Frame> frames;
   std::map<uint64_t, Alloc> allocs;
   uint64_t next_id = 1;
@@ -344,9 +347,60 @@ struct Runtime::Impl {
       *out = frames.size() - 1;
       return {};
     }
-    // Least recently used first, but a frame that a prefetch filled for an operation that
-    // has not run yet goes only when nothing else can: evicting it would make that
-    // operation upload it again.
+    size_t victim = cfg.cache_policy == XVRAM_CACHE_POLICY_LRU ? lru_victim(keep)
+                                                                 : clock_victim(keep);
+    if (victim == frames.size())
+      return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "residency", "acquire_frame",
+                        "every frame is pinned by the current operation");
+    if (Error e = evict_frame(victim))
+      return e;
+    ++t.handle_reuses;
+    *out = victim;
+    return {};
+  }
+
+  bool evictable(const Frame& f, const std::set<std::pair<uint64_t, uint32_t>>& keep) const {
+    return f.owner && f.owner != kArenaOwner && !keep.count({f.owner, f.chunk});
+  }
+
+  // CLOCK, as the reference's default policy (reference src/residency/policy.cpp:17-28,
+  // 88-): frames fall into cost classes -- clean before dirty, a frame a prefetch filled
+  // and nothing used yet before one in use -- and within the cheapest class the hand
+  // sweeps from where it stopped, clearing reference bits, and takes the first frame whose
+  // bit is already clear (second chance).  frames.size() if none is evictable.
+  size_t clock_victim(const std::set<std::pair<uint64_t, uint32_t>>& keep) {
+    const size_t n = frames.size();
+    auto cost = [this](const Frame& f) {
+      const Chunk& ch = allocs.at(f.owner).chunks[f.chunk];
+      const bool dirty = ch.written && ch.dev_valid && !ch.backing_valid;
+      return (dirty ? 3u : 0u) + (f.prefetched ? 1u : 2u);
+    };
+    unsigned cheapest = UINT_MAX;
+    for (const Frame& f : frames)
+      if (evictable(f, keep))
+        cheapest = std::min(cheapest, cost(f));
+    if (cheapest == UINT_MAX)
+      return n;
+    for (int pass = 0; pass < 2; ++pass)
+      for (size_t scanned = 0; scanned < n; ++scanned) {
+        const size_t i = (clock_hand + scanned) % n;
+        Frame& f = frames[i];
+        if (!evictable(f, keep) || cost(f) != cheapest)
+          continue;
+        if (f.referenced) {
+          f.referenced = false;
+          continue;
+        }
+        clock_hand = (i + 1) % n;
+        return i;
+      }
+    return n;
+  }
+
+  // LRU: least recently used first, but a frame that a prefetch filled for an operation
+  // that has not run yet goes only when nothing else can: evicting it would make that
+  // operation upload it again.
+  size_t lru_victim(const std::set<std::pair<uint64_t, uint32_t>>& keep) const {
     size_t victim = frames.size();
     for (int pass = 0; pass < 2 && victim == frames.size(); ++pass) {
       uint64_t oldest = UINT64_MAX;
@@ -361,14 +415,7 @@ struct Runtime::Impl {
         }
       }
     }
-    if (victim == frames.size())
-      return make_error(XVRAM_STATUS_BUDGET_PRESSURE, "residency", "acquire_frame",
-                        "every frame is pinned by the current operation");
-    if (Error e = evict_frame(victim))
-      return e;
-    ++t.handle_reuses;
-    *out = victim;
-    return {};
+    return victim;
   }
 
   // Maps chunk c of `a` if needed; uploads its host data when `upload` and the host copy
@@ -379,6 +426,7 @@ struct Runtime::Impl {
     if (ch.frame >= 0) {
       ++t.cache_hits;
       frames[static_cast<size_t>(ch.frame)].touch = ++clock;
+      frames[static_cast<size_t>(ch.frame)].referenced = true;
       return {};
     }
     ++t.cache_misses;
@@ -396,6 +444,7 @@ struct Runtime::Impl {
     f.chunk = c;
     f.used = true;
     f.touch = ++clock;
+    f.referenced = true;
     ch.frame = static_cast<int32_t>(fi);
     ch.dev_valid = !ch.written; // undefined contents are valid anywhere
     if (upload && ch.written && ch.backing_valid && a.host) {

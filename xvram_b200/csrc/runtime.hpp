@@ -47,6 +47,9 @@ struct RuntimeConfig {
   // device's free memory and shrinks (or, after repeated samples with room, regrows up to
   // the budget it opened with) its frame pool to free + own frames - headroom.
   uint64_t budget_poll_ms = 100;
+  // Victim choice for resident chunks: 0 = CLOCK (the reference's default), 1 = LRU.
+  // Streamed GEMMs evict panels by exact next use either way (the plan knows it).
+  uint32_t cache_policy = 0;
   // Planning rates (estimates only; they steer geometry choice, never correctness).
   double flops_per_s = 70e12;
   double h2d_bytes_per_s = 50e9;

@@ -223,6 +223,7 @@ public:
       rc.cache_target_bytes = cfg_.cache_target_bytes;
       rc.headroom_bytes = cfg_.device_headroom_bytes;
       rc.budget_poll_ms = cfg_.budget_poll_ms;
+      rc.cache_policy = cfg_.cache_policy;
       DeviceFactory factory = device_factory();
       std::unique_ptr<Device> dev = factory ? factory() : nullptr;
       if (!dev)

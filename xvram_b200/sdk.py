@@ -15,7 +15,7 @@ u32, u64, i32, i64, f64 = C.c_uint32, C.c_uint64, C.c_int32, C.c_int64, C.c_doub
 vp = C.c_void_p
 TIMEOUT_INFINITE = (1 << 64) - 1
 
-# status codes (include/xvram.h)
+# status codes (include/xvram/xvram.h)
 (SUCCESS, INVALID_ARGUMENT, INCOMPATIBLE_ABI, UNSUPPORTED, UNAVAILABLE, HOST_OUT_OF_MEMORY,
  DEVICE_OUT_OF_MEMORY, BUDGET_PRESSURE, BUSY, NOT_READY, TIMEOUT, CORRUPTION, CALLBACK_FAILED,
  CUDA_ERROR, CUBLAS_ERROR, POISONED, CLEANUP_FAILED, CLOSED, CANCELLED, INTERNAL) = range(20)
@@ -25,6 +25,7 @@ FP16, BF16, FP32, FP64 = range(4)
 COMPUTE_AUTO, COMPUTE_FP32_STRICT, COMPUTE_FP32_TF32, COMPUTE_FP64 = range(4)
 ROW_MAJOR, COLUMN_MAJOR = 0, 1
 OP_N, OP_T = 0, 1
+CACHE_POLICY_CLOCK, CACHE_POLICY_LRU = 0, 1
 ZERO_INITIALIZE = 1
 
 
