@@ -594,9 +594,12 @@ def run_mlp(args) -> None:
     bias_all = ((torch.rand((LAYERS, F), generator=g, device=dev) * 2 - 1) / np.sqrt(F))
     x = (torch.rand((BATCH, F), generator=g, device=dev) * 2 - 1)
 
-    # the sharded layers' exchange uses an F x B staging workspace in each transaction
+    # the sharded layers' exchange uses an F x B staging workspace in each transaction.
+    # LRU: while layer i computes, the prefetch of layer i+1's weight takes the frames of
+    # layer i-1 (least recently used), never those of the weight still in use.
     s = sdk.Sdk(sdk.session_config(device_ordinal=local, cache_target_bytes=budget,
-                                   workspace_cap_bytes=max(4 << 20, abytes)))
+                                   workspace_cap_bytes=max(4 << 20, abytes),
+                                   cache_policy=sdk.CACHE_POLICY_LRU))
     group = None
     if world > 1:
         group = shard.ShardGroup(shard.exchange_unique_id(rank), rank, world)
