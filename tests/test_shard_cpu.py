@@ -182,3 +182,29 @@ def test_unique_id_without_gpu():
     except RuntimeError:
         return  # no NCCL library on this host: nothing else to check
     assert len(uid) == shard.ID_BYTES
+
+
+def test_row_partition_rejects_bad_arguments():
+    import ctypes as C
+    from xvram_b200._native import lib
+    b0, n = C.c_int64(0), C.c_int64(0)
+    for m, world, rank in ((-1, 2, 0), (10, 0, 0), (10, 2, 2), (10, 2, -1)):
+        assert lib.xvram_b200_shard_rows(m, world, rank, C.byref(b0), C.byref(n)) == 1
+    assert lib.xvram_b200_shard_rows(10, 2, 0, None, C.byref(n)) == 1
+
+
+def test_custom_group_rejects_incomplete_collectives():
+    import ctypes as C
+    from xvram_b200._native import ShardCollectives, lib
+    ops = ShardCollectives()
+    ops.struct_size = C.sizeof(ShardCollectives)
+    out = C.c_uint64(0)
+    # no functions
+    assert lib.xvram_b200_shard_group_create_custom(C.byref(ops), 0, 1, C.byref(out)) == 1
+    ops.all_reduce_max_u64 = ShardCollectives.ALL_REDUCE(lambda *a: 0)
+    ops.all_gather_f32 = ShardCollectives.ALL_GATHER(lambda *a: 0)
+    ops.struct_size = 8   # older/smaller than v1
+    assert lib.xvram_b200_shard_group_create_custom(C.byref(ops), 0, 1, C.byref(out)) == 1
+    ops.struct_size = C.sizeof(ShardCollectives)
+    assert lib.xvram_b200_shard_group_create_custom(C.byref(ops), 1, 1, C.byref(out)) == 1
+    assert lib.xvram_b200_shard_group_create_custom(None, 0, 1, C.byref(out)) == 1
