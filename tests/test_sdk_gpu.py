@@ -346,3 +346,26 @@ def test_sdk_calls_from_a_callback_answer_busy(s):
     assert seen == {"read": sdk.BUSY, "drain": sdk.BUSY, "close": sdk.BUSY}
     Y.write(np.ones(1024, dtype=np.float32))  # still open and working
     assert np.all(download(Y, 1024) == 1.0)
+
+
+def test_process_exits_cleanly_with_a_session_left_open():
+    """A session that its owner never closes keeps a budget-sampler thread that queries
+    the device every budget_poll_ms.  At process exit the library stops such samplers
+    before the CUDA runtime tears its state down, so the process ends with status 0 (a
+    sampler still querying a torn-down runtime could crash the exit)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path.insert(0, {str(root)!r})\n"
+        "from xvram_b200 import sdk\n"
+        "s = sdk.Sdk(sdk.session_config(budget_poll_ms=1))\n"
+        "a = s.alloc(1 << 20)\n"
+        "a.write(np.ones(1 << 18, dtype=np.float32))\n"
+        "print('left open')\n")
+    for _ in range(3):
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                           timeout=120)
+        assert r.returncode == 0 and "left open" in r.stdout, (r.returncode, r.stderr[-2000:])
