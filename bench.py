@@ -241,7 +241,7 @@ def _rows_of(seed: int, n: int, first: int, count: int) -> "np.ndarray":
 
 
 def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2d_gbs: float,
-                   d2h_gbs: float, device_ordinal: int = 0) -> dict:
+                   d2h_gbs: float, device_ordinal: int = 0, tf32_steps: int = 0) -> dict:
     """One or more streamed GEMMs through the compat ABI with operands far above the device
     budget (BASELINE config 3's form: NT, alpha 1, beta 1, n^3, cache_target_bytes =
     budget): the operands are written through memcpy(H2D) into the adapter's host backing
@@ -249,7 +249,10 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     clock up to its completion (XVRAM_B200_SYNC_GEMM is not needed: a streamed GEMM
     completes before the call returns).  No warm-up: the first call pays the plan and the
     frame pool, as a caller's would.  Parity: a 64 x 64 block of C is read back and checked
-    against an FP64 recomputation of the same block from the seeded generators."""
+    against an FP64 recomputation of the same block from the seeded generators.
+    With tf32_steps, that many more calls follow with the handle in math mode 3 (the
+    three-term TF32 tensor-core path, FP32-accurate within the same tolerance), reported
+    under "tf32x3" against max(TF32 work / the tensor peak, host bytes / the link)."""
     import numpy as np
 
     from xvram_b200 import compat as cp
@@ -288,6 +291,22 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
             times.append(time.perf_counter() - start)
             t1 = api.telemetry().runtime
             moved.append((t1.bytes_h2d - b0[0], t1.bytes_d2h - b0[1]))
+    strict_info = cp.runtime_info()
+    tf32_times, tf32_moved = [], []
+    if tf32_steps:
+        api.check("math", api.t.blas_set_math_mode(h, 3))
+        for _ in range(tf32_steps):
+            t0 = api.telemetry().runtime
+            b0 = (t0.bytes_h2d, t0.bytes_d2h)
+            start = time.perf_counter()
+            api.check("sgemm", api.sgemm(h, 0, 1, n, n, n, 1.0, ptrs[0], n, ptrs[1], n, 1.0,
+                                         ptrs[2], n))
+            api.check("synchronize", api.t.synchronize())
+            tf32_times.append(time.perf_counter() - start)
+            t1 = api.telemetry().runtime
+            tf32_moved.append((t1.bytes_h2d - b0[0], t1.bytes_d2h - b0[1]))
+        api.check("math", api.t.blas_set_math_mode(h, 0))
+    tf32_info = cp.runtime_info()
     # parity on a 64 x 64 block (C = C0 + calls * A B^T in exact arithmetic)
     s, i0, j0 = 64, (n // 3) // 64 * 64, (2 * n // 3) // 64 * 64
     got = np.empty((s, s), np.float32)                       # [j, i]
@@ -298,10 +317,11 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     c0 = np.empty((s, s), np.float32)
     for jj in range(s):
         xd.fill_uniform(c0[jj], seeds[2], first_index=i0 + (j0 + jj) * n, threads=1)
-    want = c0.astype(np.float64).T + len(times) * (a_rows @ b_rows.T)   # [i, j]
-    err = float(np.max(np.abs(got.T.astype(np.float64) - want))) / (len(times) * n)
+    calls = len(times) + len(tf32_times)
+    want = c0.astype(np.float64).T + calls * (a_rows @ b_rows.T)   # [i, j]
+    err = float(np.max(np.abs(got.T.astype(np.float64) - want))) / (calls * n)
     tel = api.telemetry()
-    info = cp.runtime_info()
+    info = strict_info
     for d in ptrs:
         api.free(d)
     api.blas_destroy(h)
@@ -313,7 +333,7 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     t_fp32 = flop / (peak_tflops * 1e12)
     t_roof = max(t_fp32, alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
     rt = tel.runtime
-    return {
+    out = {
         "workload": f"C3 form, out of core through the compat ABI: {n}^3 NT alpha 1 beta 1, "
                     f"{n * n * 4 >> 30} GiB per operand, device budget {budget_gib:g} GiB, 1 GPU",
         "value": flop / sec / 1e12, "unit": "TFLOP/s", "steps": len(times), "warmup": 0,
@@ -350,6 +370,30 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
         "setup_s": {"fill_and_memcpy_h2d": round(t_fill, 1)},
         "clocks": clocks.summary(),
     }
+    if tf32_times:
+        tsec = min(tf32_times)
+        th2d, td2h = tf32_moved[tf32_times.index(tsec)]
+        p_tf32 = measured_tf32_peak()
+        t_tensor = 3 * flop / (p_tf32 * 1e12)
+        t_link = max(alg_h2d / (h2d_gbs * 1e9), alg_d2h / (d2h_gbs * 1e9))
+        out["tf32x3"] = {
+            "what": "the same call with blas_set_math_mode(3): three-term TF32 on "
+                    "tcgen05/TMEM, within max|err|/(K max|a| max|b|) <= 1e-6 (the check "
+                    "above covers both calls)",
+            "value": flop / tsec / 1e12, "unit": "TFLOP/s", "ms_per_step": 1e3 * tsec,
+            "roofline": {"t_roof_ms": 1e3 * max(t_tensor, t_link),
+                         "frac": max(t_tensor, t_link) / tsec,
+                         "bound": "tensor" if t_tensor >= t_link else "host-link",
+                         "p_tf32_tflops": p_tf32, "tf32_flop": 3 * flop},
+            "host_link": {"h2d_bytes": th2d, "d2h_bytes": td2h,
+                          "h2d_over_algorithmic": th2d / alg_h2d,
+                          "achieved_h2d_gbs": th2d / tsec / 1e9},
+            "plan": {"block_m": int(tf32_info.last_block_m),
+                     "block_n": int(tf32_info.last_block_n),
+                     "panel_k": int(tf32_info.last_panel_k),
+                     "steps": int(tf32_info.last_steps)},
+        }
+    return out
 
 
 def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: int, rank: int,
@@ -454,7 +498,8 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
 def child_c3s(args, local: int) -> dict:
     """`bench.py --workload c3s --steps 1` in a child process; its JSON line as a dict."""
     cmd = [sys.executable, str(ROOT / "bench.py"), "--workload", "c3s", "--steps", "1",
-           "--ooc-n", str(args.ooc_n), "--ooc-budget-gib", str(args.ooc_budget_gib)]
+           "--ooc-n", str(args.ooc_n), "--ooc-budget-gib", str(args.ooc_budget_gib),
+           "--ooc-tf32-steps", "1"]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", str(local)))
     for key in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
         env.pop(key, None)
@@ -478,7 +523,7 @@ def run_out_of_core(args) -> None:
     peak_tflops, probes = measure_fp32_peak(dev, stream)
     h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
     leg = ooc_compat_leg(args.ooc_n, args.ooc_budget_gib, args.steps, peak_tflops, h2d_gbs,
-                         d2h_gbs)
+                         d2h_gbs, tf32_steps=args.ooc_tf32_steps)
     leg["roofline"]["fp32_probes"] = probes
     print(json.dumps({"metric": METRIC, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
                       **leg}), flush=True)
@@ -1194,6 +1239,8 @@ def main() -> None:
     ap.add_argument("--mlp-budget-gib", type=float, default=8.0)
     ap.add_argument("--ooc-n", type=int, default=65536)
     ap.add_argument("--ooc-budget-gib", type=float, default=10.0)
+    ap.add_argument("--ooc-tf32-steps", type=int, default=0,
+                    help="c3s: calls in math mode 3 (three-term TF32) after the strict ones")
     ap.add_argument("--skip-ooc", action="store_true",
                     help="leave the out-of-core legs (the 'ooc' key) out of the default run")
     args = ap.parse_args()
