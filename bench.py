@@ -430,7 +430,8 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
     if world == 1:
         xd.fill_uniform(b_h, 41)
     else:
-        nb = min(Nt, -(-env_int("XVRAM_B200_SHARD_BLOCK_N", 1024) // 32) * 32)
+        # the library's block width (xvram_b200_sgemm_sharded's default is 512 columns)
+        nb = min(Nt, -(-env_int("XVRAM_B200_SHARD_BLOCK_N", 512) // 32) * 32)
         wc = -(-nb // world)
         cols = {int(c) for _, c in samples}
         for n0 in range(0, Nt, nb):

@@ -92,7 +92,10 @@ const NcclApi& nccl() {
 constexpr double kInitTimeoutS = 120.0;
 constexpr double kWaitTimeoutS = 60.0;
 constexpr uint64_t kHeadroomBytes = 1ull << 30; // left free on the device for everything else
-constexpr uint64_t kDefaultBlockN = 1024;       // C block width (columns)
+// C block width (columns).  Measured on C2 TN at one GPU (median of 8 calls): 512 -> 10.76
+// ms, 1024 -> 11.18 ms, 2048 -> 12.21 ms: narrower blocks start the first kernel and end
+// the last write-back sooner.
+constexpr uint64_t kDefaultBlockN = 512;
 constexpr uint64_t kTileM = 128;                // row granularity of partitions and row groups
 // B and C block buffers in flight: block j+2's copies may start while block j's
 // write-back is still running.
