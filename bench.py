@@ -831,6 +831,32 @@ def measure_link(dev, stream, barrier) -> tuple[float, float]:
 
 
 # ------------------------------------------------------------------------------ GPU arm
+def pipelined_steps(n, stream, side, bufs, gathered, consumed, gather, kernel) -> None:
+    """n steps of (gather B into a buffer, kernel on it) with two B buffers: step i+1's
+    gather runs on `side` while step i's kernel runs on `stream`.  The side stream waits
+    for everything already on `stream` first (so a start event recorded there covers the
+    first gather), and a buffer is refilled only after the kernel that read it.  The
+    last kernel is the last work on `stream`."""
+    import torch
+    side.wait_stream(stream)
+
+    def issue(i):
+        buf = i % 2
+        side.wait_event(consumed[buf])
+        with torch.cuda.stream(side):
+            gather(bufs[buf])
+            gathered[buf].record(side)
+
+    issue(0)
+    for i in range(n):
+        if i + 1 < n:
+            issue(i + 1)
+        stream.wait_event(gathered[i % 2])
+        with torch.cuda.stream(stream):
+            assert kernel(bufs[i % 2]) == 0
+        consumed[i % 2].record(stream)
+
+
 def main_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -885,33 +911,44 @@ def main_gpu(args) -> None:
 
     # ---------------- kernel-only: inputs resident in HBM.  At N > 1 the job is one
     # problem split by C rows: each rank holds its A rows, its C rows and a 1/N column
-    # slice of the shared B, and every step first all-gathers B over NVLink (NCCL, on the
-    # timed stream) and then runs the kernel on the gathered B.
+    # slice of the shared B.  Every step all-gathers B over NVLink (NCCL) and runs the
+    # kernel on the gathered B; B is double-buffered, so step i+1's gather (on a side
+    # stream) overlaps step i's kernel, as a pipeline of successive GEMMs would run.
     B_slice = B[rank * (N // world):(rank + 1) * (N // world)].clone() if world > 1 else None
     B_run = torch.empty_like(B) if world > 1 else B
     if world > 1:
         assert N % world == 0
 
-    def launch():
-        if world > 1:
-            dist.all_gather_into_tensor(B_run, B_slice)
-        st = xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B_run, K, BETA, Cd, M, stream=stream)
-        assert st == 0, st
+    def gather_b(dst):
+        dist.all_gather_into_tensor(dst, B_slice)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            launch()
-    stream.synchronize()
+    def launch_steps(n: int) -> None:
+        """n steps on `stream` (and, at N > 1, its side stream); enqueue only."""
+        if world == 1:
+            with torch.cuda.stream(stream):
+                for _ in range(n):
+                    assert xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B, K, BETA, Cd, M,
+                                    stream=stream) == 0
+            return
+        pipelined_steps(n, stream, side, B_bufs, gathered, consumed, gather_b,
+                        lambda bb: xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, bb, K, BETA, Cd,
+                                            M, stream=stream))
+
+    side = torch.cuda.Stream(device=dev) if world > 1 else None
+    B_bufs = [B_run, torch.empty_like(B)] if world > 1 else None
+    gathered = [torch.cuda.Event(), torch.cuda.Event()]
+    consumed = [torch.cuda.Event(), torch.cuda.Event()]
+
+    launch_steps(args.warmup)
+    torch.cuda.synchronize()
     assert xd.kernel_status(stream) == 0
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(args.steps):
-                launch()
-            stop.record(stream)
+        start.record(stream)
+        launch_steps(args.steps)   # at N > 1 the first gather waits for `start` (below)
+        stop.record(stream)
         stop.synchronize()
     torch.cuda.synchronize()
     barrier()
@@ -937,7 +974,7 @@ def main_gpu(args) -> None:
     else:
         kernel_ms = step_ms
     achieved = FLOP / (kernel_ms * 1e-3) / 1e12
-    del B_slice
+    del B_slice, B_bufs
 
     # ---------------- kernel-only, tensor-core path (three-term TF32 on tcgen05/TMEM)
     tc_need = lib.xvram_b200_sgemm_workspace_bytes(OP_A | 0x100, OP_B, M, N, K)

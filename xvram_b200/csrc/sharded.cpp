@@ -90,7 +90,8 @@ const NcclApi& nccl() {
 }
 
 constexpr double kInitTimeoutS = 120.0;
-constexpr double kWaitTimeoutS = 60.0;
+constexpr double kWaitTimeoutS = 60.0;   // per host wait (per stretch of blocks at the end)
+constexpr uint64_t kProgressMarks = 256;   // progress events per call at most
 constexpr uint64_t kHeadroomBytes = 1ull << 30; // left free on the device for everything else
 // C block width (columns).  Measured on C2 TN at one GPU (median of 8 calls): 512 -> 10.76
 // ms, 1024 -> 11.18 ms, 2048 -> 12.21 ms: narrower blocks start the first kernel and end
@@ -206,6 +207,10 @@ struct ShardGroup {
   // compute stream, end of the call, plan exchange done.
   EventId a_free[2] = {}, a_all = 0, group_end[2] = {}, out = 0, plan_ev = 0;
   std::vector<EventId> a_ev; // one per A panel: panel p resident (and canonical)
+  // Progress marks: recorded on the compute stream after every `stride`-th block's kernel,
+  // so the end-of-call wait allows kWaitTimeoutS per stretch of blocks, not for the whole
+  // call (a full-size call runs for minutes).
+  std::vector<EventId> progress_ev;
   Buffer a_canon, a_raw[2], b_raw[kSlots], b_canon[kSlots], c_blk[kSlots], plan_dev;
   uint64_t* plan_host = nullptr; // 2 x u64, page-locked
   bool aborted = false;
@@ -552,6 +557,13 @@ xvram_status run_sharded(ShardGroup& g, uint32_t op_a, uint32_t op_b, uint64_t M
         return status_of(e);
       g.a_ev.push_back(ev);
     }
+    const uint64_t marks = std::min<uint64_t>(kProgressMarks, pl.groups * ((N + pl.nb - 1) / pl.nb));
+    while (g.progress_ev.size() < marks) {
+      EventId ev = 0;
+      if (xvram::Error e = d.event_create(&ev))
+        return status_of(e);
+      g.progress_ev.push_back(ev);
+    }
   }
 
   // ---- 3. enqueue
@@ -563,6 +575,10 @@ xvram_status run_sharded(ShardGroup& g, uint32_t op_a, uint32_t op_b, uint64_t M
   const int64_t ldm = static_cast<int64_t>(pl.ldm), ldn = static_cast<int64_t>(pl.ldn);
   const xvram::GemmTypes fp32{};
   uint64_t q = 0; // global block counter: slot q % kSlots, compute stream q & 1
+  const uint64_t total_blocks = pl.groups * blocks;
+  const uint64_t marks = std::min<uint64_t>(kProgressMarks, total_blocks);
+  const uint64_t stride = (total_blocks + marks - 1) / marks; // blocks per progress mark
+  uint64_t marked = 0;
   xvram::Error e;
   auto h2d = [&](uint64_t dst, uint64_t dp, uint64_t src, uint64_t sp, uint64_t w, uint64_t h) {
     info.h2d_bytes += w * h;
@@ -677,6 +693,8 @@ xvram_status run_sharded(ShardGroup& g, uint32_t op_a, uint32_t op_b, uint64_t M
       }
       if (!e)
         e = d.event_record(g.b_free[s], cs);
+      if (!e && (q + 1) % stride == 0 && marked < marks)
+        e = d.event_record(g.progress_ev[marked++], cs);
 
       // (d) C's block j back to the host
       if (!e && mr > 0) {
@@ -705,7 +723,13 @@ xvram_status run_sharded(ShardGroup& g, uint32_t op_a, uint32_t op_b, uint64_t M
     g.aborted = true;
     return status_of(e);
   }
-  xvram_status st = bounded_wait(g, g.out);
+  // Every stretch of blocks must finish within kWaitTimeoutS of the one before; then the
+  // last write-back.
+  xvram_status st = XVRAM_STATUS_SUCCESS;
+  for (uint64_t i = 0; i < marked && st == XVRAM_STATUS_SUCCESS; ++i)
+    st = bounded_wait(g, g.progress_ev[i]);
+  if (st == XVRAM_STATUS_SUCCESS)
+    st = bounded_wait(g, g.out);
   if (st == XVRAM_STATUS_SUCCESS) {
     uint32_t word = 0;
     if (d.kernel_status(g.d2h, &word))
