@@ -241,14 +241,15 @@ def _rows_of(seed: int, n: int, first: int, count: int) -> "np.ndarray":
 
 
 def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2d_gbs: float,
-                   d2h_gbs: float, device_ordinal: int = 0, tf32_steps: int = 0) -> dict:
+                   d2h_gbs: float, device_ordinal: int = 0, tf32_steps: int = 0,
+                   warmup: int = 0) -> dict:
     """One or more streamed GEMMs through the compat ABI with operands far above the device
     budget (BASELINE config 3's form: NT, alpha 1, beta 1, n^3, cache_target_bytes =
     budget): the operands are written through memcpy(H2D) into the adapter's host backing
     (256 MiB at a time, no full host copies), then each blas_sgemm call is timed on the host
     clock up to its completion (XVRAM_B200_SYNC_GEMM is not needed: a streamed GEMM
-    completes before the call returns).  No warm-up: the first call pays the plan and the
-    frame pool, as a caller's would.  Parity: a 64 x 64 block of C is read back and checked
+    completes before the call returns).  `warmup` untimed calls come first (the first call
+    of a process also creates the frame pool; later calls remap its frames).  Parity: a 64 x 64 block of C is read back and checked
     against an FP64 recomputation of the same block from the seeded generators.
     With tf32_steps, that many more calls follow with the handle in math mode 3 (the
     three-term TF32 tensor-core path, FP32-accurate within the same tolerance), reported
@@ -279,6 +280,10 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     del stage
     h = api.blas_create()
     flop = 2.0 * n ** 3
+    for _ in range(warmup):
+        api.check("sgemm", api.sgemm(h, 0, 1, n, n, n, 1.0, ptrs[0], n, ptrs[1], n, 1.0,
+                                     ptrs[2], n))
+        api.check("synchronize", api.t.synchronize())
     times, moved = [], []
     with ClockSampler(device_ordinal, 200) as clocks:
         for _ in range(max(steps, 1)):
@@ -317,7 +322,7 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     c0 = np.empty((s, s), np.float32)
     for jj in range(s):
         xd.fill_uniform(c0[jj], seeds[2], first_index=i0 + (j0 + jj) * n, threads=1)
-    calls = len(times) + len(tf32_times)
+    calls = warmup + len(times) + len(tf32_times)
     want = c0.astype(np.float64).T + calls * (a_rows @ b_rows.T)   # [i, j]
     err = float(np.max(np.abs(got.T.astype(np.float64) - want))) / (calls * n)
     tel = api.telemetry()
@@ -336,7 +341,7 @@ def ooc_compat_leg(n: int, budget_gib: float, steps: int, peak_tflops: float, h2
     out = {
         "workload": f"C3 form, out of core through the compat ABI: {n}^3 NT alpha 1 beta 1, "
                     f"{n * n * 4 >> 30} GiB per operand, device budget {budget_gib:g} GiB, 1 GPU",
-        "value": flop / sec / 1e12, "unit": "TFLOP/s", "steps": len(times), "warmup": 0,
+        "value": flop / sec / 1e12, "unit": "TFLOP/s", "steps": len(times), "warmup": warmup,
         "ms_per_step": 1e3 * sec, "step_ms": [round(1e3 * t, 1) for t in times],
         "operand_bytes_over_budget": 3 * n * n * 4 / budget,
         "roofline": {"t_roof_ms": 1e3 * t_roof, "frac": t_roof / sec,
@@ -499,8 +504,8 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
 def child_c3s(args, local: int) -> dict:
     """`bench.py --workload c3s --steps 1` in a child process; its JSON line as a dict."""
     cmd = [sys.executable, str(ROOT / "bench.py"), "--workload", "c3s", "--steps", "1",
-           "--ooc-n", str(args.ooc_n), "--ooc-budget-gib", str(args.ooc_budget_gib),
-           "--ooc-tf32-steps", "1"]
+           "--warmup", "1", "--ooc-n", str(args.ooc_n), "--ooc-budget-gib",
+           str(args.ooc_budget_gib), "--ooc-tf32-steps", "1"]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", str(local)))
     for key in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
         env.pop(key, None)
@@ -524,7 +529,7 @@ def run_out_of_core(args) -> None:
     peak_tflops, probes = measure_fp32_peak(dev, stream)
     h2d_gbs, d2h_gbs = measure_link(dev, stream, lambda: None)
     leg = ooc_compat_leg(args.ooc_n, args.ooc_budget_gib, args.steps, peak_tflops, h2d_gbs,
-                         d2h_gbs, tf32_steps=args.ooc_tf32_steps)
+                         d2h_gbs, tf32_steps=args.ooc_tf32_steps, warmup=args.warmup)
     leg["roofline"]["fp32_probes"] = probes
     print(json.dumps({"metric": METRIC, "n_gpus": 1, "dtype": "f32", "data": "synthetic",
                       **leg}), flush=True)
