@@ -939,7 +939,8 @@ def main_gpu(args) -> None:
                         lambda bb: xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, bb, K, BETA, Cd,
                                             M, stream=stream))
 
-    side = torch.cuda.Stream(device=dev) if world > 1 else None
+    # high priority, so the gather's few CTAs are scheduled as soon as kernel CTAs retire
+    side = torch.cuda.Stream(device=dev, priority=-1) if world > 1 else None
     B_bufs = [B_run, torch.empty_like(B)] if world > 1 else None
     gathered = [torch.cuda.Event(), torch.cuda.Event()]
     consumed = [torch.cuda.Event(), torch.cuda.Event()]
