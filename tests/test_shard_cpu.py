@@ -208,3 +208,24 @@ def test_custom_group_rejects_incomplete_collectives():
     ops.struct_size = C.sizeof(ShardCollectives)
     assert lib.xvram_b200_shard_group_create_custom(C.byref(ops), 1, 1, C.byref(out)) == 1
     assert lib.xvram_b200_shard_group_create_custom(None, 0, 1, C.byref(out)) == 1
+
+
+def test_failing_collective_fails_the_call_and_poisons_the_group():
+    """A collective that raises (or returns an error) fails the sharded call and leaves the
+    group POISONED; nothing hangs (one rank, fake device)."""
+    import numpy as np
+    from fake_device import installed
+    from xvram_b200 import shard
+
+    def bad_reduce(ptr, count, stream):
+        raise RuntimeError("peer lost")
+
+    with installed():
+        g = shard.ShardGroup.custom(0, 2, bad_reduce, lambda *a: 0)
+        a = np.ones((64, 128), np.float32)
+        b = np.ones((64, 128), np.float32)
+        c = np.zeros((64, 128), np.float32)
+        st = g.sgemm(0, 0, 128, 64, 64, 1.0, a, 128, b, 64, 0.0, c, 128)
+        assert st == 13                                   # CUDA_ERROR from the collective
+        assert g.sgemm(0, 0, 128, 64, 64, 1.0, a, 128, b, 64, 0.0, c, 128) == 15  # POISONED
+        g.close()

@@ -73,12 +73,20 @@ class ShardGroup:
         """A group over the caller's collectives.  all_reduce_max_u64(ptr, count, stream)
         and all_gather_f32(send_ptr, recv_ptr, count, stream) receive device addresses
         (host addresses on a host test device) as ints and return 0 on success."""
+        # A Python exception cannot cross the C boundary: it becomes a failed collective
+        # (XVRAM_STATUS_CUDA_ERROR), which fails the call and poisons the group.
         def _reduce(_ctx, buf, count, stream):
-            return int(all_reduce_max_u64(C.cast(buf, C.c_void_p).value, count, stream) or 0)
+            try:
+                return int(all_reduce_max_u64(C.cast(buf, C.c_void_p).value, count, stream) or 0)
+            except Exception:  # noqa: BLE001
+                return 13
 
         def _gather(_ctx, send, recv, count, stream):
-            return int(all_gather_f32(C.cast(send, C.c_void_p).value,
-                                      C.cast(recv, C.c_void_p).value, count, stream) or 0)
+            try:
+                return int(all_gather_f32(C.cast(send, C.c_void_p).value,
+                                          C.cast(recv, C.c_void_p).value, count, stream) or 0)
+            except Exception:  # noqa: BLE001
+                return 13
         ops = ShardCollectives()
         ops.struct_size = C.sizeof(ShardCollectives)
         ops.all_reduce_max_u64 = ShardCollectives.ALL_REDUCE(_reduce)
