@@ -801,6 +801,55 @@ def cublas_tf32_tflops(dev) -> float:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def library_sgemm_leg(dev, stream, A, B, c_h, steps: int, warmup: int, ours_ms: float) -> dict:
+    """The reference's own contraction call on this GPU: cublasGemmEx with
+    CUBLAS_COMPUTE_32F_PEDANTIC in pedantic math mode (xvram_b200.native_baseline), on the
+    same resident operands and op pair as the headline step, timed the same way (warm-up,
+    then `steps` calls between CUDA events on the same stream).  Also how far its C lies
+    from this library's on the same inputs, as max|C_lib - C_ours| / (K max|a| max|b|):
+    both are strict FP32 with different summation orders."""
+    import torch
+    from xvram_b200 import device as xd
+    from xvram_b200.native_baseline import PedanticSgemm
+    try:
+        gemm = PedanticSgemm(stream.cuda_stream)
+    except (RuntimeError, OSError, AttributeError) as e:
+        return {"unavailable": str(e)}
+    with gemm, torch.cuda.stream(stream):
+        c0 = c_h.to(dev, non_blocking=False)
+        c_lib = c0.clone()
+
+        def call(c):
+            gemm(OP_A, OP_B, M, N, K, ALPHA, A.data_ptr(), K, B.data_ptr(), K, BETA,
+                 c.data_ptr(), M)
+
+        for _ in range(max(3, warmup)):
+            call(c_lib)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            call(c_lib)
+        e1.record(stream)
+        e1.synchronize()
+        lib_ms = e0.elapsed_time(e1) / steps
+        c_lib.copy_(c0)
+        c_ours = c0.clone()
+        call(c_lib)
+        assert xd.sgemm(OP_A, OP_B, M, N, K, ALPHA, A, K, B, K, BETA, c_ours, M,
+                        stream=stream) == 0
+        scale = K * float(A.abs().max()) * float(B.abs().max())
+        diff = float((c_lib - c_ours).abs().max()) / scale
+        stream.synchronize()
+        assert xd.kernel_status(stream) == 0
+        del c0, c_lib, c_ours
+    return {"what": "cublasGemmEx, CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_PEDANTIC_MATH: the "
+                    "reference's strict-FP32 contraction (src/gemm/executor.cpp:211-218, "
+                    "src/platform/cublas/cublas_api.cpp:634-686) on the headline operands",
+            "value": FLOP / (lib_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": lib_ms,
+            "ours_ms_per_step": ours_ms, "speedup_ours_over_library": lib_ms / ours_ms,
+            "max_normalized_diff_vs_ours": diff}
+
+
 def measured_tf32_peak():
     """Dense TF32 tensor peak implied by the driver-measured BF16 GEMM burst figure."""
     try:
@@ -981,6 +1030,7 @@ def main_gpu(args) -> None:
         kernel_ms = step_ms
     achieved = FLOP / (kernel_ms * 1e-3) / 1e12
     del B_slice, B_bufs
+    library = library_sgemm_leg(dev, stream, A, B, c_h, args.steps, args.warmup, kernel_ms)
 
     # ---------------- kernel-only, tensor-core path (three-term TF32 on tcgen05/TMEM)
     tc_need = lib.xvram_b200_sgemm_workspace_bytes(OP_A | 0x100, OP_B, M, N, K)
@@ -1249,6 +1299,8 @@ def main_gpu(args) -> None:
             "compat_trace": ({"path": args.trace, "records": trace_records,
                               "format": "xvram.cuda_compat_trace v1 (JSON lines)"}
                              if trace_records is not None else None),
+            # the reference's own library contraction on this GPU, same operands, for context
+            "library_sgemm": library,
             "ooc": ooc or None,
             "gpu_launches": args.steps * (1 + int(OP_A == 1) + int(OP_B == 0)),
             "gpu_launches_e2e": launches_e2e,

@@ -1,6 +1,9 @@
 """The compat bench on the B200 (child process: one compat initialisation per process):
 the suite scenario with an out-of-core GEMM through a 64 MiB budget completes with every
-proof and cleanup claim true."""
+proof and cleanup claim true; the four small shapes also match the reference's
+ordinary-cuBLAS baseline (cublasGemmEx, pedantic FP32) element for element within the
+bench's tolerance; the post-shutdown counters reconcile as the reference's compat
+contract asks."""
 from __future__ import annotations
 
 import json
@@ -28,3 +31,14 @@ def test_suite_on_the_gpu(tmp_path):
     assert all(w["mismatches"] == 0 for w in rep["workloads"])
     assert all(rep["proof"].values()) and all(rep["cleanup"].values())
     assert rep["compatibility"]["rejections_failed"] == 0
+    small = [w for w in rep["workloads"] if w["reference_kind"] == "cpu_fp64_full"]
+    assert len(small) == 4
+    assert all(w["native_baseline_equal"] is True and w["native_baseline_ms"] > 0
+               for w in small)
+    cache, execution = rep["cache"], rep["execution"]
+    assert cache["transactions_completed"] == execution["tiles_retired"]
+    assert cache["mappings"] == cache["set_access_calls"] == cache["unmaps"]
+    assert cache["event_boundaries"] == cache["unmaps"] and cache["resident_bytes"] == 0
+    assert cache["physical_handles_created"] == cache["physical_handles_released"]
+    assert rep["compatibility"]["retired_va_reservations"] == 0
+    assert execution["host_backing_peak_bytes"] <= rep["configuration"]["host_store_cap_bytes"]

@@ -29,7 +29,7 @@ def check_schema(rec: dict) -> None:
 
 
 def test_record_fields_and_limits():
-    check_schema(trace_record(1, 0, "call", 1, 4096, 64, 0, "malloc_device"))
+    check_schema(trace_record(1, 0, "call", 1, 4096, 64, 0, "cudaMalloc"))
     check_schema(trace_record(2, 5, "final", 0, None, 0, 3, "completed"))
     with pytest.raises(ValueError):
         trace_record(0, 0, "call", 1, None, 0, 0, "x")
@@ -84,7 +84,10 @@ def test_traced_call_sequence():
     assert kinds[-1] == "final" and kinds.count("final") == 1
     assert kinds.count("call") == kinds.count("return") == 5
     assert kinds.count("retired_tile") == 2
-    gemm_call = next(r for r in recs if r["reason"] == "blas_sgemm" and r["transition"] == "call")
+    gemm_call = next(r for r in recs if r["reason"] == "cublasSgemm" and r["transition"] == "call")
+    assert gemm_call["allocation_id"] is None and gemm_call["bytes"] == 4 * 3 * 64
+    assert [r["reason"] for r in recs if r["transition"] == "call"] == [
+        "cudaMalloc", "cudaMemcpyH2D", "cublasSgemm", "cudaMemcpyD2H", "cudaFree"]
     tiles = [r for r in recs if r["transition"] == "retired_tile"]
     assert all(t["operation_id"] == gemm_call["operation_id"] for t in tiles)
     assert [t["tiles_retired"] for t in tiles] == [1, 2]

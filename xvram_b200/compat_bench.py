@@ -23,8 +23,10 @@ C = alpha A B + beta C (a full FP64 sum for small shapes, the pattern's period-4
 form for large ones) within 1e-4 + 2e-5 |ref|, a padding element bit for bit.  Each
 rejection check makes an unsupported call and requires it to fail without submitting
 work (tiles, mappings and copied bytes unchanged).  Digests are the reference compat
-bench's.  The ordinary-cuBLAS baseline of the reference (native_baseline_*) is not run:
-there is no cuBLAS on this path; those fields are null.
+bench's.  For the small shapes the reference's ordinary-cuBLAS baseline runs too
+(native_baseline_*: the same storage through cublasGemmEx in pedantic FP32, every stored
+element within the tolerance of this library's); on a host without a CUDA device (the
+fake device) those fields are null.
 
 The compat table allows one initialisation per process: run this as its own process.
 """
@@ -173,7 +175,7 @@ def run(scenario="suite", m=4096, n=4096, k=4096, op_a=0, op_b=0, padding=0, off
             shapes.append(("gemm", m, n, k, padding, offset, op_a, op_b))
         for name, sm, sn, sk, pad, off, sa, sb in shapes:
             workloads.append(run_workload(api, calls, h, name, sm, sn, sk, pad, off, sa, sb,
-                                          seed, alpha, beta, passes))
+                                          seed, alpha, beta, passes, device))
             if workloads[-1]["mismatches"]:
                 raise RuntimeError("CPU reference or padding verification failed")
         if scenario in ("suite", "rejection"):
@@ -212,8 +214,42 @@ def run(scenario="suite", m=4096, n=4096, k=4096, op_a=0, op_b=0, padding=0, off
                         exit_code, reason, message, diagnostics, bool(sink), trace_records)
 
 
+def native_baseline(arrays, lds, m, n, k, offset, op_a, op_b, alpha, beta, passes, device):
+    """The reference's native baseline (src/compat_bench/native_baseline.cpp:10-130): the
+    same padded operand storage copied to the device and `passes` ordinary cuBLAS calls
+    (cublasGemmEx, CUBLAS_COMPUTE_32F_PEDANTIC, pedantic math; xvram_b200.native_baseline),
+    each followed by a stream synchronisation, timed together on the host clock.  Returns
+    C's storage and those milliseconds, or None on a host without a CUDA device (the
+    host-memory fake device), where the report's native_baseline_* fields stay null.  Like
+    the reference it takes small resident cases only (each operand at most 16 MiB)."""
+    try:
+        import torch
+    except ImportError:
+        return None
+    if not torch.cuda.is_available():
+        return None
+    from .native_baseline import PedanticSgemm
+    if any(a.nbytes > 16 << 20 for a in arrays):
+        raise RuntimeError("baseline is limited to small resident cases")
+    dev = torch.device("cuda", device)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.device(dev), torch.cuda.stream(stream):
+        t = [torch.from_numpy(a).to(dev) for a in arrays]
+        stream.synchronize()
+        with PedanticSgemm(stream.cuda_stream) as gemm:
+            t0 = time.perf_counter()
+            for _ in range(passes):
+                gemm(op_a, op_b, m, n, k, alpha, t[0].data_ptr() + 4 * offset, lds[0],
+                     t[1].data_ptr() + 4 * offset, lds[1], beta, t[2].data_ptr() + 4 * offset,
+                     lds[2])
+                stream.synchronize()
+            ms = (time.perf_counter() - t0) * 1e3
+        c = t[2].cpu().numpy()
+    return c, ms
+
+
 def run_workload(api, calls, h, name, m, n, k, padding, offset, op_a, op_b, seed, alpha, beta,
-                 passes) -> dict:
+                 passes, device=0) -> dict:
     before = api.telemetry()
     arrays = [fill(m, n, k, op_a, op_b, padding, offset, seed, w) for w in "abc"]
     lds = [storage(m, n, k, op_a, op_b, padding, offset, w)[2] for w in "abc"]
@@ -245,6 +281,16 @@ def run_workload(api, calls, h, name, m, n, k, padding, offset, op_a, op_b, seed
     bad = np.zeros(out.size, dtype=bool)
     bad[material] = ~ok.reshape(-1)
     bad[~material] = ~pad_ok
+    native_equal = native_ms = None
+    if full:
+        # every stored element, matrix and padding, against the ordinary cuBLAS result
+        # (reference src/compat_bench/executor.cpp:278-284, 326-329)
+        baseline = native_baseline(arrays, lds, m, n, k, offset, op_a, op_b, alpha, beta,
+                                   passes, device)
+        if baseline is not None:
+            base_ok = close_enough(out.astype(np.float64), baseline[0].astype(np.float64))
+            bad |= ~base_ok
+            native_equal, native_ms = bool(base_ok.all()), float(baseline[1])
     err = np.abs(actual - ref)
     for p in ptrs:
         calls.free(p)
@@ -271,7 +317,7 @@ def run_workload(api, calls, h, name, m, n, k, padding, offset, op_a, op_b, seed
         else 0.0,
         "digest": compat_digest(out), "reference_digest": compat_digest(expected),
         "reference_kind": "cpu_fp64_full" if full else "cpu_fp64_analytic_periodic_v1",
-        "native_baseline_equal": None, "native_baseline_ms": None,
+        "native_baseline_equal": native_equal, "native_baseline_ms": native_ms,
         "pass_timings": timing(timings),
     }
 
@@ -322,8 +368,11 @@ def build_report(generated, scenario, m, n, k, op_a, op_b, padding, offset, seed
                  diagnostics, trace_enabled, trace_records) -> dict:
     from .gemm_bench import device_query
     dev = device_query(device)
-    last = tel_last or tel_first
-    fin = tel_closed or last
+    # One snapshot for the whole report, taken after shutdown, as the reference's executor
+    # does (src/compat_bench/executor.cpp:433-447): the cache counters then show every
+    # frame unmapped and every physical handle released.
+    fin = tel_closed or tel_last or tel_first
+    last = fin
     rt = last.runtime if last is not None else None
     u = lambda x: int(x) if x is not None else 0
     mismatches = sum(w["mismatches"] for w in workloads)
@@ -334,8 +383,8 @@ def build_report(generated, scenario, m, n, k, op_a, op_b, padding, offset, seed
         "events_drained": bool(closed and fin and fin.cleanup_events_drained),
         "allocations_released": bool(fin and fin.allocations_released == fin.allocations_created),
         "handles_destroyed": bool(fin and fin.handles_destroyed == fin.handles_created),
-        "reservations_freed": bool(fin and fin.retired_va_reservations_freed ==
-                                   fin.retired_va_reservations),
+        "reservations_freed": bool(fin and fin.retired_va_reservations == 0 and
+                                   fin.retired_va_bytes == 0),
         "adapter_closed": bool(closed), "worker_terminated": bool(closed),
         "trace_closed": True,
     }

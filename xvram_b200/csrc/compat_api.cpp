@@ -33,6 +33,39 @@
 #include <new>
 #include <vector>
 
+#include <fstream>
+#include <string>
+#include <unistd.h>
+
+namespace {
+// Physical and currently available host RAM: /proc/meminfo's MemTotal and MemAvailable,
+// else the page counts sysconf reports.
+bool host_memory(uint64_t* physical, uint64_t* available) {
+  std::ifstream f("/proc/meminfo");
+  std::string key;
+  uint64_t kib = 0, total = 0, avail = 0;
+  std::string unit;
+  while (f >> key >> kib) {
+    std::getline(f, unit);
+    if (key == "MemTotal:")
+      total = kib << 10;
+    else if (key == "MemAvailable:")
+      avail = kib << 10;
+  }
+  if (!total || !avail) {
+    const long page = sysconf(_SC_PAGESIZE), pages = sysconf(_SC_PHYS_PAGES),
+               free_pages = sysconf(_SC_AVPHYS_PAGES);
+    if (page > 0 && pages > 0 && free_pages > 0) {
+      total = static_cast<uint64_t>(page) * static_cast<uint64_t>(pages);
+      avail = static_cast<uint64_t>(page) * static_cast<uint64_t>(free_pages);
+    }
+  }
+  *physical = total;
+  *available = avail;
+  return total != 0 && avail != 0;
+}
+} // namespace
+
 namespace xvram {
 namespace {
 
@@ -138,7 +171,29 @@ public:
     rc.budget_poll_ms = config->session.budget_poll_ms;
     rc.cache_policy = config->session.cache_policy;
     Error err;
-    try {
+    // Host-memory admission (reference src/cuda_compat/runtime_backend.cpp:103-139): keep
+    // max(4 GiB, physical / 4) of RAM free and cap the runtime's host ledger -- the pinned
+    // backing of every allocation -- at the rest of what is available now.
+    uint64_t physical = 0, available = 0;
+    if (!host_memory(&physical, &available))
+      err = make_error(XVRAM_STATUS_UNAVAILABLE, "cuda_compat", "host_budget",
+                       "host memory telemetry is required for raw backing admission");
+    const uint64_t host_headroom = std::max<uint64_t>(4ull << 30, physical / 4);
+    {
+      std::lock_guard lock(snap_mu_);
+      tel_.host_physical_bytes = physical;
+      tel_.host_available_bytes = available;
+    }
+    if (!err && available <= host_headroom)
+      err = make_error(XVRAM_STATUS_HOST_OUT_OF_MEMORY, "cuda_compat", "host_budget",
+                       "available RAM does not leave the automatic host headroom");
+    if (!err) {
+      rc.host_store_cap_bytes = available - host_headroom;
+      std::lock_guard lock(snap_mu_);
+      tel_.host_headroom_bytes = host_headroom;
+      tel_.host_store_cap_bytes = rc.host_store_cap_bytes;
+    }
+    if (!err) try {
       DeviceScope scope(rc.device_ordinal);
       auto factory = device_factory();
       std::unique_ptr<Device> dev = factory ? factory() : nullptr;
@@ -564,6 +619,7 @@ private:
     tel_.tiles_retired = x.tiles_retired;
     tel_.host_backing_bytes = x.host_backing_bytes;
     tel_.host_backing_peak_bytes = x.host_backing_peak_bytes;
+    tel_.host_budget_bytes = x.host_backing_bytes; // the host ledger now (current state)
     tel_.retired_va_reservations = x.retired_va_reservations;
     tel_.retired_va_bytes = x.retired_va_bytes;
     tel_.retired_va_reservations_freed = x.retired_va_reservations_freed;

@@ -216,6 +216,10 @@ struct Runtime::Impl {
   Error ensure_backing(Alloc& a) {
     if (a.host)
       return {};
+    if (cfg.host_store_cap_bytes && a.bytes > cfg.host_store_cap_bytes - std::min(
+                                                  cfg.host_store_cap_bytes, x.host_backing_bytes))
+      return make_error(XVRAM_STATUS_HOST_OUT_OF_MEMORY, "runtime", "host_backing",
+                        "the allocation's host backing would exceed the host store cap");
     void* p = nullptr;
     if (Error e = dev->host_alloc(a.bytes, &p))
       return e;
@@ -738,7 +742,9 @@ Error Runtime::close() {
       a.host = nullptr;
     }
     keep(m.dev->va_free(a.va, a.reserved));
-    if (!a.live) { // a tombstoned range of a released allocation
+    if (!a.live) { // a tombstoned range of a released allocation: current -> freed
+      --m.x.retired_va_reservations;
+      m.x.retired_va_bytes -= a.reserved;
       ++m.x.retired_va_reservations_freed;
       m.x.retired_va_bytes_freed += a.reserved;
     }
@@ -1102,12 +1108,15 @@ Error Runtime::gemm(const GemmCall& call) {
   uint64_t ws = 0;
   bool in_place = false;
   m.gemm_chunks(call, &keep, &ws, &in_place);
+  const uint64_t retired_before = m.x.tiles_retired;
   Error err = in_place ? m.gemm_in_place(call, A, B, C, keep, ws) : m.gemm_streamed(call, A, B, C);
   m.x.last_gemm_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   m.t.last_transaction_ms = m.x.last_gemm_ms;
+  // One residency transaction per retired tile, as the reference counts them: at
+  // quiescence transactions_completed equals tiles_retired (docs/cuda-compat.md:159).
   if (!err)
-    ++m.t.transactions_completed;
+    m.t.transactions_completed += m.x.tiles_retired - retired_before;
   return err;
 }
 
@@ -1471,6 +1480,9 @@ Error Runtime::Impl::gemm_streamed(const GemmCall& call, Alloc& A, Alloc& B, All
         break;
       wb_rec[cs] = 1;
       t.bytes_d2h += static_cast<uint64_t>(mr) * static_cast<uint64_t>(nr) * ec;
+      // A finished C tile leaves its slot dirty-for-home: one dirty eviction written back,
+      // so dirty_evictions == writebacks_completed as in the reference's accounting.
+      ++t.dirty_evictions;
       ++t.writebacks_completed;
     }
   }

@@ -50,6 +50,9 @@ struct RuntimeConfig {
   // Victim choice for resident chunks: 0 = CLOCK (the reference's default), 1 = LRU.
   // Streamed GEMMs evict panels by exact next use either way (the plan knows it).
   uint32_t cache_policy = 0;
+  // Cap on the host ledger (the pinned host backing of every allocation); 0 = none.  An
+  // allocation whose backing would pass it fails with HOST_OUT_OF_MEMORY.
+  uint64_t host_store_cap_bytes = 0;
   // Planning rates (estimates only; they steer geometry choice, never correctness).
   double flops_per_s = 70e12;
   double h2d_bytes_per_s = 50e9;
@@ -113,9 +116,10 @@ struct RuntimeExtra {
   uint64_t gemm_streamed = 0;
   uint64_t host_backing_bytes = 0;
   uint64_t host_backing_peak_bytes = 0;
+  // Tombstoned ranges of released allocations still reserved (current state; zero after
+  // close), and those released at close (cumulative).
   uint64_t retired_va_reservations = 0;
   uint64_t retired_va_bytes = 0;
-  // Tombstoned ranges released at close.
   uint64_t retired_va_reservations_freed = 0;
   uint64_t retired_va_bytes_freed = 0;
   // Last streamed plan.

@@ -1,7 +1,8 @@
 """Compat-call trace records in the reference's trace format.
 
-The reference's compat bench writes one JSON object per line for every compat API call it
-makes: a `call` record before, a `return` record after, a `retired_tile` record for each
+The reference's compat bench writes one JSON object per line for every CUDA / cuBLAS call it
+makes (reasons cudaMalloc, cudaMemcpyH2D, cublasSgemm, cudaMemcpyD2H, cudaFree): a `call`
+record before, a `return` record after, a `retired_tile` record for each
 GEMM tile retired in between (observed from the telemetry's tile counter) and one `final`
 record (reference src/compat_bench/main.cpp:105-200, src/compat_bench/report.cpp:390-410,
 schemas/cuda-compat-trace-v1.schema.json). `TracedCompat` produces the same records around
@@ -108,42 +109,47 @@ class TracedCompat:
             self._emit("retired_tile", None, 0, "observed_event_retirement")
 
     def _traced(self, name, allocation, nbytes, fn):
+        """A call record, the call, the tiles it retired, its return record.  A call that
+        raises gets no return record (the reference's bench stops at its first failure),
+        so the final record then closes the trace with that call still open."""
         self.operation += 1
         self._emit("call", allocation, nbytes, name)
         try:
             out = fn()
-        except Exception:
+        finally:
             self._retired()
-            self._emit("return", allocation, nbytes, name + ":failed")
-            raise
-        self._retired()
         self._emit("return", allocation, nbytes, name)
         return out
 
+    # Reasons and fields as the reference's bench writes them for the CUDA / cuBLAS calls
+    # these compat entries stand in for (src/compat_bench/executor.cpp:241-347).
     def malloc(self, nbytes):
         self.next_allocation += 1
         ident = self.next_allocation
-        ptr = self._traced("malloc_device", ident, nbytes, lambda: self.api.malloc(nbytes))
+        ptr = self._traced("cudaMalloc", ident, nbytes, lambda: self.api.malloc(nbytes))
         self.allocations[ptr] = (ident, nbytes)
         return ptr
 
     def free(self, ptr):
         ident = self._allocation(ptr)
-        out = self._traced("free_device", ident, 0, lambda: self.api.free(ptr))
+        size = self.allocations.get(ptr, (None, 0))[1]
+        out = self._traced("cudaFree", ident, size, lambda: self.api.free(ptr))
         self.allocations.pop(ptr, None)
         return out
 
     def h2d(self, dst, src_ptr, nbytes):
-        return self._traced("memcpy_h2d", self._allocation(dst), nbytes,
+        return self._traced("cudaMemcpyH2D", self._allocation(dst), nbytes,
                             lambda: self.api.h2d(dst, src_ptr, nbytes))
 
     def d2h(self, dst_ptr, src, nbytes):
-        return self._traced("memcpy_d2h", self._allocation(src), nbytes,
+        return self._traced("cudaMemcpyD2H", self._allocation(src), nbytes,
                             lambda: self.api.d2h(dst_ptr, src, nbytes))
 
     def sgemm(self, h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc):
-        return self._traced("blas_sgemm", self._allocation(c), 0, lambda: self.api.sgemm(
-            h, op_a, op_b, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc))
+        """No allocation id; bytes = the logical operand bytes 4 (mk + kn + mn)."""
+        return self._traced("cublasSgemm", None, 4 * (m * k + k * n + m * n),
+                            lambda: self.api.sgemm(h, op_a, op_b, m, n, k, alpha, a, lda, b,
+                                                   ldb, beta, c, ldc))
 
     def close(self, ok: bool = True) -> None:
         self._retired()
