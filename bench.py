@@ -832,6 +832,7 @@ def library_sgemm_leg(dev, stream, A, B, c_h, steps: int, warmup: int, ours_ms: 
         e1.record(stream)
         e1.synchronize()
         lib_ms = e0.elapsed_time(e1) / steps
+        version = gemm.version()
         c_lib.copy_(c0)
         c_ours = c0.clone()
         call(c_lib)
@@ -845,6 +846,7 @@ def library_sgemm_leg(dev, stream, A, B, c_h, steps: int, warmup: int, ours_ms: 
     return {"what": "cublasGemmEx, CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_PEDANTIC_MATH: the "
                     "reference's strict-FP32 contraction (src/gemm/executor.cpp:211-218, "
                     "src/platform/cublas/cublas_api.cpp:634-686) on the headline operands",
+            "cublas_version": version,
             "value": FLOP / (lib_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": lib_ms,
             "ours_ms_per_step": ours_ms, "speedup_ours_over_library": lib_ms / ours_ms,
             "max_normalized_diff_vs_ours": diff}

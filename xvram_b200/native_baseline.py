@@ -74,6 +74,14 @@ class PedanticSgemm:
             C.c_void_p(b), CUDA_R_32F, ldb, C.byref(be), C.c_void_p(c), CUDA_R_32F, ldc,
             CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT), "cublasGemmEx")
 
+    def version(self) -> int:
+        """cublasGetVersion_v2: major * 10000 + minor * 100 + patch (12.9.1 -> 120901)."""
+        v = C.c_int(0)
+        self._lib.cublasGetVersion_v2.argtypes = [C.c_void_p, C.POINTER(C.c_int)]
+        self._lib.cublasGetVersion_v2.restype = C.c_int
+        self._check(self._lib.cublasGetVersion_v2(self._h, C.byref(v)), "cublasGetVersion_v2")
+        return int(v.value)
+
     def close(self) -> None:
         if self._h:
             self._lib.cublasDestroy_v2(self._h)
