@@ -62,36 +62,28 @@ namespace {
 #ifndef XVRAM_FFMA_STAGES
 #define XVRAM_FFMA_STAGES 4
 #endif
-// Groups of 4 k unrolled per loop iteration.  With one FFMA per FMA, 2 keeps the loop
-// body (~1,100 instructions) small enough for the instruction cache; the fully unrolled
-// 32-k stage (8) stalls on instruction fetch (ncu: no_instruction 0.61 per issue) and runs
-// ~2 % slower.  The packed M-/N-major loop has half the FMA instructions and runs best
-// fully unrolled (C2: 1, 2, 4, 8 groups -> 56.9, 55.5, 61.1, 61.5 TFLOP/s).
+// Groups of 4 k unrolled per loop iteration of the K-major kernels.  With one FFMA per
+// FMA, 2 keeps the loop body (~1,100 instructions) small enough for the instruction cache;
+// the fully unrolled 32-k stage (8) stalls on instruction fetch (ncu: no_instruction 0.61
+// per issue) and runs ~2 % slower.  The packed M-/N-major stage has half the FMA
+// instructions and runs fully unrolled (C2: 1, 2, 4, 8 groups -> 56.9, 55.5, 61.1, 61.5
+// TFLOP/s).
 #ifndef XVRAM_FFMA_GROUP_UNROLL
 #define XVRAM_FFMA_GROUP_UNROLL 2
-#endif
-#ifndef XVRAM_FFMA_GROUP_UNROLL_MN
-#define XVRAM_FFMA_GROUP_UNROLL_MN 8
-#endif
-// Packed FP32 FMA (FFMA2, sm_100) for N-major B tiles: one instruction updates two
-// adjacent accumulator columns, which halves the FMA issue slots per k and leaves room for
-// the shared-memory loads and address arithmetic.  Per component it is the same
-// round-to-nearest FMA as fmaf, so results are bit-identical either way.
-#ifndef XVRAM_FFMA_PACKED
-#define XVRAM_FFMA_PACKED 1
 #endif
 constexpr int kBM = 128;
 constexpr int kBK = 32;
 constexpr int kStages = XVRAM_FFMA_STAGES;
 constexpr int kGroupUnroll = XVRAM_FFMA_GROUP_UNROLL;
-constexpr int kGroupUnrollMN = XVRAM_FFMA_GROUP_UNROLL_MN;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kTnCount = kThreads / 16;     // threads sharing an A fragment: 16 B fragments
+constexpr int kCtasPerSm = 1;               // the ring takes ~193 KB of shared memory
 constexpr int kAStageFloats = kBM * kBK;
 
 // Thread tile 8 x TN (TN = 8 or 16): CTA tile 128 x (16 * TN).
 template <int TN> struct TileCfg {
-  static constexpr int BN = 16 * TN;
+  static constexpr int BN = kTnCount * TN;
   static constexpr int BStageFloats = BN * kBK;
   static constexpr uint32_t StageBytes = (kAStageFloats + BStageFloats) * sizeof(float);
   static constexpr int SmemBytes =
@@ -150,11 +142,11 @@ __device__ __forceinline__ void load_frag(const float* tile, int g, int t, float
 
 // Tile-local row (or column) of a thread's i-th fragment entry: 16-strided rows for
 // K-major tiles, groups of four consecutive rows every 64 for M/N-major tiles.
-template <bool KMAJOR> __device__ __forceinline__ int frag_index(int t, int i) {
+template <bool KMAJOR, int S = 16> __device__ __forceinline__ int frag_index(int t, int i) {
   if constexpr (KMAJOR)
-    return t + 16 * i;
+    return t + S * i;
   else
-    return 64 * (i >> 2) + 4 * t + (i & 3);
+    return 4 * S * (i >> 2) + 4 * t + (i & 3);
 }
 
 // Accumulators: acc[i][j / 2] holds columns j (x) and j + 1 (y) of row i.
@@ -169,7 +161,7 @@ __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const floa
   const int chunk = (g ^ (tn & 7)) * 4;
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const float4 v = *reinterpret_cast<const float4*>(bs + (tn + 16 * j) * kBK + chunk);
+    const float4 v = *reinterpret_cast<const float4*>(bs + (tn + kTnCount * j) * kBK + chunk);
     const float b[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
@@ -187,14 +179,14 @@ __device__ __forceinline__ void ffma_group_bk(const float (&a)[4][8], const floa
 template <int TN, int NJ>
 __device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const float* bs, int g,
                                               int tn, float2 (&acc)[8][NJ / 2]) {
-  constexpr int BN = 16 * TN;
+  constexpr int BN = kTnCount * TN;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const float* row = bs + (4 * g + kk) * BN + 4 * tn;
     float2 b[NJ / 2];
 #pragma unroll
     for (int q = 0; q < NJ / 4; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(row + 64 * q);
+      const float4 v = *reinterpret_cast<const float4*>(row + 4 * kTnCount * q);
       b[2 * q + 0] = make_float2(v.x, v.y);
       b[2 * q + 1] = make_float2(v.z, v.w);
     }
@@ -210,41 +202,47 @@ __device__ __forceinline__ void ffma_group_bn(const float (&a)[4][8], const floa
   }
 }
 
-// M-major A and N-major B (the layout the canonicalising transposes produce): one k at a
-// time, loading that k's 8 A values and NJ B values just before their FMAs, which keeps the
-// packed form's duplicated A values within the register budget.
+// One 32-k stage of M-major A and N-major B (the layout the canonicalising transposes
+// produce).  Per k a thread loads its 8 A values (two 16-byte loads) and NJ B values, and
+// issues 8 x NJ / 2 packed FP32 FMAs (FFMA2, sm_100: one instruction updates two adjacent
+// accumulator columns with the same round-to-nearest FMA per component as fmaf, so the
+// bits equal the scalar form's).  The next k's fragments are loaded into a second register
+// set before the current k's FMAs (CUDA events, C2: 6.692 against 6.699 ms with the loads
+// issued just before their own FMAs).
 template <int TN, int NJ>
-__device__ __forceinline__ void ffma_group_mn(const float* as, const float* bs, int g, int tm,
-                                              int tn, float2 (&acc)[8][NJ / 2]) {
-  constexpr int BN = 16 * TN;
+__device__ __forceinline__ void ffma_stage_mn(const float* as, const float* bs, int tm, int tn,
+                                              float2 (&acc)[8][NJ / 2]) {
+  constexpr int BN = kTnCount * TN;
+  float4 al[2], ah[2], bv[2][NJ / 4];
+  auto load = [&](int kk, int slot) {
+    const float* arow = as + kk * kBM + 4 * tm;
+    al[slot] = *reinterpret_cast<const float4*>(arow);
+    ah[slot] = *reinterpret_cast<const float4*>(arow + 64);
+    const float* brow = bs + kk * BN + 4 * tn;
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    const float* arow = as + (4 * g + kk) * kBM + 4 * tm;
-    const float4 alo = *reinterpret_cast<const float4*>(arow);
-    const float4 ahi = *reinterpret_cast<const float4*>(arow + 64);
-    const float a[8] = {alo.x, alo.y, alo.z, alo.w, ahi.x, ahi.y, ahi.z, ahi.w};
-    const float* brow = bs + (4 * g + kk) * BN + 4 * tn;
+    for (int q = 0; q < NJ / 4; ++q)
+      bv[slot][q] = *reinterpret_cast<const float4*>(brow + 4 * kTnCount * q);
+  };
+  load(0, 0);
+#pragma unroll
+  for (int kk = 0; kk < kBK; ++kk) {
+    const int cur = kk & 1;
+    if (kk + 1 < kBK)
+      load(kk + 1, cur ^ 1);
+    const float a[8] = {al[cur].x, al[cur].y, al[cur].z, al[cur].w,
+                        ah[cur].x, ah[cur].y, ah[cur].z, ah[cur].w};
     float2 b[NJ / 2];
 #pragma unroll
     for (int q = 0; q < NJ / 4; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(brow + 64 * q);
-      b[2 * q + 0] = make_float2(v.x, v.y);
-      b[2 * q + 1] = make_float2(v.z, v.w);
+      b[2 * q + 0] = make_float2(bv[cur][q].x, bv[cur][q].y);
+      b[2 * q + 1] = make_float2(bv[cur][q].z, bv[cur][q].w);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-#if XVRAM_FFMA_PACKED
       const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
       for (int j2 = 0; j2 < NJ / 2; ++j2)
         acc[i][j2] = __ffma2_rn(ai, b[j2], acc[i][j2]);
-#else
-#pragma unroll
-      for (int j2 = 0; j2 < NJ / 2; ++j2) {
-        acc[i][j2].x = fmaf(a[i], b[j2].x, acc[i][j2].x);
-        acc[i][j2].y = fmaf(a[i], b[j2].y, acc[i][j2].y);
-      }
-#endif
     }
   }
 }
@@ -314,7 +312,7 @@ __device__ __forceinline__ void prefetch_c(const FfmaParams& p, int m0, int n0) 
   const int tn = threadIdx.x >> 4;
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const int col = n0 + frag_index<B_KMAJOR>(tn, j);
+    const int col = n0 + frag_index<B_KMAJOR, kTnCount>(tn, j);
     if (col < p.n) {
       const float* cc = p.c + static_cast<long long>(col) * p.ldc;
 #pragma unroll
@@ -341,7 +339,7 @@ __device__ __forceinline__ void epilogue(const FfmaParams& p, int m0, int n0,
     float cv[2][8];
 #pragma unroll
     for (int jj = 0; jj < 2; ++jj) {
-      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      const int col = n0 + frag_index<B_KMAJOR, kTnCount>(tn, j0 + jj);
       const float* cc = p.c + static_cast<long long>(col) * p.ldc;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -351,7 +349,7 @@ __device__ __forceinline__ void epilogue(const FfmaParams& p, int m0, int n0,
     }
 #pragma unroll
     for (int jj = 0; jj < 2; ++jj) {
-      const int col = n0 + frag_index<B_KMAJOR>(tn, j0 + jj);
+      const int col = n0 + frag_index<B_KMAJOR, kTnCount>(tn, j0 + jj);
       if (col >= p.n)
         continue;
       float* cc = p.c + static_cast<long long>(col) * p.ldc;
@@ -403,9 +401,7 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
     const float* as = smem_a + s * kAStageFloats;
     const float* bs = smem_b + s * Cfg::BStageFloats;
     if constexpr (!A_KMAJOR && !B_KMAJOR) {
-#pragma unroll kGroupUnrollMN
-      for (int g = 0; g < kBK / 4; ++g)
-        ffma_group_mn<TN, NJ>(as, bs, g, tm, tn, acc);
+      ffma_stage_mn<TN, NJ>(as, bs, tm, tn, acc);
     } else {
 #pragma unroll kGroupUnroll
       for (int g = 0; g < kBK / 4; ++g) {
@@ -440,7 +436,7 @@ __device__ __forceinline__ void tile_main(const CUtensorMap* tmap_a, const CUten
 }
 
 template <bool A_KMAJOR, bool B_KMAJOR, int TN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     sgemm_ffma_tma(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const FfmaParams p) {
   using Cfg = TileCfg<TN>;
@@ -518,8 +514,75 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same transpose with 64 x 64 tiles and 16-byte global loads and stores on both sides
+// (four 16-byte accesses in flight per thread, eight blocks per SM), for 16-byte aligned
+// bases and leading dimensions that are multiples of 4 floats; a tile's ragged edge falls
+// back to 4-byte accesses.
+__global__ void __launch_bounds__(256)
+    transpose_f32_vec4(const float* __restrict__ src, long long lds, float* __restrict__ dst,
+                       long long ldd, int rows, int cols, int tiles_r) {
+  __shared__ float tile[64][65]; // [column of src][row of src]
+  const int tr = blockIdx.x % tiles_r;
+  const int tc = blockIdx.x / tiles_r;
+  const int r0 = tr * 64, c0 = tc * 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int r = r0 + 4 * tx;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int cl = ty + 16 * j, c = c0 + cl;
+    if (c >= cols)
+      continue;
+    const float* s = src + static_cast<long long>(c) * lds + r;
+    float v[4];
+    if (r + 3 < rows) {
+      const float4 q = *reinterpret_cast<const float4*>(s);
+      v[0] = q.x;
+      v[1] = q.y;
+      v[2] = q.z;
+      v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[e] = r + e < rows ? s[e] : 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      tile[cl][4 * tx + e] = v[e];
+  }
+  __syncthreads();
+  const int c = c0 + 4 * tx;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int rl = ty + 16 * j, rr = r0 + rl;
+    if (rr >= rows)
+      continue;
+    float* d = dst + static_cast<long long>(rr) * ldd + c;
+    const float v[4] = {tile[4 * tx][rl], tile[4 * tx + 1][rl], tile[4 * tx + 2][rl],
+                        tile[4 * tx + 3][rl]};
+    if (c + 3 < cols) {
+      *reinterpret_cast<float4*>(d) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (c + e < cols)
+          d[e] = v[e];
+    }
+  }
+}
+
 cudaError_t launch_transpose(const float* src, long long lds, float* dst, long long ldd, int rows,
                              int cols, cudaStream_t stream) {
+  const bool vec4 = (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 && lds % 4 == 0 &&
+                    ldd % 4 == 0;
+  if (vec4) {
+    const long long tr = (rows + 63) / 64, tc = (cols + 63) / 64;
+    if (tr * tc > 0x7fffffffll)
+      return cudaErrorInvalidConfiguration;
+    transpose_f32_vec4<<<static_cast<unsigned>(tr * tc), 256, 0, stream>>>(
+        src, lds, dst, ldd, rows, cols, static_cast<int>(tr));
+    return cudaGetLastError();
+  }
   const long long tiles_r = (rows + 31) / 32, tiles_c = (cols + 31) / 32;
   if (tiles_r * tiles_c > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
@@ -653,7 +716,7 @@ cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, FfmaParams 
   if (cudaError_t e = configure_once<AK, BK, TN>(); e != cudaSuccess)
     return e;
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  const long long sms = sm_count();
+  const long long sms = static_cast<long long>(sm_count()) * kCtasPerSm;
   const long long tail = tiles % sms;
   long long grid = tiles;
   p.full_tiles = static_cast<int>(tiles);
@@ -821,7 +884,7 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
   // Wide tiles halve shared-memory traffic per FFMA; narrow N keeps 128-wide tiles so
   // fewer columns are wasted on padding.
   const int tn = n > 128 ? 16 : 8;
-  const int bn = 16 * tn;
+  const int bn = kTnCount * tn;
   CUtensorMap ta, tb;
   bool ok = a_kmajor ? encode_2d(&ta, a, k, m, lda, kBK, kBM, true)
                      : encode_2d(&ta, a, m, k, lda, kBM, kBK, false);
