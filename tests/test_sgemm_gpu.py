@@ -246,3 +246,34 @@ def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape):
     assert np.array_equal(outs[0], outs[1])
     check(outs[0], ref, c, m, k, a, b)
 
+
+
+@pytest.mark.parametrize("op_a,op_b", OPS)
+@pytest.mark.parametrize("shape", [(513, 385, 129), (1024, 768, 1000), (300, 200, 4096)])
+def test_matches_the_reference_library_contraction(oracle, op_a, op_b, shape):
+    """Against the reference's own GPU contraction on the same device inputs: cuBLAS
+    cublasGemmEx with CUBLAS_COMPUTE_32F_PEDANTIC in pedantic math mode
+    (xvram_b200.native_baseline; reference src/gemm/executor.cpp:211-218).  Both are strict
+    FP32 with different summation orders, so they agree within the SGEMM tolerance of each
+    other, and each is within it of the FP64 oracle."""
+    from xvram_b200.native_baseline import PedanticSgemm
+    m, n, k = shape
+    a, lda, b, ldb, c, ldc = operands(oracle, op_a, op_b, m, n, k, (0, 0, 0), 70)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    ours, lib = torch.from_numpy(c).cuda(), torch.from_numpy(c).cuda()
+    assert device.sgemm(op_a, op_b, m, n, k, 0.5, A, lda, B, ldb, 1.5, ours, ldc) == 0
+    assert device.kernel_status() == 0
+    try:
+        gemm = PedanticSgemm(torch.cuda.current_stream().cuda_stream)
+    except RuntimeError as e:
+        pytest.skip(str(e))
+    with gemm:
+        gemm(op_a, op_b, m, n, k, 0.5, A.data_ptr(), lda, B.data_ptr(), ldb, 1.5,
+             lib.data_ptr(), ldc)
+    torch.cuda.synchronize()
+    o, l = ours.cpu().numpy(), lib.cpu().numpy()
+    ref = oracle.gemm(op_a, op_b, m, n, k, 0.5, a, lda, b, ldb, 1.5, c, ldc)
+    amax, bmax = float(np.abs(a).max()), float(np.abs(b).max())
+    assert normalized_error(o[:, :m], l[:, :m].astype(np.float64), k, amax, bmax) <= TOLERANCE
+    assert normalized_error(o[:, :m], ref, k, amax, bmax) <= TOLERANCE
+    assert normalized_error(l[:, :m], ref, k, amax, bmax) <= TOLERANCE

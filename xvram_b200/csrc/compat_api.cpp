@@ -173,7 +173,7 @@ public:
     Error err;
     // Host-memory admission (reference src/cuda_compat/runtime_backend.cpp:103-139): keep
     // max(4 GiB, physical / 4) of RAM free and cap the runtime's host ledger -- the pinned
-    // backing of every allocation -- at the rest of what is available now.
+    // host backing of allocations -- at the rest of what is available now.
     uint64_t physical = 0, available = 0;
     if (!host_memory(&physical, &available))
       err = make_error(XVRAM_STATUS_UNAVAILABLE, "cuda_compat", "host_budget",
