@@ -50,7 +50,7 @@ struct RuntimeConfig {
   // Victim choice for resident chunks: 0 = CLOCK (the reference's default), 1 = LRU.
   // Streamed GEMMs evict panels by exact next use either way (the plan knows it).
   uint32_t cache_policy = 0;
-  // Cap on the host ledger (the pinned host backing of every allocation); 0 = none.  An
+  // Cap on the host ledger (the pinned host backing of allocations); 0 = none.  An
   // allocation whose backing would pass it fails with HOST_OUT_OF_MEMORY.
   uint64_t host_store_cap_bytes = 0;
   // Planning rates (estimates only; they steer geometry choice, never correctness).
