@@ -58,6 +58,17 @@ XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_
                                                                     int64_t m, int64_t n,
                                                                     int64_t k);
 
+/* The C tile (rows x columns) the TMA-fed FFMA kernel uses for an m x n problem whose
+ * operands are M-major / N-major (as they are after the K-major ones are transposed into
+ * workspace) on the current device: 192 x 192 (12 warps), 128 x 256 or 128 x 128 (8 warps),
+ * whichever takes fewer tile-waves on the device's SM count.  Every tiling computes each
+ * output as the same FFMA chain in k order, so results do not depend on it.
+ * INVALID_ARGUMENT for m or n outside [1, INT32_MAX] or a null output.  No reference
+ * counterpart. */
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_tile_shape(int64_t m, int64_t n,
+                                                                 int32_t* tile_m,
+                                                                 int32_t* tile_n);
+
 /*
  * xvram_b200_sgemm_device with caller-provided device workspace (256-byte aligned).  With
  * at least xvram_b200_sgemm_workspace_bytes, K-major operands are transposed into it and

@@ -43,21 +43,28 @@ m, n, k = 1024, 768, 512                      # op(A) = N, op(B) = T: no transpo
 a, b, c = orc.uniform(m * k, 1), orc.uniform(n * k, 2), orc.uniform(m * n, 3)
 A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
 
-# 1. the device entry point: the launch succeeds, the error word says the wait ran out
+# 1. the device entry point, for both tilings (1024 x 768 runs 128 x 256 tiles, 2304 x 2304
+# runs 192 x 192): the launch succeeds, the error word says the wait ran out
+for (mm, nn) in ((m, n), (2304, 2304)):
+    aa, bb = orc.uniform(mm * k, 1), orc.uniform(nn * k, 2)
+    AA, BB = torch.from_numpy(aa).cuda(), torch.from_numpy(bb).cuda()
+    Cd = torch.zeros(mm * nn, device="cuda")
+    lib.xvram_b200_test_set_kernel_stall(2_000_000)
+    assert xd.sgemm(0, 1, mm, nn, k, 1.0, AA, mm, BB, nn, 0.0, Cd, mm, path=xd.PATH_TMA) == 0
+    word = C.c_uint32(0)
+    assert lib.xvram_b200_kernel_status(0, C.byref(word)) == 0
+    assert word.value & 1, word.value             # bit 0: a consumer wait gave up
+    assert xd.kernel_status() == 0                 # reading cleared it
+    # the context is still usable: the same GEMM without the stall is correct
+    lib.xvram_b200_test_set_kernel_stall(0)
+    assert xd.sgemm(0, 1, mm, nn, k, 1.0, AA, mm, BB, nn, 0.0, Cd, mm, path=xd.PATH_TMA) == 0
+    assert xd.kernel_status() == 0
+    ref = orc.gemm(0, 1, mm, nn, k, 1.0, aa, mm, bb, nn, 0.0, None, mm)
+    err = normalized_error(Cd.cpu().numpy().reshape(nn, mm), ref, k, 1.0, 1.0)
+    assert err <= TOLERANCE, err
+if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+    assert xd.tile_shape(m, n) == (128, 256) and xd.tile_shape(2304, 2304) == (192, 192)
 Cd = torch.from_numpy(c).cuda()
-lib.xvram_b200_test_set_kernel_stall(2_000_000)
-assert xd.sgemm(0, 1, m, n, k, 1.0, A, m, B, n, 0.0, Cd, m, path=xd.PATH_TMA) == 0
-word = C.c_uint32(0)
-assert lib.xvram_b200_kernel_status(0, C.byref(word)) == 0
-assert word.value & 1, word.value             # bit 0: a consumer wait gave up
-assert xd.kernel_status() == 0                 # reading cleared it
-# the context is still usable: the same GEMM without the stall is correct
-lib.xvram_b200_test_set_kernel_stall(0)
-assert xd.sgemm(0, 1, m, n, k, 1.0, A, m, B, n, 0.0, Cd, m, path=xd.PATH_TMA) == 0
-assert xd.kernel_status() == 0
-ref = orc.gemm(0, 1, m, n, k, 1.0, a, m, b, n, 0.0, None, m)
-err = normalized_error(Cd.cpu().numpy().reshape(n, m), ref, k, 1.0, 1.0)
-assert err <= TOLERANCE, err
 
 # 2. the compat adapter: blas_sgemm returns once queued; the copy of C reports TIMEOUT
 api = cp.CompatApi()

@@ -77,3 +77,22 @@ def test_get_api_contract_without_gpu():
     assert cp.get_api(size=C.sizeof(cp.ApiTable) - 8)[0] == cp.INCOMPATIBLE_ABI
     for name in cp.FN_TYPES:
         assert getattr(table, name), name
+
+
+def test_tile_shape_choice_without_a_gpu():
+    """xvram_b200_sgemm_tile_shape on a host without a device assumes a 148-SM B200: 192 x 192
+    tiles where their waves cost less than 128 x 256 tiles' at 0.95 of the FMA rate, 128 x 128
+    for N <= 128, and INVALID_ARGUMENT for sizes outside [1, INT32_MAX] or null outputs."""
+    import ctypes as C
+    from xvram_b200 import device
+    from xvram_b200._native import lib
+    assert device.tile_shape(8192, 6144) == (192, 192)      # C2: 9.5 against 10.5 / 0.95 waves
+    assert device.tile_shape(9216, 9216) == (192, 192)
+    assert device.tile_shape(2560, 2048) == (128, 256)      # 1.5 against 1.08 / 0.95 waves
+    assert device.tile_shape(8192, 512) == (128, 256)       # 512 = 2 x 256, 2.67 x 192
+    assert device.tile_shape(4096, 100) == (128, 128)
+    assert device.tile_shape(100, 4096) == (128, 256)       # M <= 128: 8 warps
+    tm, tn = C.c_int32(0), C.c_int32(0)
+    for m, n in ((0, 5), (5, 0), (1 << 31, 5), (-1, 5)):
+        assert lib.xvram_b200_sgemm_tile_shape(m, n, C.byref(tm), C.byref(tn)) == 1
+    assert lib.xvram_b200_sgemm_tile_shape(5, 5, None, C.byref(tn)) == 1

@@ -229,16 +229,25 @@ def test_workspace_query():
 
 
 @pytest.mark.parametrize("op_a,op_b", [(0, 1), (1, 0)])
-@pytest.mark.parametrize("shape", [(2560, 2048, 96),   # 160 tiles: 12-tile tail, split
-                                   (1300, 700, 64),    # 33 tiles: all half-width
-                                   (2560, 1280, 64),   # 100 tiles: tail too big to split
-                                   (2000, 3000, 700),  # 192 tiles: 44-tile tail, split
-                                   (4096, 8192, 160),  # 1024 tiles: 136-tile tail, not split
-                                   (2560, 1280, 256)])  # 100 tiles: one partial wave
-def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape):
-    """The TMA kernel runs a last, at most half-full wave as half-width tiles; every output
-    is still one FFMA chain in k order, so its bits equal the generic kernel's."""
+@pytest.mark.parametrize("shape,tile", [
+    ((2560, 2048, 96), (128, 256)),    # 160 tiles: 12-tile tail, split
+    ((1300, 700, 64), (128, 256)),     # 33 tiles: all half-width
+    ((2560, 1280, 64), (128, 256)),    # 100 tiles: tail too big to split
+    ((2000, 3000, 700), (128, 256)),   # 192 tiles: 44-tile tail, split
+    ((2560, 1280, 256), (128, 256)),   # 100 tiles: one partial wave
+    ((4096, 8192, 160), (192, 192)),   # 946 tiles: 58-tile tail, split
+    ((2688, 2688, 96), (192, 192)),    # 196 tiles: 48-tile tail, split
+    ((4224, 2304, 64), (192, 192)),    # 264 tiles: 116-tile tail, not split
+    ((2300, 2290, 100), (192, 192)),   # 144 ragged tiles, one partial wave, ragged k
+    ((8192, 6144, 64), (192, 192))])   # C2's M and N: 1376 tiles, 44-tile tail, split
+def test_tail_split_is_bit_identical_to_generic(oracle, op_a, op_b, shape, tile):
+    """Both tilings of the TMA kernel (12 warps on 192 x 192 tiles, 8 warps on 128 x 256)
+    run a last, at most half-full wave as half-width tiles; every output is still one FFMA
+    chain in k order, so its bits equal the generic kernel's.  The tiling each shape gets
+    (on a 148-SM B200) is checked first, so both forms and both tail cases are covered."""
     m, n, k = shape
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert device.tile_shape(m, n) == tile
     outs = []
     for path in (TMA, GENERIC):
         out, ref, c, a, b = run(oracle, op_a, op_b, m, n, k, 0.5, 1.5, seed=70, path=path)

@@ -103,6 +103,8 @@ def _load() -> C.CDLL:
     lib.xvram_b200_sgemm_device_noalloc.restype = u32
     lib.xvram_b200_sgemm_workspace_bytes.argtypes = [u32, u32, i64, i64, i64]
     lib.xvram_b200_sgemm_workspace_bytes.restype = u64
+    lib.xvram_b200_sgemm_tile_shape.argtypes = [i64, i64, C.POINTER(i32), C.POINTER(i32)]
+    lib.xvram_b200_sgemm_tile_shape.restype = u32
     lib.xvram_b200_shard_unique_id.argtypes = [vp, u64]
     lib.xvram_b200_shard_unique_id.restype = u32
     lib.xvram_b200_shard_group_create.argtypes = [vp, u64, i32, i32, C.POINTER(u64)]
@@ -190,6 +192,7 @@ EXPORTED = (
     "xvram_b200_sgemm_device",
     "xvram_b200_sgemm_device_ws",
     "xvram_b200_sgemm_workspace_bytes",
+    "xvram_b200_sgemm_tile_shape",
     "xvram_b200_sgemm_device_noalloc",
     "xvram_b200_kernel_status",
     "xvram_b200_shard_unique_id",

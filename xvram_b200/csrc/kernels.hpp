@@ -19,6 +19,9 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
 // Workspace that sgemm_ffma_ws uses to canonicalise K-major operands (0 when op(A) = N
 // and op(B) = T, which the kernel already reads in its fastest form).
 uint64_t sgemm_workspace_bytes(int op_a, int op_b, int m, int n, int k);
+// The C tile the TMA kernel uses for an M-/N-major (canonicalised) m x n problem on the
+// current device: 192 x 192, 128 x 256 or 128 x 128.
+void sgemm_tile_shape(int m, int n, int* tile_m, int* tile_n);
 
 // sgemm_ffma with a workspace: when the workspace is at least sgemm_workspace_bytes and
 // 256-byte aligned, K-major operands are transposed into it first and the M-major /

@@ -168,6 +168,18 @@ XVRAM_B200_API uint64_t XVRAM_CALL xvram_b200_sgemm_workspace_bytes(uint32_t op_
                                static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
 }
 
+XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_tile_shape(int64_t m, int64_t n,
+                                                                 int32_t* tile_m,
+                                                                 int32_t* tile_n) {
+  if (m <= 0 || n <= 0 || m > INT32_MAX || n > INT32_MAX || !tile_m || !tile_n)
+    return XVRAM_STATUS_INVALID_ARGUMENT;
+  int tm = 0, tn = 0;
+  sgemm_tile_shape(static_cast<int>(m), static_cast<int>(n), &tm, &tn);
+  *tile_m = tm;
+  *tile_n = tn;
+  return XVRAM_STATUS_SUCCESS;
+}
+
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_device_ws(
     uint32_t op_a, uint32_t op_b, int64_t m, int64_t n, int64_t k, float alpha, const float* a,
     int64_t lda, const float* b, int64_t ldb, float beta, float* c, int64_t ldc, void* workspace,

@@ -1,5 +1,6 @@
 // planner.cpp -- see planner.hpp.
 #include "planner.hpp"
+#include "tiling.hpp"
 
 #include <algorithm>
 #include <climits>
@@ -51,20 +52,20 @@ struct Geo {
   bool n_outer;
 };
 
-// Fraction of the SMs a launch of an mr x nr block keeps busy (last-wave quantisation).
-// CTA tiles of one kernel launch on an mr x nr block (128 x 256, or 128 x 128 when nr <=
-// 128) and the waves they take: one CTA per SM, and a last wave of at most half the SMs
-// runs as half-width tiles in about half a tile's time.
+// CTA tiles of one kernel launch on an mr x nr block, in the tiling the kernel picks for it
+// (tiling.hpp: 192 x 192, or 128 x 256 / 128 x 128 at 0.95 of that FMA rate), and the
+// waves they take: one CTA per SM, and a last wave of at most half the SMs runs as
+// half-width tiles in about half a tile's time.
 int64_t launch_ctas(int64_t mr, int64_t nr) {
-  return ceil_div(mr, kTileM) * ceil_div(nr, nr > 128 ? 256 : 128);
+  const Tiling t = choose_tiling(mr, nr, kSmCount);
+  return ceil_div(mr, t.tile_m) * ceil_div(nr, t.tile_n);
 }
-double launch_waves(int64_t mr, int64_t nr) {
-  const int64_t ctas = launch_ctas(mr, nr);
-  const int64_t full = ctas / kSmCount, tail = ctas % kSmCount;
-  return static_cast<double>(full) + (tail == 0 ? 0.0 : (2 * tail <= kSmCount ? 0.5 : 1.0));
-}
+double launch_waves(int64_t mr, int64_t nr) { return tile_waves(launch_ctas(mr, nr), kSmCount); }
+// Useful work per SM-wave slot of the launch, times the tiling's relative FMA rate.
 double wave_efficiency(int64_t mr, int64_t nr) {
-  return static_cast<double>(launch_ctas(mr, nr)) / (launch_waves(mr, nr) * kSmCount);
+  const Tiling t = choose_tiling(mr, nr, kSmCount);
+  return static_cast<double>(mr) * static_cast<double>(nr) /
+         (launch_waves(mr, nr) * kSmCount * t.tile_m * t.tile_n) * t.rate;
 }
 
 // Per-step time that does not scale with kr: launch bookkeeping plus one tile fixed cost

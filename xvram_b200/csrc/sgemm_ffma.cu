@@ -37,6 +37,7 @@
 // kernel below covers every other device-pointer call.
 #include "device_common.cuh"
 #include "kernels.hpp"
+#include "tiling.hpp"
 
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -290,7 +291,8 @@ struct UnitCoords {
   int m0, n0;
   bool half;
 };
-template <int BN> __device__ __forceinline__ UnitCoords unit_coords(const FfmaParams& p, int u) {
+template <int BN, int BM = kBM>
+__device__ __forceinline__ UnitCoords unit_coords(const FfmaParams& p, int u) {
   const bool half = u >= p.full_tiles;
   const int tile_lin = half ? p.full_tiles + ((u - p.full_tiles) >> 1) : u;
   const int half_index = half ? ((u - p.full_tiles) & 1) : 0;
@@ -299,7 +301,7 @@ template <int BN> __device__ __forceinline__ UnitCoords unit_coords(const FfmaPa
   const int group_m = min(8, p.tiles_m - first_m);
   const int tile_m = first_m + (tile_lin % group_span) % group_m;
   const int tile_n = (tile_lin % group_span) / group_m;
-  return {tile_m * kBM, tile_n * BN + half_index * (BN / 2), half};
+  return {tile_m * BM, tile_n * BN + half_index * (BN / 2), half};
 }
 
 // The epilogue reads this thread's C entries; ask L2 for their lines before the K loop,
@@ -481,6 +483,206 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   else
     tile_main<A_KMAJOR, B_KMAJOR, TN, TN>(&tmap_a, &tmap_b, smem_a, smem_b, full, empty, p, m0,
                                           n0, issued);
+}
+
+// ---------------------------------------------------------------------------------
+// The 192 x 192 tiling of the M-/N-major kernel: 12 warps (384 threads, three warps on
+// each SM sub-partition instead of two), each thread a 12 x 8 block of C (96 accumulators,
+// 168 registers: 65,536 / 384).  Per k a thread loads 12 A values (three 16-byte loads)
+// and 8 B values (two) and issues 48 packed FMAs; shared-memory traffic per FMA is 11 %
+// above the 8 x 16 form's, but the third warp per sub-partition keeps the FMA pipe fed
+// while the others wait (9216 x 9216 x 4096 NT, CUDA events: 10.867 against 11.391 ms).
+// Same ring (4 stages of 32 k, one 2D TMA load per operand, full/empty mbarriers, thread 0
+// producing), same bounded waits and abort path, same tail split into half-width (96
+// column) units, and each output is the same FFMA chain in k order, so the bits equal the
+// 128 x 256 form's and the generic kernel's.  Used where its waves cost less (t192_fits).
+constexpr int kT192Threads = 384;
+constexpr int kT192Warps = kT192Threads / 32;
+constexpr int kT192 = 192;
+constexpr int kT192StageFloats = kT192 * kBK; // per operand
+constexpr uint32_t kT192StageBytes = 2u * kT192StageFloats * sizeof(float);
+constexpr int kT192Smem = kStages * 2 * kT192StageFloats * sizeof(float) + 1024 + 256;
+
+// Tile-local row of a thread's i-th accumulator row (three runs of four, 64 apart) and
+// column of its j-th column (two runs of four, 96 apart).
+__device__ __forceinline__ int t192_row(int tm, int i) { return 64 * (i >> 2) + 4 * tm + (i & 3); }
+__device__ __forceinline__ int t192_col(int tn, int j) { return 96 * (j >> 2) + 4 * tn + (j & 3); }
+
+// One 32-k stage: A tile [32 k][192 m], B tile [32 k][192 n], both unswizzled; the next
+// k's fragments are loaded before the current k's packed FMAs.
+template <int NJ>
+__device__ __forceinline__ void t192_stage(const float* as, const float* bs, int tm, int tn,
+                                           float2 (&acc)[12][NJ / 2]) {
+  float4 a4[2][3], b4[2][NJ / 4];
+  auto load = [&](int kk, int slot) {
+    const float* ar = as + kk * kT192 + 4 * tm;
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+      a4[slot][r] = *reinterpret_cast<const float4*>(ar + 64 * r);
+    const float* br = bs + kk * kT192 + 4 * tn;
+#pragma unroll
+    for (int q = 0; q < NJ / 4; ++q)
+      b4[slot][q] = *reinterpret_cast<const float4*>(br + 96 * q);
+  };
+  load(0, 0);
+#pragma unroll
+  for (int kk = 0; kk < kBK; ++kk) {
+    const int cur = kk & 1;
+    if (kk + 1 < kBK)
+      load(kk + 1, cur ^ 1);
+    float a[12];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      a[4 * r + 0] = a4[cur][r].x;
+      a[4 * r + 1] = a4[cur][r].y;
+      a[4 * r + 2] = a4[cur][r].z;
+      a[4 * r + 3] = a4[cur][r].w;
+    }
+    float2 b[NJ / 2];
+#pragma unroll
+    for (int q = 0; q < NJ / 4; ++q) {
+      b[2 * q + 0] = make_float2(b4[cur][q].x, b4[cur][q].y);
+      b[2 * q + 1] = make_float2(b4[cur][q].z, b4[cur][q].w);
+    }
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const float2 ai = make_float2(a[i], a[i]);
+#pragma unroll
+      for (int j2 = 0; j2 < NJ / 2; ++j2)
+        acc[i][j2] = __ffma2_rn(ai, b[j2], acc[i][j2]);
+    }
+  }
+}
+
+__device__ __forceinline__ void t192_issue(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                           float* smem_a, float* smem_b, uint64_t* full, int kt,
+                                           int m0, int n0) {
+  const int s = kt % kStages;
+  mbar_arrive_expect_tx(&full[s], kT192StageBytes);
+  tma_load_2d(smem_a + s * kT192StageFloats, tmap_a, &full[s], m0, kt * kBK);
+  tma_load_2d(smem_b + s * kT192StageFloats, tmap_b, &full[s], n0, kt * kBK);
+}
+
+// K loop and epilogue of one 192 x 192 tile (NJ = 8) or of its half-width unit (NJ = 4:
+// the thread's first run of four columns, 96 of the tile's 192).
+template <int NJ>
+__device__ __forceinline__ void t192_tile(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                          float* smem_a, float* smem_b, uint64_t* full,
+                                          uint64_t* empty, const FfmaParams& p, int m0, int n0,
+                                          int issued) {
+  const int tid = threadIdx.x;
+  const int tm = tid & 15, tn = tid >> 4;
+  if (p.beta != 0.0f) { // C's lines into L2 before the K loop (one prefetch per run of four)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int col = n0 + t192_col(tn, j);
+      if (col < p.n) {
+        const float* cc = p.c + static_cast<long long>(col) * p.ldc;
+#pragma unroll
+        for (int i = 0; i < 12; i += 4) {
+          const int row = m0 + t192_row(tm, i);
+          if (row < p.m)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(cc + row));
+        }
+      }
+    }
+  }
+  float2 acc[12][NJ / 2];
+#pragma unroll
+  for (int i = 0; i < 12; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ / 2; ++j)
+      acc[i][j] = make_float2(0.0f, 0.0f);
+  bool aborted = false;
+  if (p.stall_ns && !mbar_wait_bounded(empty + kStages, 0, p.stall_ns)) {
+    atomicOr(&xvram_kernel_error, 1u);
+    aborted = true;
+  }
+  for (int kt = 0; kt < p.k_tiles && !aborted; ++kt) {
+    const int s = kt % kStages;
+    const uint32_t phase = (kt / kStages) & 1;
+    if (!mbar_wait_bounded(&full[s], phase, p.timeout_ns)) {
+      atomicOr(&xvram_kernel_error, 1u);
+      aborted = true;
+      break;
+    }
+    t192_stage<NJ>(smem_a + s * kT192StageFloats, smem_b + s * kT192StageFloats, tm, tn, acc);
+    __syncwarp();
+    if ((tid & 31) == 0)
+      mbar_arrive(&empty[s]);
+    // Refill this stage with tile kt + 4 once every warp has released tile kt.
+    if (tid == 0 && issued < p.k_tiles) {
+      if (!mbar_wait_bounded(&empty[s], phase, p.timeout_ns)) {
+        atomicOr(&xvram_kernel_error, 2u);
+        aborted = true;
+        break;
+      }
+      t192_issue(tmap_a, tmap_b, smem_a, smem_b, full, issued++, m0, n0);
+    }
+  }
+  if (aborted) {
+    if (tid == 0)
+      drain_loads(full, issued, p.timeout_ns);
+    return;
+  }
+  // C = alpha * acc + beta * C, a column at a time: its 12 C reads before its stores.
+  const float alpha = p.alpha, beta = p.beta;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int col = n0 + t192_col(tn, j);
+    if (col >= p.n)
+      continue;
+    float* cc = p.c + static_cast<long long>(col) * p.ldc;
+    float cv[12];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const int row = m0 + t192_row(tm, i);
+      cv[i] = (beta != 0.0f && row < p.m) ? cc[row] : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const int row = m0 + t192_row(tm, i);
+      if (row < p.m) {
+        const float v = alpha * acc_at(acc[i][j >> 1], j & 1);
+        cc[row] = (beta == 0.0f) ? v : fmaf(beta, cv[i], v);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kT192Threads, 1)
+    sgemm_ffma_tma_192(const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_b, const FfmaParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  float* smem = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* smem_a = smem;
+  float* smem_b = smem + kStages * kT192StageFloats;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * kT192StageFloats);
+  uint64_t* empty = full + kStages;
+  const UnitCoords uc = unit_coords<kT192, kT192>(p, blockIdx.x);
+  const int m0 = uc.m0, n0 = uc.n0;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kT192Warps);
+    }
+    mbar_init(&empty[kStages], 1); // the stall hook's barrier: nothing arrives on it
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  int issued = 0; // meaningful in thread 0 only
+  if (tid == 0) {
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+    for (; issued < kStages && issued < p.k_tiles; ++issued)
+      t192_issue(&tmap_a, &tmap_b, smem_a, smem_b, full, issued, m0, n0);
+  }
+  if (uc.half)
+    t192_tile<4>(&tmap_a, &tmap_b, smem_a, smem_b, full, empty, p, m0, n0, issued);
+  else
+    t192_tile<8>(&tmap_a, &tmap_b, smem_a, smem_b, full, empty, p, m0, n0, issued);
 }
 
 // ---------------------------------------------------------------------------------
@@ -731,6 +933,31 @@ cudaError_t launch_tma(const CUtensorMap& ta, const CUtensorMap& tb, FfmaParams 
   return cudaGetLastError();
 }
 
+// Whether an M-/N-major problem runs as 192 x 192 tiles on this device (tiling.hpp).
+bool t192_fits(int m, int n) { return choose_tiling(m, n, sm_count()).tile_m == kT192; }
+
+cudaError_t launch_t192(const CUtensorMap& ta, const CUtensorMap& tb, FfmaParams p,
+                        cudaStream_t stream) {
+  static const cudaError_t configured = cudaFuncSetAttribute(
+      sgemm_ffma_tma_192, cudaFuncAttributeMaxDynamicSharedMemorySize, kT192Smem);
+  if (configured != cudaSuccess)
+    return configured;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long sms = sm_count();
+  const long long tail = tiles % sms;
+  long long grid = tiles;
+  p.full_tiles = static_cast<int>(tiles);
+  if (tail > 0 && 2 * tail <= sms) {
+    p.full_tiles = static_cast<int>(tiles - tail);
+    grid = tiles + tail;
+  }
+  if (grid > 0x7fffffffll)
+    return cudaErrorInvalidConfiguration;
+  sgemm_ffma_tma_192<<<static_cast<unsigned>(grid), kT192Threads, kT192Smem, stream>>>(ta, tb,
+                                                                                      p);
+  return cudaGetLastError();
+}
+
 template <int TN>
 cudaError_t launch_tn(bool a_kmajor, bool b_kmajor, const CUtensorMap& ta, const CUtensorMap& tb,
                       const FfmaParams& p, cudaStream_t stream) {
@@ -744,6 +971,12 @@ cudaError_t launch_tn(bool a_kmajor, bool b_kmajor, const CUtensorMap& ta, const
 }
 
 } // namespace
+
+void sgemm_tile_shape(int m, int n, int* tile_m, int* tile_n) {
+  const Tiling t = choose_tiling(m, n, sm_count());
+  *tile_m = t.tile_m;
+  *tile_n = t.tile_n;
+}
 
 bool sgemm_tma_eligible(int op_a, int op_b, const float* a, long long lda, const float* b,
                         long long ldb) {
@@ -881,6 +1114,26 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
 
   const bool a_kmajor = op_a != 0;
   const bool b_kmajor = op_b == 0;
+  FfmaParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.k_tiles = (k + kBK - 1) / kBK;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.c = c;
+  p.ldc = ldc;
+  p.timeout_ns = kernel_wait_limit_ns();
+  p.stall_ns = g_test_stall_ns.load(std::memory_order_relaxed);
+  if (!a_kmajor && !b_kmajor && t192_fits(m, n)) {
+    CUtensorMap ta, tb;
+    if (!encode_2d(&ta, a, m, k, lda, kT192, kBK, false) ||
+        !encode_2d(&tb, b, n, k, ldb, kT192, kBK, false))
+      return cudaErrorInvalidValue;
+    p.tiles_m = (m + kT192 - 1) / kT192;
+    p.tiles_n = (n + kT192 - 1) / kT192;
+    return launch_t192(ta, tb, p, stream);
+  }
   // Wide tiles halve shared-memory traffic per FFMA; narrow N keeps 128-wide tiles so
   // fewer columns are wasted on padding.
   const int tn = n > 128 ? 16 : 8;
@@ -892,19 +1145,8 @@ cudaError_t sgemm_ffma(int op_a, int op_b, int m, int n, int k, float alpha, con
                        : encode_2d(&tb, b, n, k, ldb, bn, kBK, false));
   if (!ok)
     return cudaErrorInvalidValue;
-  FfmaParams p;
-  p.m = m;
-  p.n = n;
-  p.k = k;
-  p.k_tiles = (k + kBK - 1) / kBK;
   p.tiles_m = (m + kBM - 1) / kBM;
   p.tiles_n = (n + bn - 1) / bn;
-  p.alpha = alpha;
-  p.beta = beta;
-  p.c = c;
-  p.ldc = ldc;
-  p.timeout_ns = kernel_wait_limit_ns();
-  p.stall_ns = g_test_stall_ns.load(std::memory_order_relaxed);
   if (static_cast<long long>(p.tiles_m) * p.tiles_n > 0x7fffffffll)
     return cudaErrorInvalidConfiguration;
   return tn == 16 ? launch_tn<16>(a_kmajor, b_kmajor, ta, tb, p, stream)

@@ -37,6 +37,17 @@ def workspace_bytes(op_a: int, op_b: int, m: int, n: int, k: int) -> int:
     return lib.xvram_b200_sgemm_workspace_bytes(op_a, op_b, m, n, k)
 
 
+def tile_shape(m: int, n: int) -> tuple[int, int]:
+    """The C tile (rows, columns) the TMA kernel uses for an M-/N-major m x n problem on the
+    current device: (192, 192), (128, 256) or (128, 128)."""
+    import ctypes as C
+    tm, tn = C.c_int32(0), C.c_int32(0)
+    st = lib.xvram_b200_sgemm_tile_shape(m, n, C.byref(tm), C.byref(tn))
+    if st != 0:
+        raise ValueError(f"xvram_b200_sgemm_tile_shape failed with status {st}")
+    return tm.value, tn.value
+
+
 def sgemm_ws(op_a: int, op_b: int, m: int, n: int, k: int, alpha: float, a, lda: int, b,
              ldb: int, beta: float, c, ldc: int, workspace, workspace_bytes: int, stream=None,
              path: int = PATH_AUTO) -> int:
