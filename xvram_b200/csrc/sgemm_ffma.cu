@@ -7,15 +7,19 @@
 // (reference src/gemm/executor.cpp:147-329, src/platform/cublas/cublas_api.cpp:751-918).
 // Every product and sum is an FP32 FFMA; there is no TF32 or reduced-precision step.
 //
-// Main kernel (sgemm_ffma_tma): 128 x BN C tile per CTA (BN = 256 by default, 128 for
-// narrow N), K in stages of 32.
+// Two tilings of one TMA-fed design (which one runs: tiling.hpp):
+//   * sgemm_ffma_tma_192 (M-/N-major operands): 192 x 192 C tiles, 12 warps, 12 x 8 per
+//     thread -- see its own comment further down;
+//   * sgemm_ffma_tma (every layout): described here.
+// sgemm_ffma_tma: 128 x BN C tile per CTA (BN = 256 by default, 128 for narrow N), K in
+// stages of 32.
 //   * 8 warps (256 threads) each own an 8 x (BN/16) block of C per thread in registers;
 //     a warp releases a stage on its "empty" mbarrier when it has consumed it;
 //   * thread 0 also drives the 4-deep ring of 2D TMA loads: it fills every stage up
 //     front and refills a stage with the tile 4 ahead once all eight warps have
 //     released it; completion is signalled on the stage's "full" mbarrier.
-//   There is no separate producer warp: a 9-warp block would put three warps on one
-//   SM sub-partition and cap every thread at 168 registers, too few for 8x16.
+//   There is no separate producer warp: a 9-warp block would cap every thread at 224
+//   registers, too few for 8x16 (240-254).
 // Why 8x16 per thread: an LDS.128 costs four shared-memory wavefronts whatever the
 // broadcast, so shared-memory bandwidth per FFMA falls only with the register tile.  An
 // 8x8 tile needs one wavefront per SM-clock at full FFMA rate (all of it); 8x16 needs
