@@ -435,8 +435,9 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
     if world == 1:
         xd.fill_uniform(b_h, 41)
     else:
-        # the library's block width (xvram_b200_sgemm_sharded's default is 512 columns)
-        nb = min(Nt, -(-env_int("XVRAM_B200_SHARD_BLOCK_N", 512) // 32) * 32)
+        # the library's block width (xvram_b200_sgemm_sharded's default is 576 columns;
+        # checked against the call's plan after the first step)
+        nb = min(Nt, -(-env_int("XVRAM_B200_SHARD_BLOCK_N", 576) // 32) * 32)
         wc = -(-nb // world)
         cols = {int(c) for _, c in samples}
         for n0 in range(0, Nt, nb):
@@ -453,6 +454,8 @@ def ooc_sharded_leg(Mt: int, Nt: int, Kt: int, steps: int, warmup: int, world: i
 
     for _ in range(warmup):
         step()
+    if world > 1 and warmup:
+        assert group.last_plan()["block_n"] == nb, (group.last_plan()["block_n"], nb)
     times = []
     with ClockSampler(local, 200) as clocks:
         for _ in range(steps):

@@ -347,7 +347,7 @@ XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_shard_allgather_rows(
  * may pass different m_local (0 included); the call agrees on one plan first.  Blocking;
  * every wait is bounded (TIMEOUT after 60 s without progress, after which the group is
  * unusable and returns POISONED).  Tuning (environment, read per call; the same on every
- * rank): XVRAM_B200_SHARD_BLOCK_N = C block width (default 512),
+ * rank): XVRAM_B200_SHARD_BLOCK_N = C block width (default 576),
  * XVRAM_B200_SHARD_BUDGET_BYTES = cap on the device memory the call may use.
  */
 XVRAM_B200_API xvram_status XVRAM_CALL xvram_b200_sgemm_sharded(
